@@ -1,0 +1,294 @@
+#!/usr/bin/env python
+"""Decode-step benchmark: ragged paged MLA decode (config 2) on N B200s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl hk|reference]
+
+A step is one pass of the hot path over the configuration-2 batch: pack the 64 ragged lanes
+into one token stream, append each lane's new latent row into the paged cache, then ragged
+paged MLA attention (128 heads, 512 latent + 64 rope, bf16, page 64, contexts log-uniform in
+[1K, 128K]) with split-KV partials merged by LSE.  Lanes are independent, so N GPUs run N
+independent 64-lane batches (weak scaling, no data-path collective); `value` is the tokens
+of all ranks over the slowest rank's device time.
+
+The KV cache (~2 GB per rank) is far larger than the 126 MB L2, so steps read it from HBM
+without an explicit flush.  Inputs are synthetic (seeded), see hyperkernel_b200/workload.py.
+
+--impl reference times the CPU restatement of the same step (oracle/, the reference has no
+runnable implementation of this path on this box) on all host cores, on a bounded sample of
+lanes per step scaled to the whole batch.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+HEADS = 128
+PAGE = 64
+DK, DV = 576, 512
+
+
+def _dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def attn_bytes(kv_len: np.ndarray, tokens: int, heads: int = HEADS) -> int:
+    """Algorithmic HBM bytes of one attention launch: every cached latent row read once
+    (576 bf16, shared by all heads), queries read, outputs and LSE written."""
+    return int(kv_len.sum()) * DK * 2 + tokens * heads * (DK * 2 + DV * 2 + 4)
+
+
+def attn_flops(kv_len: np.ndarray, heads: int = HEADS) -> int:
+    return int(2 * heads * (DK + DV) * int(kv_len.sum()))
+
+
+def cpu_sample_layout(lay, target_rows: int):
+    """The first lanes of the workload whose rows sum to about target_rows (at least one)."""
+    from hyperkernel_b200 import workload as W
+
+    ctx, rows = [], 0
+    for c in lay.context:
+        if ctx and rows + c + 1 > target_rows:
+            break
+        ctx.append(int(c))
+        rows += int(c) + 1
+    sub = W.paged_layout(W.Rng(99), np.array(ctx), np.ones(len(ctx), np.int64), PAGE)
+    return sub, rows
+
+
+def cpu_step_seconds(lay, target_rows: int, reps: int = 1):
+    """Times the CPU oracle (pack + append + attention) on a sample; returns
+    (seconds per full step extrapolated by KV rows, sample rows, sample lanes, threads)."""
+    import oracle
+
+    sub, rows = cpu_sample_layout(lay, target_rows)
+    g = np.random.default_rng(7)
+    T = sub.num_tokens
+    q = g.integers(0, 1 << 16, size=(T, HEADS, DK), dtype=np.uint16) & np.uint16(0xBFFF)
+    cache = (g.integers(0, 1 << 16, size=(sub.num_slots, DK), dtype=np.uint16) & np.uint16(0xBFFF))
+    kv_new = g.integers(0, 1 << 16, size=(T, DK), dtype=np.uint16) & np.uint16(0xBFFF)
+    best = math.inf
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        p = oracle.pack(sub.new_rows, sub.context, sub.block_table, PAGE, sub.num_pages, T)
+        oracle.kv_append_bf16(kv_new, p["slot_mapping"][:T], cache)
+        oracle.mla_decode(q, sub.block_table, p["cu_seqlens"], p["positions"][:T], PAGE,
+                          1.0 / math.sqrt(DK), kv_bf16=cache)
+        best = min(best, time.perf_counter() - t0)
+    full_rows = int(lay.kv_len.sum())
+    return best * full_rows / rows, rows, sub.lanes, oracle.threads()
+
+
+def run_reference(args):
+    """CPU restatement of the step on all host cores, one bounded sample per step."""
+    world, rank, _ = _dist()
+    if rank != 0:
+        return 0
+    from hyperkernel_b200 import workload as W
+
+    lay = W.config2_layout(seed=0)
+    tokens = lay.num_tokens
+    target = 60_000
+    for _ in range(args.warmup):
+        cpu_step_seconds(lay, target)
+    secs = []
+    for _ in range(args.steps):
+        s, rows, lanes, threads = cpu_step_seconds(lay, target)
+        secs.append(s)
+    step_s = float(np.mean(secs))
+    value = tokens / step_s
+    line = {
+        "impl": "reference", "metric": "ragged decode step tokens/s (MLA config 2)",
+        "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16 in, fp64 accumulation",
+        "data": "synthetic (seeded)",
+        "config": {"workload": "config2: 64 lanes, ctx log-uniform [1K,128K], 128 heads, "
+                               "MLA 512+64, page 64", "lanes": lay.lanes,
+                   "kv_rows": int(lay.kv_len.sum())},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": f"pack+append+attention of the first {lanes} lanes "
+                                   f"({rows} KV rows, 128 heads) per step, scaled by "
+                                   f"{int(lay.kv_len.sum())} / {rows} KV rows"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="hk", choices=["hk", "reference"])
+    ap.add_argument("--attn-impl", type=int, default=0, help="0 best, 1 portable, 2 tcgen05")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+
+    from hyperkernel_b200 import _lib as hk
+    from hyperkernel_b200 import workload as W
+    from hyperkernel_b200.clocks import ClockSampler
+    from hyperkernel_b200.step import MlaDecodeStep
+
+    world, rank, local = _dist()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
+
+    lay = W.config2_layout(seed=rank)
+    T = lay.num_tokens
+    max_kv = int(lay.kv_len.max())
+    gen = torch.Generator(device=device)
+    gen.manual_seed(1000 + rank)
+    cache = torch.randn((lay.num_slots, DK), generator=gen, device=device, dtype=torch.float32).to(torch.bfloat16)
+    q = torch.randn((T, HEADS, DK), generator=gen, device=device, dtype=torch.float32).to(torch.bfloat16)
+    kv_new = torch.randn((T, DK), generator=gen, device=device, dtype=torch.float32).to(torch.bfloat16)
+    lane_tokens = torch.from_numpy(lay.new_rows.astype(np.int32)).to(device)
+    lane_pos = torch.from_numpy(lay.context.astype(np.int32)).to(device)
+    step = MlaDecodeStep(lay.block_table, lay.num_pages, PAGE, HEADS, 1.0 / math.sqrt(DK), T,
+                         max_kv, device, cache=cache, impl=args.attn_impl)
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # warm-up (untimed)
+    for _ in range(args.warmup):
+        step.run(lane_tokens, lane_pos, q, kv_new, T)
+    torch.cuda.synchronize()
+    hk.check_errors()
+
+    sampler = ClockSampler(local).start()
+    n_ev = args.steps
+    ev_a = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
+    ev_b = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = hk.kernel_launches()
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    start.record(stream)
+    for i in range(args.steps):
+        p = step.packed
+        s = hk.stream_ptr(stream)
+        hk.call("hk_pack", hk.ptr(lane_tokens), hk.ptr(lane_pos), hk.ptr(step.block_table),
+                step.block_table.shape[1], step.lanes, PAGE, step.num_pages, T,
+                hk.ptr(p["cu_seqlens"]), hk.ptr(p["seq_lens"]), hk.ptr(p["positions"]),
+                hk.ptr(p["slot_mapping"]), hk.ptr(p["token_lane"]), hk.ptr(p["active"]), s)
+        hk.call("hk_kv_append_bf16", hk.ptr(kv_new), hk.ptr(p["slot_mapping"]), T, DK,
+                hk.ptr(step.cache), step.cache.shape[0], s)
+        ev_a[i].record(stream)
+        step.attention_only(q, T, stream)
+        ev_b[i].record(stream)
+    end.record(stream)
+    torch.cuda.synchronize()
+    t1 = time.perf_counter()
+    barrier()
+    launches = hk.kernel_launches() - launches0
+    sampler.stop()
+    hk.check_errors()
+    ms = start.elapsed_time(end)
+    attn_ms = float(np.mean([a.elapsed_time(b) for a, b in zip(ev_a, ev_b)]))
+    if world > 1:
+        t = torch.tensor([ms, attn_ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, attn_ms = float(t[0]), float(t[1])
+    clocks = sampler.summary(t0, t1)
+
+    # end to end through the host-facing step with pinned host buffers
+    q_h = q.cpu().pin_memory()
+    kv_h = kv_new.cpu().pin_memory()
+    lt_h = lane_tokens.cpu().pin_memory()
+    lp_h = lane_pos.cpu().pin_memory()
+    out_h = torch.empty((T, HEADS, DV), dtype=torch.bfloat16).pin_memory()
+    for _ in range(args.warmup):
+        step.step_host(lt_h, lp_h, q_h, kv_h, out_h, T, stream)
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step.step_host(lt_h, lp_h, q_h, kv_h, out_h, T, stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t[0])
+    hk.check_errors()
+
+    total_tokens = T * world
+    value = total_tokens * args.steps / (ms / 1e3)
+    e2e_value = total_tokens * args.steps / (e2e_ms / 1e3)
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        peak, peak_src = float(peaks["hbm_gbs"]), "measured"
+    except Exception:
+        peak, peak_src = 6650.0, "fallback"
+    abytes = attn_bytes(lay.kv_len, T)
+    achieved = abytes / (attn_ms / 1e3) / 1e9
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        s, rows, lanes, threads = cpu_step_seconds(lay, 200_000)
+        cpu = {"value": T / s, "unit": "tokens/s", "cores": threads, "kind": "port",
+               "sample": f"pack+append+attention of the first {lanes} lanes ({rows} KV rows, "
+                         f"128 heads), scaled by {int(lay.kv_len.sum())} / {rows} KV rows"}
+
+    if rank == 0:
+        line = {
+            "metric": "ragged decode step tokens/s (MLA config 2)", "value": value,
+            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
+            "config": {"workload": "config2: 64 lanes, ctx log-uniform [1K,128K], 128 heads, "
+                                   "MLA 512+64, page 64, pack+append+attention",
+                       "lanes_per_gpu": lay.lanes, "kv_rows_per_gpu": int(lay.kv_len.sum()),
+                       "l2": "inputs larger than L2 (~2 GB KV per GPU), no flush",
+                       "attn_impl": args.attn_impl},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None,
+                         "kernel": "attention (hk_mla_decode)", "kernel_ms": attn_ms,
+                         "algorithmic_bytes": abytes, "peak_source": peak_src,
+                         "tflops": attn_flops(lay.kv_len) / (attn_ms / 1e3) / 1e12},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "tokens/s",
+                    "h2d_bytes_per_step": MlaDecodeStep.h2d_bytes(lay.lanes, T, HEADS),
+                    "d2h_bytes_per_step": MlaDecodeStep.d2h_bytes(T, HEADS)},
+            "gpu_launches": int(launches),
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,220 @@
+/*
+ * hk.h — C ABI of the B200-native continuous-batching decode step.
+ *
+ * Plain pointers and sizes only: no CUDA, PyTorch or C++ types cross this boundary.
+ * Device pointers are raw CUDA device addresses; `stream` is a cudaStream_t passed as
+ * void* (NULL = the legacy default stream).  bf16 values travel as uint16_t bit patterns,
+ * e4m3 values as uint8_t.
+ *
+ * Every function returns 0 on success or a negative HK_E* code; hk_last_error() then
+ * gives a one-line message (thread-local).  Kernels that find bad input (an index past a
+ * buffer, a page id past the pool) skip the access, set a device error word and the next
+ * hk_check_errors() on that device reports it.  No entry point ever falls back to a CPU
+ * path: without a usable sm_100 device they return HK_ENODEV.
+ *
+ * Reference interfaces replaced (paths inside mr-d-self-driving/Hyperkernel):
+ *   - the `Kernel` trait, src/gpu/mod.rs:42-46 (pools / push / drain) and its data types
+ *     Share / Command / Event / Sampled, src/gpu/mod.rs:13-40  ->  hk_open ... hk_drain;
+ *   - the device half of src/gpu/feed.rs:40-208 and the closed sm_103a megakernel
+ *     (kernels/b300/c*, ring message `drafting`) -> the per-kernel entry points below.
+ */
+#ifndef HK_H
+#define HK_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define HK_OK 0
+#define HK_EINVAL -1   /* a bad argument: null pointer, size out of range, misaligned */
+#define HK_ENODEV -2   /* no usable sm_100 device */
+#define HK_ECUDA -3    /* a CUDA runtime / driver error */
+#define HK_EDEVICE -4  /* a kernel set its device error word (bad index, bounded wait ran out) */
+#define HK_ESPACE -5   /* a caller buffer or workspace too small */
+#define HK_ESTATE -6   /* a call out of order (e.g. push past the granted horizon) */
+
+/* ------------------------------------------------------------------------------------ */
+/* Library                                                                               */
+/* ------------------------------------------------------------------------------------ */
+
+const char* hk_version(void);
+/* Message of the last failed call on this thread ("" if none). */
+const char* hk_last_error(void);
+/* SM count and compute capability of the current device. */
+int hk_device_info(int* sm_count, int* cc_major, int* cc_minor);
+/* Number of CUDA kernels this library has launched in this process (all devices). */
+uint64_t hk_kernel_launches(void);
+/* Reads and clears the device error word of the current device: 0 when clean, else
+ * HK_EDEVICE with the first recorded code/site in hk_last_error().  Synchronises. */
+int hk_check_errors(void);
+
+/* ------------------------------------------------------------------------------------ */
+/* a7  pack: ragged lanes -> one token stream                                            */
+/* Replaces the packing the closed megakernel does from the `drafting` ring message      */
+/* (per-lane tokens[w*6], pos[w], pages[w*4097], slot[w]); block-table rows are those    */
+/* Cache::pages emits, src/engine/cache.rs:195-226.                                      */
+/* ------------------------------------------------------------------------------------ */
+
+/* Inputs (device): lane_tokens[num_lanes] new rows this step (0 = idle lane, 1 = decode,
+ * 1+d = spec verify, n = prompt chunk); lane_pos[num_lanes] position of the lane's first
+ * new row; block_table[num_lanes][bt_stride] page ids (i32, 0 = scratch page).
+ * Outputs (device): cu_seqlens[num_lanes+1] exclusive scan of lane_tokens;
+ * seq_lens[num_lanes] = lane_pos + lane_tokens (KV rows after the append, 0 if idle);
+ * positions[T], slot_mapping[T] = block_table[lane][pos / page_size] * page_size +
+ * pos % page_size, token_lane[T]; active[0] = number of non-idle lanes, active[1..] their
+ * lane ids in ascending order.  T = sum(lane_tokens) must be <= max_tokens, else the
+ * rows past max_tokens are not written and the device error word is set.  A row whose
+ * page is 0 (the scratch page) or past num_pages is written with slot -1 and flags the
+ * error word.  Bit-exact: integer only. */
+int hk_pack(const int32_t* lane_tokens, const int32_t* lane_pos, const int32_t* block_table,
+            int32_t bt_stride, int32_t num_lanes, int32_t page_size, int32_t num_pages,
+            int32_t max_tokens, int32_t* cu_seqlens, int32_t* seq_lens, int32_t* positions,
+            int32_t* slot_mapping, int32_t* token_lane, int32_t* active, void* stream);
+
+/* ------------------------------------------------------------------------------------ */
+/* a8  KV append into the paged cache                                                    */
+/* ------------------------------------------------------------------------------------ */
+
+/* MLA latent rows: kv_new[T][row_elems] bf16 -> kv_cache[slot][row_elems] bf16
+ * (row_elems = 576 = 512 latent + 64 rope for the configs; a multiple of 8). */
+int hk_kv_append_bf16(const uint16_t* kv_new, const int32_t* slot_mapping, int32_t num_tokens,
+                      int32_t row_elems, uint16_t* kv_cache, int64_t num_slots, void* stream);
+
+/* MLA latent rows quantised to e4m3 with one fp32 scale per row:
+ * scale = max(amax(row), 1e-12) / 448, q = e4m3_rn_satfinite(x / scale). */
+int hk_kv_append_fp8(const uint16_t* kv_new, const int32_t* slot_mapping, int32_t num_tokens,
+                     int32_t row_elems, uint8_t* kv_cache, float* kv_scale, int64_t num_slots,
+                     void* stream);
+
+/* GQA rows (config 1): k_new/v_new[T][kv_heads*head_dim] fp32 -> k_cache/v_cache[slot][..]. */
+int hk_kv_append_f32(const float* k_new, const float* v_new, const int32_t* slot_mapping,
+                     int32_t num_tokens, int32_t row_elems, float* k_cache, float* v_cache,
+                     int64_t num_slots, void* stream);
+
+/* ------------------------------------------------------------------------------------ */
+/* a9/a10  ragged paged decode attention with split-KV partials and LSE merge           */
+/* Query row t of lane b sits at positions[t] and attends KV rows 0..positions[t]       */
+/* (causal inside a spec-verify block or a prompt chunk).                                */
+/* ------------------------------------------------------------------------------------ */
+
+/* GQA fp32 (config 1): q[T][q_heads][head_dim], caches [num_slots][kv_heads][head_dim].
+ * out[T][q_heads][head_dim], lse[T][q_heads] (natural log, of scale*q.k). */
+int hk_gqa_decode_f32(const float* q, const float* k_cache, const float* v_cache,
+                      const int32_t* block_table, int32_t bt_stride, const int32_t* cu_seqlens,
+                      const int32_t* positions, int32_t num_lanes, int32_t num_tokens,
+                      int32_t q_heads, int32_t kv_heads, int32_t head_dim, int32_t page_size,
+                      int64_t num_slots, float scale, float* out, float* lse, void* stream);
+
+/* MLA absorbed decode, bf16 (config 2): q[T][heads][576], kv_cache[slot][576] (latent 512
+ * then rope 64), out[T][heads][512] bf16, lse[T][heads] fp32.  Scores use all 576 dims,
+ * values the first 512.  The work is split across SMs by KV range; partials of split
+ * lanes go to `workspace` (size from hk_mla_workspace_size) and are merged by LSE.
+ * impl: 0 = best available (tcgen05 when heads == 128), 1 = portable CUDA-core kernel,
+ * 2 = tcgen05 2-SM kernel (heads must be 128). */
+size_t hk_mla_workspace_size(int32_t num_lanes, int32_t num_tokens, int32_t heads,
+                             int32_t max_kv_len);
+int hk_mla_decode(const uint16_t* q, const uint16_t* kv_cache, const int32_t* block_table,
+                  int32_t bt_stride, const int32_t* cu_seqlens, const int32_t* positions,
+                  int32_t num_lanes, int32_t num_tokens, int32_t heads, int32_t page_size,
+                  int64_t num_slots, int32_t max_kv_len, float scale, uint16_t* out, float* lse,
+                  void* workspace, size_t workspace_bytes, int32_t impl, void* stream);
+
+/* MLA decode over an e4m3 latent cache with per-row fp32 scales (config 5). */
+int hk_mla_decode_fp8(const uint16_t* q, const uint8_t* kv_cache, const float* kv_scale,
+                      const int32_t* block_table, int32_t bt_stride, const int32_t* cu_seqlens,
+                      const int32_t* positions, int32_t num_lanes, int32_t num_tokens,
+                      int32_t heads, int32_t page_size, int64_t num_slots, int32_t max_kv_len,
+                      float scale, uint16_t* out, float* lse, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
+/* Partial attention of a KV shard, for context parallelism: the same contract as
+ * hk_mla_decode_fp8 restricted to KV rows [kv_begin[b], kv_end[b]) of each lane, writing
+ * fp32 o_part[T][heads][512] (normalised within the shard) and lse_part[T][heads] (-inf
+ * where the shard holds no row).  max_kv_len bounds kv_end - kv_begin; the workspace size
+ * is hk_mla_workspace_size(num_lanes, num_tokens, heads, max_kv_len). */
+int hk_mla_partial_fp8(const uint16_t* q, const uint8_t* kv_cache, const float* kv_scale,
+                       const int32_t* block_table, int32_t bt_stride, const int32_t* cu_seqlens,
+                       const int32_t* positions, const int32_t* kv_begin, const int32_t* kv_end,
+                       int32_t num_lanes, int32_t num_tokens, int32_t heads, int32_t page_size,
+                       int64_t num_slots, int32_t max_kv_len, float scale, float* o_part,
+                       float* lse_part, void* workspace, size_t workspace_bytes, void* stream);
+
+/* a10  LSE merge of n_parts partials: o_parts[n][rows][dv] fp32, lse_parts[n][rows]
+ * -> out[rows][dv] bf16 and lse_out[rows]:  m = max lse_i,
+ * out = sum_i e^(lse_i - m) o_i / sum_i e^(lse_i - m),  lse = m + log(sum e^(lse_i - m)). */
+int hk_lse_merge(const float* o_parts, const float* lse_parts, int32_t n_parts, int64_t rows,
+                 int32_t dv, uint16_t* out, float* lse_out, void* stream);
+
+/* ------------------------------------------------------------------------------------ */
+/* a11  FP8 block-scaled linear                                                          */
+/* ------------------------------------------------------------------------------------ */
+
+/* Quantise bf16 activations x[rows][k] to e4m3 in 1x128 blocks:
+ * sx[rows][k/128] = max(amax, 1e-12)/448, xq = e4m3_rn_satfinite(x / sx).  k % 128 == 0. */
+int hk_quant_fp8(const uint16_t* x, int64_t rows, int32_t k, uint8_t* xq, float* sx,
+                 void* stream);
+
+/* y[m][n] bf16 = sum over 128-blocks kb of (xq[m][kb] . wq[n][kb]) * sx[m][kb] * sw[n/128][kb]
+ * with wq[n][k] e4m3 and sw[ceil(n/128)][k/128] fp32; fp32 accumulation.
+ * k % 128 == 0, n % 16 == 0. */
+int hk_gemm_fp8(const uint8_t* xq, const float* sx, const uint8_t* wq, const float* sw,
+                int64_t m, int32_t n, int32_t k, uint16_t* y, void* stream);
+
+/* ------------------------------------------------------------------------------------ */
+/* a12-a15  MoE: router, permutation, grouped FP8 GEMM, combine                          */
+/* ------------------------------------------------------------------------------------ */
+
+/* Sigmoid router: s = sigmoid(logits[t][e]); the top_k experts by s + bias[e] (ties: the
+ * lower expert id first); weights = s[chosen] / sum s[chosen] * route_scale.
+ * ids[t][top_k] i32 in descending order of s + bias, weights[t][top_k] fp32.
+ * num_experts <= 256, top_k <= 16. */
+int hk_route(const float* logits, const float* bias, int32_t tokens, int32_t num_experts,
+             int32_t top_k, float route_scale, int32_t* ids, float* weights, void* stream);
+
+/* Stable permutation of the (token, k) pairs into per-expert groups, ordered by
+ * (expert, token, k): offsets[num_experts+1] exclusive scan of the per-expert counts;
+ * perm_token[P] source token of permuted row p; perm_weight[P]; inv[t*top_k+k] = the
+ * permuted row of pair (t, k).  P = tokens*top_k.  Bit-exact. */
+int hk_permute(const int32_t* ids, const float* weights, int32_t tokens, int32_t top_k,
+               int32_t num_experts, int32_t* offsets, int32_t* perm_token, float* perm_weight,
+               int32_t* inv, void* stream);
+
+/* Grouped expert FFN.  Rows of expert e are permuted rows offsets[e]..offsets[e+1] (at most
+ * `rows` in all, offsets[num_experts] <= rows); their inputs are xq[perm_token[p]] (e4m3,
+ * 1x128 scales sx, `tokens` rows).  Per expert:
+ * h = silu(x Wg^T) * (x Wu^T) (Wg, Wu = halves of w13[e][2*inter][hidden]),
+ * y[p] = h Wd^T (w2[e][hidden][inter]), all weights e4m3 with 128x128 fp32 block scales
+ * (s13[e][2*inter/128][hidden/128], s2[e][hidden/128][inter/128]); h is re-quantised to
+ * e4m3 1x128 blocks before the down projection.  y[P][hidden] bf16.
+ * `workspace` holds h: see hk_moe_workspace_size. */
+size_t hk_moe_workspace_size(int64_t rows, int32_t inter);
+int hk_moe_grouped(const uint8_t* xq, const float* sx, int32_t tokens, const int32_t* offsets,
+                   const int32_t* perm_token, int64_t rows, int32_t num_experts, int32_t hidden,
+                   int32_t inter, const uint8_t* w13, const float* s13, const uint8_t* w2,
+                   const float* s2, uint16_t* y, void* workspace, size_t workspace_bytes,
+                   void* stream);
+
+/* out[t][hidden] bf16 = sum_k perm_weight[inv[t,k]] * y[inv[t,k]] (+ shared[t] when not
+ * NULL), fp32 accumulation in k order; y has `rows` rows. */
+int hk_combine(const uint16_t* y, int64_t rows, const float* perm_weight, const int32_t* inv,
+               const uint16_t* shared, int32_t tokens, int32_t top_k, int32_t hidden,
+               uint16_t* out, void* stream);
+
+/* ------------------------------------------------------------------------------------ */
+/* RoPE table (pinned against the reference's fixtures; src/gpu/load.rs:824-846)         */
+/* ------------------------------------------------------------------------------------ */
+
+/* Host function: fills table[rows][dim] fp32 with, per row p, dim/2 cosines then dim/2
+ * sines of p * freq_i, freq_i = base^(-2i/dim) with YaRN-style correction when
+ * original_seq_len > 0.  No device needed. */
+int hk_rope_table(int64_t rows, int32_t dim, float base, int32_t original_seq_len,
+                  float factor, float beta_fast, float beta_slow, float* table);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HK_H */

@@ -1,0 +1,352 @@
+"""GPU parity of every kernel behind include/hk.h against the CPU oracle.
+
+Integer work (pack, slot mapping, appends, route ids, permutation) must be bit-exact;
+floating point is compared as max|gpu - oracle| / max|oracle| (normwise max-abs-rel):
+  - GQA fp32 attention (config 1): absolute 1e-5;
+  - bf16 / e4m3 attention, FP8 GEMM, MoE: max-abs-rel <= 2e-2 against the fp64-accumulated
+    oracle on the same bf16 / e4m3 inputs.
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from hyperkernel_b200 import workload as W
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-2
+
+
+def rel_err(got, want):
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    return float(np.abs(got - want).max() / max(np.abs(want).max(), 1e-30))
+
+
+def dev(a, cuda):
+    t = torch.from_numpy(np.ascontiguousarray(a))
+    return t.to(cuda)
+
+
+def bf16_dev(bits, cuda):
+    return torch.from_numpy(np.ascontiguousarray(bits).view(np.int16)).to(cuda).view(torch.bfloat16)
+
+
+def to_np_bf16(t):
+    return W.bf16_bits_to_f32(t.view(torch.int16).cpu().numpy().view(np.uint16))
+
+
+# ------------------------------------------------------------------------------------------
+# a7 pack / a8 append
+# ------------------------------------------------------------------------------------------
+
+def _mixed_layout(seed=0):
+    rng = W.Rng(seed)
+    lanes = 40
+    ctx = rng.integers(0, 3000, lanes)
+    rows = np.ones(lanes, np.int64)
+    rows[::7] = 0            # idle lanes
+    rows[1::9] = 5           # spec verify blocks
+    rows[3] = 300            # a prompt chunk crossing pages
+    return W.paged_layout(rng, ctx, rows, 64, spare_pages=5)
+
+
+def test_pack_matches_oracle_bit_exact(hk, orc, cuda):
+    lay = _mixed_layout()
+    T = lay.num_tokens
+    want = orc.pack(lay.new_rows, lay.context, lay.block_table, 64, lay.num_pages, T + 3)
+    got = hk.pack(dev(lay.new_rows.astype(np.int32), cuda), dev(lay.context.astype(np.int32), cuda),
+                  dev(lay.block_table, cuda), 64, lay.num_pages, T + 3)
+    hk.check_errors()
+    for k in ("cu_seqlens", "seq_lens", "active"):
+        assert np.array_equal(got[k].cpu().numpy(), want[k]), k
+    for k in ("positions", "slot_mapping", "token_lane"):
+        assert np.array_equal(got[k].cpu().numpy()[:T], want[k][:T]), k
+
+
+def test_pack_flags_scratch_page(hk, cuda):
+    bt = dev(np.array([[5, 0]], np.int32), cuda)
+    hk.pack(dev(np.array([2], np.int32), cuda), dev(np.array([63], np.int32), cuda), bt, 64, 8, 4)
+    with pytest.raises(hk.HKError, match="pack page"):
+        hk.check_errors()
+    hk.check_errors()  # cleared
+
+
+def test_append_bf16_fp8_f32_bit_exact(hk, orc, cuda):
+    lay = _mixed_layout(1)
+    T = lay.num_tokens
+    p = orc.pack(lay.new_rows, lay.context, lay.block_table, 64, lay.num_pages, T)
+    slot = p["slot_mapping"][:T].copy()
+    inp = W.mla_inputs(lay, 16, seed=2)
+    # bf16
+    cache = np.zeros((lay.num_slots, 576), np.uint16)
+    orc.kv_append_bf16(inp["kv_new"], slot, cache)
+    c_dev = torch.zeros((lay.num_slots, 576), dtype=torch.int16, device=cuda)
+    hk.kv_append_bf16(dev(inp["kv_new"].view(np.int16), cuda), dev(slot, cuda), c_dev)
+    hk.check_errors()
+    assert np.array_equal(c_dev.cpu().numpy().view(np.uint16), cache)
+    # e4m3 + scale
+    c8 = np.zeros((lay.num_slots, 576), np.uint8)
+    s8 = np.zeros(lay.num_slots, np.float32)
+    orc.kv_append_fp8(inp["kv_new"], slot, c8, s8)
+    c8_dev = torch.zeros((lay.num_slots, 576), dtype=torch.uint8, device=cuda)
+    s8_dev = torch.zeros(lay.num_slots, dtype=torch.float32, device=cuda)
+    hk.kv_append_fp8(dev(inp["kv_new"].view(np.int16), cuda), dev(slot, cuda), c8_dev, s8_dev)
+    hk.check_errors()
+    assert np.array_equal(c8_dev.cpu().numpy(), c8)
+    assert np.array_equal(s8_dev.cpu().numpy(), s8)
+    # fp32 K/V rows
+    k = W.Rng(3).normal(T * 256).astype(np.float32).reshape(T, 256)
+    v = W.Rng(4).normal(T * 256).astype(np.float32).reshape(T, 256)
+    kc = np.zeros((lay.num_slots, 256), np.float32)
+    vc = np.zeros((lay.num_slots, 256), np.float32)
+    orc.kv_append_f32(k, v, slot, kc, vc)
+    kc_d = torch.zeros((lay.num_slots, 256), device=cuda)
+    vc_d = torch.zeros((lay.num_slots, 256), device=cuda)
+    hk.kv_append_f32(dev(k, cuda), dev(v, cuda), dev(slot, cuda), kc_d, vc_d)
+    hk.check_errors()
+    assert np.array_equal(kc_d.cpu().numpy(), kc) and np.array_equal(vc_d.cpu().numpy(), vc)
+
+
+def test_append_rejects_bad_slot(hk, cuda):
+    c = torch.zeros((64, 576), dtype=torch.int16, device=cuda)
+    hk.kv_append_bf16(torch.ones((2, 576), dtype=torch.int16, device=cuda),
+                      dev(np.array([3, 64], np.int32), cuda), c)
+    with pytest.raises(hk.HKError, match="append slot"):
+        hk.check_errors()
+    assert int(c[3, 0]) == 1 and int(c.sum()) == 576
+
+
+# ------------------------------------------------------------------------------------------
+# a9 / a10 attention
+# ------------------------------------------------------------------------------------------
+
+def test_config1_gqa_step_matches_oracle(hk, orc, cuda):
+    c = W.config1(seed=0)
+    lay = c["layout"]
+    T = lay.num_tokens
+    p = orc.pack(lay.new_rows, lay.context, lay.block_table, 64, lay.num_pages, T)
+    kc, vc = c["k_cache"].copy(), c["v_cache"].copy()
+    orc.kv_append_f32(c["k_new"], c["v_new"], p["slot_mapping"][:T], kc, vc)
+    want, want_lse = orc.gqa_decode(c["q"], kc, vc, lay.block_table, p["cu_seqlens"],
+                                    p["positions"][:T], 8, 2, 128, 64, c["scale"])
+    g = hk.pack(dev(lay.new_rows.astype(np.int32), cuda), dev(lay.context.astype(np.int32), cuda),
+                dev(lay.block_table, cuda), 64, lay.num_pages, T)
+    kc_d, vc_d = dev(c["k_cache"], cuda), dev(c["v_cache"], cuda)
+    hk.kv_append_f32(dev(c["k_new"], cuda), dev(c["v_new"], cuda), g["slot_mapping"], kc_d, vc_d)
+    out, lse = hk.gqa_decode(dev(c["q"], cuda), kc_d, vc_d, dev(lay.block_table, cuda),
+                             g["cu_seqlens"], g["positions"], 2, 64, c["scale"])
+    hk.check_errors()
+    assert np.array_equal(g["slot_mapping"].cpu().numpy(), p["slot_mapping"][:T])
+    assert np.abs(out.cpu().numpy() - want).max() <= 1e-5
+    assert np.abs(lse.cpu().numpy() - want_lse).max() <= 1e-5
+
+
+def _mla_case(seed, lanes, lo, hi, heads, rows=1, fp8=False, long_ctx=None):
+    if long_ctx is not None:
+        lay = W.config5_layout(seed=seed, long_ctx=long_ctx, short_lanes=lanes - 1, lo=lo, hi=hi,
+                               rows=rows)
+    else:
+        lay = W.config2_layout(seed=seed, lanes=lanes, lo=lo, hi=hi, new_rows=rows)
+    inp = W.mla_inputs(lay, heads, seed=seed + 100)
+    return lay, inp
+
+
+def _run_mla(hk, orc, cuda, lay, inp, impl=0, fp8=False):
+    T = lay.num_tokens
+    p = orc.pack(lay.new_rows, lay.context, lay.block_table, 64, lay.num_pages, T)
+    assert p["err"] == 0
+    slot = p["slot_mapping"][:T]
+    g = hk.pack(dev(lay.new_rows.astype(np.int32), cuda), dev(lay.context.astype(np.int32), cuda),
+                dev(lay.block_table, cuda), 64, lay.num_pages, T)
+    q = bf16_dev(inp["q"], cuda)
+    max_kv = int(lay.kv_len.max())
+    if not fp8:
+        cache = inp["kv_cache"].copy()
+        orc.kv_append_bf16(inp["kv_new"], slot, cache)
+        want, want_lse = orc.mla_decode(inp["q"], lay.block_table, p["cu_seqlens"],
+                                        p["positions"][:T], 64, inp["scale"], kv_bf16=cache)
+        c = bf16_dev(inp["kv_cache"], cuda)
+        hk.kv_append_bf16(bf16_dev(inp["kv_new"], cuda), g["slot_mapping"], c)
+        out, lse = hk.mla_decode(q, c, dev(lay.block_table, cuda), g["cu_seqlens"], g["positions"],
+                                 64, max_kv, inp["scale"], impl=impl)
+    else:
+        c8 = np.zeros((lay.num_slots, 576), np.uint8)
+        s8 = np.zeros(lay.num_slots, np.float32)
+        # cached rows quantised through the same append path, then the step's new rows
+        all_slots = np.arange(lay.num_slots, dtype=np.int32)
+        orc.kv_append_fp8(inp["kv_cache"], all_slots, c8, s8)
+        orc.kv_append_fp8(inp["kv_new"], slot, c8, s8)
+        want, want_lse = orc.mla_decode(inp["q"], lay.block_table, p["cu_seqlens"],
+                                        p["positions"][:T], 64, inp["scale"], kv_fp8=c8, kv_scale=s8)
+        c8d = torch.zeros((lay.num_slots, 576), dtype=torch.uint8, device=cuda)
+        s8d = torch.zeros(lay.num_slots, dtype=torch.float32, device=cuda)
+        hk.kv_append_fp8(bf16_dev(inp["kv_cache"], cuda), dev(all_slots, cuda), c8d, s8d)
+        hk.kv_append_fp8(bf16_dev(inp["kv_new"], cuda), g["slot_mapping"], c8d, s8d)
+        assert np.array_equal(c8d.cpu().numpy(), c8)
+        out, lse = hk.mla_decode_fp8(q, c8d, s8d, dev(lay.block_table, cuda), g["cu_seqlens"],
+                                     g["positions"], 64, max_kv, inp["scale"])
+    hk.check_errors()
+    return to_np_bf16(out), lse.cpu().numpy(), want, want_lse
+
+
+def test_mla_portable_matches_oracle_with_splits(hk, orc, cuda):
+    lay, inp = _mla_case(seed=21, lanes=6, lo=64, hi=9000, heads=32)
+    out, lse, want, want_lse = _run_mla(hk, orc, cuda, lay, inp, impl=1)
+    assert rel_err(out, want) <= TOL
+    assert np.abs(lse - want_lse).max() <= 1e-3
+
+
+def test_mla_decode_128_heads_matches_oracle(hk, orc, cuda):
+    lay, inp = _mla_case(seed=22, lanes=8, lo=1024, hi=6000, heads=128)
+    out, lse, want, want_lse = _run_mla(hk, orc, cuda, lay, inp, impl=0)
+    assert rel_err(out, want) <= TOL
+    assert np.abs(lse - want_lse).max() <= 1e-3
+
+
+def test_mla_fp8_spec_verify_matches_oracle(hk, orc, cuda):
+    lay, inp = _mla_case(seed=23, lanes=4, lo=300, hi=2000, heads=16, rows=5, long_ctx=9000)
+    out, lse, want, want_lse = _run_mla(hk, orc, cuda, lay, inp, fp8=True)
+    assert rel_err(out, want) <= TOL
+    assert np.abs(lse - want_lse).max() <= 1e-3
+
+
+def test_context_parallel_partials_merge_to_whole(hk, orc, cuda):
+    """Shard the KV of every lane into 3 ranges, attend each, merge by LSE on the device."""
+    lay, inp = _mla_case(seed=24, lanes=3, lo=500, hi=3000, heads=16, rows=5, long_ctx=7000)
+    T = lay.num_tokens
+    p = orc.pack(lay.new_rows, lay.context, lay.block_table, 64, lay.num_pages, T)
+    c8 = np.zeros((lay.num_slots, 576), np.uint8)
+    s8 = np.zeros(lay.num_slots, np.float32)
+    orc.kv_append_fp8(inp["kv_cache"], np.arange(lay.num_slots, dtype=np.int32), c8, s8)
+    want, want_lse = orc.mla_decode(inp["q"], lay.block_table, p["cu_seqlens"], p["positions"][:T],
+                                    64, inp["scale"], kv_fp8=c8, kv_scale=s8)
+    kv = lay.kv_len
+    cuts = [np.zeros_like(kv), kv // 3, (2 * kv) // 3, kv]
+    q = bf16_dev(inp["q"], cuda)
+    args = (dev(c8, cuda), dev(s8, cuda), dev(lay.block_table, cuda), dev(p["cu_seqlens"], cuda),
+            dev(p["positions"][:T].copy(), cuda))
+    parts, lses = [], []
+    for i in range(3):
+        o, l = hk.mla_partial_fp8(q, *args, dev(cuts[i].astype(np.int32), cuda),
+                                  dev(cuts[i + 1].astype(np.int32), cuda), 64, int(kv.max()),
+                                  inp["scale"])
+        parts.append(o.reshape(T * 16, 512))
+        lses.append(l.reshape(T * 16))
+    out, lse = hk.lse_merge(torch.stack(parts).contiguous(), torch.stack(lses).contiguous())
+    hk.check_errors()
+    assert rel_err(to_np_bf16(out), want.reshape(-1, 512)) <= TOL
+    assert np.abs(lse.cpu().numpy() - want_lse.ravel()).max() <= 1e-3
+
+
+def test_lse_merge_matches_oracle(hk, orc, cuda):
+    rng = W.Rng(30)
+    n, rows, dv = 5, 300, 512
+    o = rng.normal(n * rows * dv).astype(np.float32).reshape(n, rows, dv)
+    l = (rng.normal(n * rows) * 3).astype(np.float32).reshape(n, rows)
+    l[1, :7] = -np.inf
+    want, want_lse = orc.lse_merge(o, l)
+    out, lse = hk.lse_merge(dev(o, cuda), dev(l, cuda))
+    assert rel_err(to_np_bf16(out), want) <= 1e-2
+    assert np.abs(lse.cpu().numpy() - want_lse).max() <= 1e-5
+
+
+# ------------------------------------------------------------------------------------------
+# a11 FP8 linear
+# ------------------------------------------------------------------------------------------
+
+def test_quant_fp8_bit_exact(hk, orc, cuda):
+    x = W.f32_to_bf16_bits(W.Rng(40).normal(100 * 1024).astype(np.float32) * 3).reshape(100, 1024)
+    xq, sx = orc.quant_fp8(x)
+    gq, gs = hk.quant_fp8(bf16_dev(x, cuda))
+    assert np.array_equal(gq.cpu().numpy(), xq)
+    assert np.array_equal(gs.cpu().numpy(), sx)
+
+
+@pytest.mark.parametrize("m,n,k", [(300, 512, 1024), (640, 1536, 1792), (7, 128, 256)])
+def test_gemm_fp8_matches_oracle(hk, orc, cuda, m, n, k):
+    rng = W.Rng(41)
+    x = W.f32_to_bf16_bits(rng.normal(m * k).astype(np.float32)).reshape(m, k)
+    wf = (rng.normal(n * k) * 0.02).astype(np.float32).reshape(n, k)
+    nb = (n + 127) // 128
+    sw = np.zeros((nb, k // 128), np.float32)
+    wq = np.zeros((n, k), np.uint8)
+    for i in range(nb):
+        for j in range(k // 128):
+            blk = wf[i * 128:(i + 1) * 128, j * 128:(j + 1) * 128]
+            s = max(float(np.abs(blk).max()), 1e-12) / 448.0
+            sw[i, j] = s
+            wq[i * 128:(i + 1) * 128, j * 128:(j + 1) * 128] = W.e4m3_encode(blk / s)
+    xq, sx = orc.quant_fp8(x)
+    want = orc.gemm_fp8(xq, sx, wq, sw)
+    y = hk.gemm_fp8(dev(xq, cuda), dev(sx, cuda), dev(wq, cuda), dev(sw, cuda))
+    assert rel_err(to_np_bf16(y), want) <= TOL
+
+
+# ------------------------------------------------------------------------------------------
+# a12-a15 MoE
+# ------------------------------------------------------------------------------------------
+
+def test_route_bit_exact(hk, orc, cuda):
+    rng = W.Rng(50)
+    T, E, K = 512, 256, 8
+    logits = rng.normal(T * E).astype(np.float32).reshape(T, E)
+    bias = (rng.normal(E) * 0.05).astype(np.float32)
+    ids, w = orc.route(logits, bias, K, 2.5)
+    gi, gw = hk.route(dev(logits, cuda), dev(bias, cuda), K, 2.5)
+    assert np.array_equal(gi.cpu().numpy(), ids)
+    assert np.array_equal(gw.cpu().numpy(), w)
+    ids0, _ = orc.route(logits, None, K, 1.0)
+    gi0, _ = hk.route(dev(logits, cuda), None, K, 1.0)
+    assert np.array_equal(gi0.cpu().numpy(), ids0)
+
+
+def test_permute_bit_exact(hk, orc, cuda):
+    rng = W.Rng(51)
+    T, K, E = 1500, 8, 257  # more pairs than one round of the CTA
+    ids = rng.integers(0, E - 1, T * K).reshape(T, K).astype(np.int32)
+    w = rng.uniform(T * K).astype(np.float32).reshape(T, K)
+    want = orc.permute(ids, w, E)
+    got = hk.permute(dev(ids, cuda), dev(w, cuda), E)
+    for a, b in zip(got, want):
+        assert np.array_equal(a.cpu().numpy()[:len(b)], b)
+
+
+def _moe_case(tokens, experts, hidden, inter, top_k, seed):
+    inp = W.moe_inputs(tokens, experts, hidden, inter, top_k=top_k, seed=seed)
+    return inp
+
+
+def test_moe_layer_matches_oracle(hk, orc, cuda):
+    T, E, H, I, K = 96, 8, 256, 256, 2
+    inp = _moe_case(T, E, H, I, K, seed=52)
+    ids, w = orc.route(inp["logits"], None, K, 1.0)
+    off, tok, pw, inv = orc.permute(ids, w, E)
+    xq, sx = orc.quant_fp8(inp["x"])
+    y = orc.moe_grouped(xq, sx, off, tok, H, I, inp["w13"], inp["s13"], inp["w2"], inp["s2"])
+    y_bits = W.f32_to_bf16_bits(y)
+    want = orc.combine(y_bits, pw, inv, None, T, K)
+    # device path
+    gi, gw = hk.route(dev(inp["logits"], cuda), None, K, 1.0)
+    goff, gtok, gpw, ginv = hk.permute(gi, gw, E)
+    gxq, gsx = hk.quant_fp8(bf16_dev(inp["x"], cuda))
+    gy = hk.moe_grouped(gxq, gsx, goff, gtok, T * K, H, I, dev(inp["w13"], cuda),
+                        dev(inp["s13"], cuda), dev(inp["w2"], cuda), dev(inp["s2"], cuda))
+    out = hk.combine(gy, gpw, ginv, None, T, K)
+    hk.check_errors()
+    assert rel_err(to_np_bf16(gy)[:T * K], y) <= TOL
+    assert rel_err(to_np_bf16(out), want) <= TOL
+
+
+def test_combine_matches_oracle(hk, orc, cuda):
+    rng = W.Rng(53)
+    T, K, Hd = 33, 8, 7168 // 4
+    y = W.f32_to_bf16_bits(rng.normal(T * K * Hd).astype(np.float32)).reshape(T * K, Hd)
+    shared = W.f32_to_bf16_bits(rng.normal(T * Hd).astype(np.float32)).reshape(T, Hd)
+    inv = rng.permutation(T * K).astype(np.int32)
+    pw = rng.uniform(T * K).astype(np.float32)
+    want = orc.combine(y, pw, inv, shared, T, K)
+    out = hk.combine(bf16_dev(y, cuda), dev(pw, cuda), dev(inv, cuda), bf16_dev(shared, cuda), T, K)
+    assert rel_err(to_np_bf16(out), want) <= 1e-2
