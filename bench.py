@@ -128,6 +128,35 @@ def run_reference(args):
     return 0
 
 
+def run_e2e(args, step, q, kv_new, lane_tokens, lane_pos, T, stream, barrier, world, device):
+    """Same step through MlaDecodeStep.step_host: pinned host inputs copied in and the output
+    copied out inside the timed region, every step."""
+    import torch
+    import torch.distributed as dist
+
+    q_h = q.cpu().pin_memory()
+    kv_h = kv_new.cpu().pin_memory()
+    lt_h = lane_tokens.cpu().pin_memory()
+    lp_h = lane_pos.cpu().pin_memory()
+    out_h = torch.empty((T, HEADS, DV), dtype=torch.bfloat16).pin_memory()
+    for _ in range(args.warmup):
+        step.step_host(lt_h, lp_h, q_h, kv_h, out_h, T, stream)
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step.step_host(lt_h, lp_h, q_h, kv_h, out_h, T, stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t[0])
+    return e2e_ms
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -136,6 +165,10 @@ def main(argv=None):
     ap.add_argument("--impl", default="hk", choices=["hk", "reference"])
     ap.add_argument("--attn-impl", type=int, default=0, help="0 best, 1 portable, 2 tcgen05")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--lanes", type=int, default=64, help="profiling override of config 2")
+    ap.add_argument("--ctx-min", type=int, default=1024, help="profiling override of config 2")
+    ap.add_argument("--ctx-max", type=int, default=131072, help="profiling override of config 2")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host round trip leg")
     args = ap.parse_args(argv)
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -157,7 +190,7 @@ def main(argv=None):
 
         dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
 
-    lay = W.config2_layout(seed=rank)
+    lay = W.config2_layout(seed=rank, lanes=args.lanes, lo=args.ctx_min, hi=args.ctx_max)
     T = lay.num_tokens
     max_kv = int(lay.kv_len.max())
     gen = torch.Generator(device=device)
@@ -219,31 +252,14 @@ def main(argv=None):
     clocks = sampler.summary(t0, t1)
 
     # end to end through the host-facing step with pinned host buffers
-    q_h = q.cpu().pin_memory()
-    kv_h = kv_new.cpu().pin_memory()
-    lt_h = lane_tokens.cpu().pin_memory()
-    lp_h = lane_pos.cpu().pin_memory()
-    out_h = torch.empty((T, HEADS, DV), dtype=torch.bfloat16).pin_memory()
-    for _ in range(args.warmup):
-        step.step_host(lt_h, lp_h, q_h, kv_h, out_h, T, stream)
-    torch.cuda.synchronize()
-    barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        step.step_host(lt_h, lp_h, q_h, kv_h, out_h, T, stream)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t[0])
+    e2e_ms = float("nan")
+    if not args.no_e2e:
+        e2e_ms = run_e2e(args, step, q, kv_new, lane_tokens, lane_pos, T, stream, barrier, world,
+                         device)
     hk.check_errors()
-
     total_tokens = T * world
     value = total_tokens * args.steps / (ms / 1e3)
-    e2e_value = total_tokens * args.steps / (e2e_ms / 1e3)
+    e2e_value = None if args.no_e2e else total_tokens * args.steps / (e2e_ms / 1e3)
     peaks = {}
     try:
         peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
@@ -277,9 +293,10 @@ def main(argv=None):
                          "algorithmic_bytes": abytes, "peak_source": peak_src,
                          "tflops": attn_flops(lay.kv_len) / (attn_ms / 1e3) / 1e12},
             "cpu_baseline": cpu,
-            "e2e": {"value": e2e_value, "unit": "tokens/s",
-                    "h2d_bytes_per_step": MlaDecodeStep.h2d_bytes(lay.lanes, T, HEADS),
-                    "d2h_bytes_per_step": MlaDecodeStep.d2h_bytes(T, HEADS)},
+            "e2e": None if e2e_value is None else {
+                "value": e2e_value, "unit": "tokens/s",
+                "h2d_bytes_per_step": MlaDecodeStep.h2d_bytes(lay.lanes, T, HEADS),
+                "d2h_bytes_per_step": MlaDecodeStep.d2h_bytes(T, HEADS)},
             "gpu_launches": int(launches),
             "clocks": clocks,
         }

@@ -112,8 +112,10 @@ int hk_gqa_decode_f32(const float* q, const float* k_cache, const float* v_cache
  * then rope 64), out[T][heads][512] bf16, lse[T][heads] fp32.  Scores use all 576 dims,
  * values the first 512.  The work is split across SMs by KV range; partials of split
  * lanes go to `workspace` (size from hk_mla_workspace_size) and are merged by LSE.
- * impl: 0 = best available (tcgen05 when heads == 128), 1 = portable CUDA-core kernel,
- * 2 = tcgen05 2-SM kernel (heads must be 128). */
+ * impl: 0 = best available (tcgen05 when heads == 128 and pages hold 64 rows), 1 = portable
+ * CUDA-core kernel, 2 = tcgen05 2-SM kernel.  The tcgen05 kernel reads whole pages: rows past
+ * a lane's length in its last page, and the scratch page 0, must hold finite values (a
+ * zero-filled pool satisfies this); they get zero weight but pass through the tensor core. */
 size_t hk_mla_workspace_size(int32_t num_lanes, int32_t num_tokens, int32_t heads,
                              int32_t max_kv_len);
 int hk_mla_decode(const uint16_t* q, const uint16_t* kv_cache, const int32_t* block_table,

@@ -199,11 +199,52 @@ def test_mla_portable_matches_oracle_with_splits(hk, orc, cuda):
     assert np.abs(lse - want_lse).max() <= 1e-3
 
 
-def test_mla_decode_128_heads_matches_oracle(hk, orc, cuda):
+@pytest.mark.parametrize("impl", [1, 2])
+def test_mla_decode_128_heads_matches_oracle(hk, orc, cuda, impl):
+    """impl 1 = portable CUDA-core kernel, impl 2 = tcgen05 2-SM kernel; rows split across
+    several SM pairs are merged by LSE."""
     lay, inp = _mla_case(seed=22, lanes=8, lo=1024, hi=6000, heads=128)
-    out, lse, want, want_lse = _run_mla(hk, orc, cuda, lay, inp, impl=0)
+    out, lse, want, want_lse = _run_mla(hk, orc, cuda, lay, inp, impl=impl)
     assert rel_err(out, want) <= TOL
     assert np.abs(lse - want_lse).max() <= 1e-3
+
+
+@pytest.mark.parametrize("seed,lanes,lo,hi", [(31, 1, 1, 2), (32, 3, 30, 200), (33, 20, 64, 5000)])
+def test_mla_tcgen05_ragged_edges(hk, orc, cuda, seed, lanes, lo, hi):
+    """Single-row and sub-page contexts, partial last pages, many short lanes."""
+    lay, inp = _mla_case(seed=seed, lanes=lanes, lo=lo, hi=hi, heads=128)
+    out, lse, want, want_lse = _run_mla(hk, orc, cuda, lay, inp, impl=2)
+    assert rel_err(out, want) <= TOL
+    assert np.abs(lse - want_lse).max() <= 1e-3
+
+
+def test_mla_tcgen05_spec_verify_rows(hk, orc, cuda):
+    """1 + 4 rows per lane, causal inside the block: every row is its own query."""
+    lay, inp = _mla_case(seed=34, lanes=3, lo=100, hi=3000, heads=128, rows=5)
+    out, lse, want, want_lse = _run_mla(hk, orc, cuda, lay, inp, impl=2)
+    assert rel_err(out, want) <= TOL
+    assert np.abs(lse - want_lse).max() <= 1e-3
+
+
+def test_mla_tcgen05_matches_portable_at_config2_scale(hk, cuda):
+    """Full configuration-2 batch (64 lanes, ~1.95 M cached rows): the tcgen05 kernel and the
+    portable kernel agree (the CPU oracle is too slow at this size)."""
+    lay = W.config2_layout(seed=0)
+    T = lay.num_tokens
+    g = torch.Generator(device=cuda)
+    g.manual_seed(5)
+    cache = torch.randn((lay.num_slots, 576), generator=g, device=cuda).to(torch.bfloat16)
+    q = torch.randn((T, 128, 576), generator=g, device=cuda).to(torch.bfloat16)
+    pk = hk.pack(dev(lay.new_rows.astype(np.int32), cuda), dev(lay.context.astype(np.int32), cuda),
+                 dev(lay.block_table, cuda), 64, lay.num_pages, T)
+    bt = dev(lay.block_table, cuda)
+    args = (q, cache, bt, pk["cu_seqlens"], pk["positions"], 64, int(lay.kv_len.max()), 1 / 24.0)
+    o1, l1 = hk.mla_decode(*args, impl=1)
+    o2, l2 = hk.mla_decode(*args, impl=2)
+    hk.check_errors()
+    a, b = o1.float().cpu().numpy(), o2.float().cpu().numpy()
+    assert rel_err(b, a) <= TOL
+    assert np.abs(l1.cpu().numpy() - l2.cpu().numpy()).max() <= 1e-3
 
 
 def test_mla_fp8_spec_verify_matches_oracle(hk, orc, cuda):
