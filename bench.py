@@ -231,7 +231,7 @@ def main(argv=None):
                 step.block_table.shape[1], step.lanes, PAGE, step.num_pages, T,
                 hk.ptr(p["cu_seqlens"]), hk.ptr(p["seq_lens"]), hk.ptr(p["positions"]),
                 hk.ptr(p["slot_mapping"]), hk.ptr(p["token_lane"]), hk.ptr(p["active"]), s)
-        hk.call("hk_kv_append_bf16", hk.ptr(kv_new), hk.ptr(p["slot_mapping"]), T, DK,
+        hk.call("hk_kv_append_bf16", hk.ptr(kv_new), hk.ptr(p["slot_mapping"]), T, DK, PAGE,
                 hk.ptr(step.cache), step.cache.shape[0], s)
         ev_a[i].record(stream)
         step.attention_only(q, T, stream)

@@ -12,8 +12,11 @@ from pathlib import Path
 
 import torch
 
+import os
+
 PKG = Path(__file__).resolve().parent
-LIB_PATH = PKG / "libhk.so"
+# HK_LIB_PATH selects another build of the same library (A/B timing of kernel variants).
+LIB_PATH = Path(os.environ.get("HK_LIB_PATH", PKG / "libhk.so"))
 HEADER = PKG.parent / "include" / "hk.h"
 
 HK_OK, HK_EINVAL, HK_ENODEV, HK_ECUDA, HK_EDEVICE, HK_ESPACE, HK_ESTATE = 0, -1, -2, -3, -4, -5, -6
@@ -28,7 +31,7 @@ SIGNATURES = {
     "hk_kernel_launches": (C.c_uint64, []),
     "hk_check_errors": (C.c_int, []),
     "hk_pack": (C.c_int, [P, P, P, I32, I32, I32, I32, I32, P, P, P, P, P, P, P]),
-    "hk_kv_append_bf16": (C.c_int, [P, P, I32, I32, P, I64, P]),
+    "hk_kv_append_bf16": (C.c_int, [P, P, I32, I32, I32, P, I64, P]),
     "hk_kv_append_fp8": (C.c_int, [P, P, I32, I32, P, P, I64, P]),
     "hk_kv_append_f32": (C.c_int, [P, P, P, I32, I32, P, P, I64, P]),
     "hk_gqa_decode_f32": (C.c_int, [P, P, P, P, I32, P, P, I32, I32, I32, I32, I32, I32, I64, F32, P, P, P]),
@@ -153,10 +156,11 @@ def pack(lane_tokens, lane_pos, block_table, page_size, num_pages, max_tokens, s
     return o
 
 
-def kv_append_bf16(kv_new, slot_mapping, kv_cache, num_tokens=None, stream=None):
+def kv_append_bf16(kv_new, slot_mapping, kv_cache, num_tokens=None, page_rows=64, stream=None):
+    """Appends rows into the page-blocked latent cache (page_rows=0: a row-major cache)."""
     n = kv_new.shape[0] if num_tokens is None else num_tokens
-    call("hk_kv_append_bf16", ptr(kv_new), ptr(slot_mapping), n, kv_new.shape[-1], ptr(kv_cache),
-         kv_cache.shape[0], stream_ptr(stream))
+    call("hk_kv_append_bf16", ptr(kv_new), ptr(slot_mapping), n, kv_new.shape[-1], page_rows,
+         ptr(kv_cache), kv_cache.shape[0], stream_ptr(stream))
 
 
 def kv_append_fp8(kv_new, slot_mapping, kv_cache, kv_scale, num_tokens=None, stream=None):

@@ -5,8 +5,8 @@
 //    the group; lanes split head_dim, online softmax in fp32.
 //  * MLA (configs 2 and 5, any head count that is a multiple of 16): one CTA per
 //    (query row, KV split, block of 16 heads).  A tile of 32 latent rows is staged in
-//    shared memory as fp32 (bf16 or e4m3*scale source), scores use all 576 dims, values
-//    the first 512.  Partials of every split go to fp32 scratch and hk_lse_merge-style
+//    shared memory as fp32 (a page-blocked bf16 cache, or a row-major e4m3 cache times its
+//    per-row scale), scores use all 576 dims, values the first 512.  Partials of every split go to fp32 scratch and hk_lse_merge-style
 //    merging produces the output.  The tcgen05 kernel (attn_mla_sm100.cu) replaces this
 //    one for 128-head decode; this one stays for other head counts, the fp8 cache and
 //    the context-parallel shard partials.
@@ -172,8 +172,10 @@ __global__ void __launch_bounds__(kMlaThreads) mla_portable_kernel(MlaArgs a) {
         float* dst = k_s + j * kRowPad + v * 8;
         const int page = page_s[j];
         if (j < n && page >= 0) {
-          const int64_t slot = (int64_t)page * a.page_size + (base + j) % a.page_size;
-          const uint4 u = reinterpret_cast<const uint4*>(a.kv_bf16 + slot * kMlaDim)[v];
+          // page-blocked layout: block v / 8 of the page, row (pos % page_size), column v % 8
+          const int64_t r = (base + j) % a.page_size;
+          const uint4 u = reinterpret_cast<const uint4*>(
+              a.kv_bf16 + (int64_t)page * a.page_size * kMlaDim)[(v >> 3) * a.page_size * 8 + r * 8 + (v & 7)];
           const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
           for (int e = 0; e < 4; ++e) {

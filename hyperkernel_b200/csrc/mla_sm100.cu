@@ -12,10 +12,12 @@
 //                                  running max grows by more than 8 in log2 units)
 //   O += P V     : 2 N-blocks x 4 pages x 4 MMAs M=128 N=256 K=16 (A = P, K-major; B = V,
 //                  MN-major; CTA r supplies dims 256j + 128r .. +127 of every token)
-// K chunks ([128 rows][64 dims]) and V chunks ([64 tokens][128 dims]) stream through one
+// The cache is page-blocked (each page stores its rows' dims in nine 64-dim blocks), so each
+// TMA box is one contiguous 8 KB block.  K chunks ([128 rows][64 dims]) and V chunks
+// ([64 tokens][128 dims]) stream through one
 // ring of five 16 KB entries in the exact order the MMA warp consumes them, so a chunk is
-// refilled as soon as its four MMAs retire.  Shared memory per SM: Q 72 KB + P 2 x 32 KB +
-// ring 80 KB = 216 KB.  HBM bytes are the KV rows once; the V half each SM needs from its
+// refilled as soon as its four MMAs retire.  Shared memory per SM: Q 72 KB + P 32 KB + ring
+// 7 x 16 KB = 216 KB.  HBM bytes are the KV rows once; the V half each SM needs from its
 // partner's rows is read a second time through L2.
 //
 // Work split: the 256-token tiles of all query rows are laid end to end and cut into one
@@ -45,13 +47,13 @@ constexpr int kThreads = 192;
 
 constexpr int kBox = 64 * 128;           // one TMA box: [64 rows][64 dims] bf16, 128B-swizzled
 constexpr int kEntry = 2 * kBox;         // ring entry: two boxes
-constexpr int kRing = 5;
+constexpr int kRing = 7;
 constexpr int kPAtom = kBox;             // [64 heads][64 tokens]
 constexpr int kPBuf = 4 * kPAtom;        // 256 tokens
 
 constexpr int kOffQ = 0;                 // 9 boxes
 constexpr int kOffP = kOffQ + 9 * kBox;
-constexpr int kOffRing = kOffP + 2 * kPBuf;
+constexpr int kOffRing = kOffP + kPBuf;       // one P buffer: softmax(g) writes it after PV(g-1)
 constexpr int kOffCtl = kOffRing + kRing * kEntry;
 constexpr int kCtlBytes = 2048;
 constexpr int kSmemBytes = kOffCtl + kCtlBytes;
@@ -59,17 +61,17 @@ static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 // Control block layout (byte offsets inside the control block).
 constexpr int kBarFull = 0;      // [kRing] leader: both SMs' TMA bytes of a ring entry
-constexpr int kBarEmpty = 40;    // [kRing] each SM: entry consumed (MMA commit, multicast)
-constexpr int kBarQFull = 80;    // leader: both SMs' Q bytes
-constexpr int kBarQEmpty = 88;   // each SM: Q no longer read (MMA commit)
-constexpr int kBarSFull = 96;    // [2] each SM: S ready (MMA commit)
-constexpr int kBarSFree = 112;   // [2] leader: S read by all 8 softmax warps
-constexpr int kBarPFull = 128;   // [2] leader: P written by all 8 softmax warps
-constexpr int kBarODone = 144;   // each SM: PV of a tile complete (MMA commit)
-constexpr int kBarOFree = 152;   // leader: epilogue of a segment done reading O
-constexpr int kTmemSlot = 160;
-constexpr int kAbort = 164;
-constexpr int kXchMax = 256;     // [2][128] floats
+constexpr int kBarEmpty = 64;    // [kRing] each SM: entry consumed (MMA commit, multicast)
+constexpr int kBarQFull = 128;   // leader: both SMs' Q bytes
+constexpr int kBarQEmpty = 136;  // each SM: Q no longer read (MMA commit)
+constexpr int kBarSFull = 144;   // [2] each SM: S ready (MMA commit)
+constexpr int kBarSFree = 160;   // [2] leader: S read by all 8 softmax warps
+constexpr int kBarPFull = 176;   // [2] leader: P written by all 8 softmax warps
+constexpr int kBarODone = 192;   // each SM: PV of a tile complete (MMA commit)
+constexpr int kBarOFree = 200;   // leader: epilogue of a segment done reading O
+constexpr int kTmemSlot = 208;
+constexpr int kAbort = 212;
+constexpr int kXchMax = 256;     // [2][128] floats (kXchL ends at 1792 < kCtlBytes)
 constexpr int kXchL = kXchMax + 1024;  // [128] floats
 
 constexpr int kTmemO = 0;        // 256 columns
@@ -467,8 +469,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t dst, fbar;
             if (!next_entry(dst, fbar)) return false;
             for (int aa = 0; aa < 2; ++aa)
-              tma_load_2d_pair(dst + aa * kBox, &kv_map, fbar, 256 * j + 128 * (int)rank + 64 * aa,
-                               pages[p] * kPage);
+              tma_load_2d_pair(dst + aa * kBox, &kv_map, fbar, 0,
+                               (pages[p] * 9 + 4 * j + 2 * (int)rank + aa) * kPage);
           }
         return true;
       };
@@ -490,8 +492,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t dst, fbar;
             if (!next_entry(dst, fbar)) { ok = false; break; }
             for (int hh = 0; hh < 2; ++hh)
-              tma_load_2d_pair(dst + hh * kBox, &kv_map, fbar, 64 * d,
-                               cur[2 * (int)rank + hh] * kPage);
+              tma_load_2d_pair(dst + hh * kBox, &kv_map, fbar, 0,
+                               (cur[2 * (int)rank + hh] * 9 + d) * kPage);
           }
           if (ok && i > a) ok = load_v(prev);
           for (int p = 0; p < 4; ++p) prev[p] = cur[p];
@@ -519,14 +521,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma_commit_pair(bar(kBarEmpty + 8 * (e % kRing)));
         ++e;
       };
-      // PV of tile gg: 2 N-blocks x 4 pages, each a ring entry of 4 MMAs.
       auto issue_pv = [&](int gg, bool first, int seg_of) -> bool {
         const int s = gg & 1;
         if (!mbar_wait(bar(kBarPFull + 8 * s), (gg >> 1) & 1, abort, prm.err, 3)) return false;
         if (first && seg_of > 0 && !mbar_wait(bar(kBarOFree), (seg_of - 1) & 1, abort, prm.err, 4))
           return false;
         tc_fence_after();
-        const uint32_t pb = p_s + s * kPBuf;
+        const uint32_t pb = p_s;
         for (int j = 0; j < 2; ++j) {
           for (int p = 0; p < 4; ++p) {
             uint32_t src;
@@ -629,11 +630,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float m_use = (first || rescale) ? m_new : m_run;
         const float corr = rescale ? ex2_approx(m_run - m_new) : 1.f;
         const float m_sub = (m_use == -INFINITY) ? 0.f : m_use;
-        if (__any_sync(0xffffffffu, rescale)) {
-          // O rows of this warp are rescaled once the previous tile's PV has completed.
+        // The single P buffer and (on a rescale) O are rewritten only once PV(g-1) is done.
+        // PV(g-2) is known complete (S(g) was ready), so this parity wait is unambiguous.
+        if (g >= 1) {
           live = mbar_wait(bar(kBarODone), (g - 1) & 1, abort, prm.err, 9);
           live = __all_sync(0xffffffffu, live);
           if (!live) continue;
+        }
+        if (__any_sync(0xffffffffu, rescale)) {
           tc_fence_after();
 #pragma unroll 1
           for (int c = 0; c < 8; ++c) {
@@ -647,7 +651,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // P row hd, tokens th*128 .. th*128+127: 16 chunks of 8 tokens in atoms of 64.
         float psum = 0.f;
-        uint8_t* prow = p_base + s * kPBuf + hd * 128;
+        uint8_t* prow = p_base + hd * 128;
 #pragma unroll
         for (int c = 0; c < 16; ++c) {
           uint32_t w[4];
@@ -796,11 +800,13 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-int make_map_bf16(CUtensorMap* m, const void* base, uint64_t rows, uint32_t box_rows) {
+// 2-D bf16 map of `rows` rows of `cols` elements, boxes of box_rows x 64, 128B swizzle.
+int make_map_bf16(CUtensorMap* m, const void* base, uint64_t rows, uint32_t cols,
+                  uint32_t box_rows) {
   EncodeTiledFn f = encode_fn();
   if (f == nullptr) return hk::fail(HK_ECUDA, "cuTensorMapEncodeTiled unavailable");
-  cuuint64_t dims[2] = {(cuuint64_t)kDK, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)kDK * 2};
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
   cuuint32_t box[2] = {64, box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = f(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
@@ -859,8 +865,11 @@ int mla_sm100(const uint16_t* q, const uint16_t* kv_cache, const int32_t* block_
   if (clusters > kMaxClusters) clusters = kMaxClusters;
 
   CUtensorMap q_map, kv_map;
-  HK_TRY(make_map_bf16(&q_map, q, (uint64_t)num_tokens * kHeads, 64));
-  HK_TRY(make_map_bf16(&kv_map, kv_cache, (uint64_t)num_slots, 64));
+  // q: rows of 576 dims.  The page-blocked cache: every page is 9 blocks of 64 rows x 64 dims,
+  // so as a 2-D array it is (num_slots * 9) rows of 64 dims; block d of page p starts at row
+  // (p * 9 + d) * 64 and one box is a contiguous 8 KB.
+  HK_TRY(make_map_bf16(&q_map, q, (uint64_t)num_tokens * kHeads, kDK, 64));
+  HK_TRY(make_map_bf16(&kv_map, kv_cache, (uint64_t)num_slots * 9, 64, 64));
 
   mla_plan_kernel<<<1, 1024, 0, stream>>>(positions, num_tokens, clusters, plan, err_word());
   HK_TRY_LAUNCH("mla_plan_kernel");

@@ -117,6 +117,28 @@ __global__ void append_vec_kernel(const uint4* __restrict__ src, const int32_t* 
   for (int v = lane; v < row_vec; v += 32) out[v] = in[v];
 }
 
+// Page-blocked latent rows: 16-byte vector v of a row (8 elements) goes to block v / 8 of
+// the row's page, at row (slot % page_rows), column (v % 8) * 8.
+__global__ void append_blocked_kernel(const uint4* __restrict__ src,
+                                      const int32_t* __restrict__ slot, int32_t num_tokens,
+                                      int32_t row_vec, int32_t page_rows,
+                                      uint4* __restrict__ cache, int64_t num_slots,
+                                      unsigned long long* err) {
+  const int64_t t = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (t >= num_tokens) return;
+  const int s = slot[t];
+  if (s < 0 || s >= num_slots) {
+    if (lane == 0) hk_flag(err, hk::kErrAppendSlot, (unsigned)t);
+    return;
+  }
+  const uint4* in = src + t * row_vec;
+  uint4* page = cache + (int64_t)(s / page_rows) * page_rows * row_vec;
+  const int r = s % page_rows;
+  for (int v = lane; v < row_vec; v += 32)
+    page[(int64_t)(v >> 3) * page_rows * 8 + r * 8 + (v & 7)] = in[v];
+}
+
 // Two-buffer variant for GQA K and V rows.
 __global__ void append_kv_kernel(const uint4* __restrict__ k_src, const uint4* __restrict__ v_src,
                                  const int32_t* __restrict__ slot, int32_t num_tokens,
@@ -202,19 +224,30 @@ int hk_pack(const int32_t* lane_tokens, const int32_t* lane_pos, const int32_t* 
 }
 
 int hk_kv_append_bf16(const uint16_t* kv_new, const int32_t* slot_mapping, int32_t num_tokens,
-                      int32_t row_elems, uint16_t* kv_cache, int64_t num_slots, void* stream) {
+                      int32_t row_elems, int32_t page_rows, uint16_t* kv_cache, int64_t num_slots,
+                      void* stream) {
   HK_TRY(hk::ensure_device());
   HK_REQUIRE(kv_new && slot_mapping && kv_cache, "hk_kv_append_bf16: null pointer");
   HK_REQUIRE(num_tokens >= 0 && row_elems > 0 && row_elems % 8 == 0 && num_slots > 0,
              "hk_kv_append_bf16: row_elems %d must be a positive multiple of 8", row_elems);
+  HK_REQUIRE(page_rows >= 0 && (page_rows == 0 || (row_elems % 64 == 0 && num_slots % page_rows == 0)),
+             "hk_kv_append_bf16: page_rows %d needs row_elems %% 64 == 0 and whole pages",
+             page_rows);
   HK_REQUIRE(((uintptr_t)kv_new | (uintptr_t)kv_cache) % 16 == 0,
              "hk_kv_append_bf16: buffers must be 16-byte aligned");
   if (num_tokens == 0) return HK_OK;
   const int64_t threads = (int64_t)num_tokens * 32;
-  append_vec_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
-      (const uint4*)kv_new, slot_mapping, num_tokens, row_elems / 8, (uint4*)kv_cache, num_slots,
-      hk::err_word());
-  HK_TRY_LAUNCH("append_vec_kernel");
+  if (page_rows == 0) {
+    append_vec_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+        (const uint4*)kv_new, slot_mapping, num_tokens, row_elems / 8, (uint4*)kv_cache,
+        num_slots, hk::err_word());
+    HK_TRY_LAUNCH("append_vec_kernel");
+  } else {
+    append_blocked_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+        (const uint4*)kv_new, slot_mapping, num_tokens, row_elems / 8, page_rows,
+        (uint4*)kv_cache, num_slots, hk::err_word());
+    HK_TRY_LAUNCH("append_blocked_kernel");
+  }
   return HK_OK;
 }
 

@@ -47,10 +47,6 @@ class MlaDecodeStep:
         self.d_q = torch.empty((T, heads, 576), dtype=torch.bfloat16, device=self.device)
         self.d_kv_new = torch.empty((T, 576), dtype=torch.bfloat16, device=self.device)
 
-    def launches_per_step(self) -> int:
-        before = hk.kernel_launches()
-        return before  # resolved by the caller as a difference
-
     def run(self, lane_tokens, lane_pos, q, kv_new, num_tokens: int, stream=None):
         """One step from device tensors; returns (out, lse) views of the first num_tokens rows."""
         s = hk.stream_ptr(stream)
@@ -61,7 +57,7 @@ class MlaDecodeStep:
                 hk.ptr(p["positions"]), hk.ptr(p["slot_mapping"]), hk.ptr(p["token_lane"]),
                 hk.ptr(p["active"]), s)
         hk.call("hk_kv_append_bf16", hk.ptr(kv_new), hk.ptr(p["slot_mapping"]), num_tokens, 576,
-                hk.ptr(self.cache), self.cache.shape[0], s)
+                self.page_size, hk.ptr(self.cache), self.cache.shape[0], s)
         hk.call("hk_mla_decode", hk.ptr(q), hk.ptr(self.cache), hk.ptr(self.block_table),
                 self.block_table.shape[1], hk.ptr(p["cu_seqlens"]), hk.ptr(p["positions"]),
                 self.lanes, num_tokens, self.heads, self.page_size, self.cache.shape[0],

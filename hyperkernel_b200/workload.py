@@ -87,6 +87,17 @@ def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
     return u.astype(np.uint16)
 
 
+def latent_rows(cache: np.ndarray, slots, page_rows: int = 64) -> np.ndarray:
+    """Rows `slots` of a page-blocked latent cache ([slots][row] array), as [len][row]."""
+    slots = np.asarray(slots, dtype=np.int64)
+    row = cache.shape[1]
+    flat = cache.reshape(-1)
+    e = np.arange(row, dtype=np.int64)
+    off = ((slots // page_rows) * page_rows * row)[:, None] + ((e // 64) * page_rows * 64)[None, :] \
+        + ((slots % page_rows) * 64)[:, None] + (e % 64)[None, :]
+    return flat[off]
+
+
 def bf16_bits_to_f32(b: np.ndarray) -> np.ndarray:
     return (np.ascontiguousarray(b, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
 

@@ -78,10 +78,19 @@ int hk_pack(const int32_t* lane_tokens, const int32_t* lane_pos, const int32_t* 
 /* a8  KV append into the paged cache                                                    */
 /* ------------------------------------------------------------------------------------ */
 
-/* MLA latent rows: kv_new[T][row_elems] bf16 -> kv_cache[slot][row_elems] bf16
- * (row_elems = 576 = 512 latent + 64 rope for the configs; a multiple of 8). */
+/* MLA latent rows: kv_new[T][row_elems] bf16 -> the cache row `slot` (row_elems = 576 =
+ * 512 latent + 64 rope for the configs).
+ * page_rows == 0: row-major cache, element (slot, e) at slot * row_elems + e (row_elems a
+ * multiple of 8).
+ * page_rows  > 0: the page-blocked latent cache that hk_mla_decode reads: pages of page_rows
+ * rows, each page storing its rows in blocks of 64 elements, block-major, so that one block
+ * of one page is a contiguous page_rows x 64 tile:
+ *   element (slot, e) at (slot / page_rows) * page_rows * row_elems
+ *                        + (e / 64) * page_rows * 64 + (slot % page_rows) * 64 + e % 64
+ * (row_elems a multiple of 64). */
 int hk_kv_append_bf16(const uint16_t* kv_new, const int32_t* slot_mapping, int32_t num_tokens,
-                      int32_t row_elems, uint16_t* kv_cache, int64_t num_slots, void* stream);
+                      int32_t row_elems, int32_t page_rows, uint16_t* kv_cache, int64_t num_slots,
+                      void* stream);
 
 /* MLA latent rows quantised to e4m3 with one fp32 scale per row:
  * scale = max(amax(row), 1e-12) / 448, q = e4m3_rn_satfinite(x / scale). */
@@ -108,8 +117,9 @@ int hk_gqa_decode_f32(const float* q, const float* k_cache, const float* v_cache
                       int32_t q_heads, int32_t kv_heads, int32_t head_dim, int32_t page_size,
                       int64_t num_slots, float scale, float* out, float* lse, void* stream);
 
-/* MLA absorbed decode, bf16 (config 2): q[T][heads][576], kv_cache[slot][576] (latent 512
- * then rope 64), out[T][heads][512] bf16, lse[T][heads] fp32.  Scores use all 576 dims,
+/* MLA absorbed decode, bf16 (config 2): q[T][heads][576], kv_cache in the page-blocked
+ * layout of hk_kv_append_bf16 with page_rows = page_size (576 = latent 512 then rope 64 per
+ * row), out[T][heads][512] bf16, lse[T][heads] fp32.  Scores use all 576 dims,
  * values the first 512.  The work is split across SMs by KV range; partials of split
  * lanes go to `workspace` (size from hk_mla_workspace_size) and are merged by LSE.
  * impl: 0 = best available (tcgen05 when heads == 128 and pages hold 64 rows), 1 = portable

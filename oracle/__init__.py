@@ -69,12 +69,14 @@ def pack(lane_tokens, lane_pos, block_table, page_size, num_pages, max_tokens):
     return out
 
 
-def kv_append_bf16(kv_new, slot, cache):
+def kv_append_bf16(kv_new, slot, cache, page_rows=64):
+    """Writes rows into `cache` ([slots][row] array holding the page-blocked layout when
+    page_rows > 0, row-major when 0)."""
     kv_new = _c(kv_new, np.uint16)
     slot = _c(slot, np.int32)
     lib().orc_kv_append_u16.restype = C.c_int
     return lib().orc_kv_append_u16(_p(kv_new), _p(slot), C.c_int(slot.shape[0]),
-                                   C.c_int(kv_new.shape[1]), _p(cache),
+                                   C.c_int(kv_new.shape[1]), C.c_int(page_rows), _p(cache),
                                    C.c_int64(cache.shape[0]))
 
 
@@ -112,6 +114,7 @@ def gqa_decode(q, kc, vc, bt, cu, positions, q_heads, kv_heads, head_dim, page_s
 
 def mla_decode(q, bt, cu, positions, page_size, scale, kv_bf16=None, kv_fp8=None, kv_scale=None,
                kv_begin=None, kv_end=None):
+    """kv_bf16 is in the page-blocked layout (pages of page_size rows); kv_fp8 row-major."""
     q = _c(q, np.uint16)
     bt = _c(bt, np.int32)
     T, H = q.shape[0], q.shape[1]

@@ -155,15 +155,24 @@ int orc_pack(const int32_t* lane_tokens, const int32_t* lane_pos, const int32_t*
 /* a8 KV append                                                                        */
 /* ---------------------------------------------------------------------------------- */
 
-int orc_kv_append_u16(const uint16_t* src, const int32_t* slot, int T, int row, uint16_t* cache,
-                      int64_t num_slots) {
+/* Offset of element (slot, e) of a latent cache: row-major when page_rows == 0, else the
+ * page-blocked layout (pages of page_rows rows, each storing its rows in blocks of 64
+ * elements, block-major) that the device's latent cache uses. */
+static int64_t latent_off(int64_t slot, int e, int row, int page_rows) {
+  if (page_rows == 0) return slot * row + e;
+  return (slot / page_rows) * page_rows * row + (int64_t)(e / 64) * page_rows * 64 +
+         (slot % page_rows) * 64 + e % 64;
+}
+
+int orc_kv_append_u16(const uint16_t* src, const int32_t* slot, int T, int row, int page_rows,
+                      uint16_t* cache, int64_t num_slots) {
   int err = 0;
   for (int t = 0; t < T; ++t) {
     if (slot[t] < 0 || slot[t] >= num_slots) {
       err = 3;
       continue;
     }
-    memcpy(cache + (int64_t)slot[t] * row, src + (int64_t)t * row, sizeof(uint16_t) * row);
+    for (int e = 0; e < row; ++e) cache[latent_off(slot[t], e, row, page_rows)] = src[(int64_t)t * row + e];
   }
   return err;
 }
@@ -248,7 +257,8 @@ void orc_gqa_decode_f32(const float* q, const float* kc, const float* vc, const 
   }
 }
 
-/* MLA absorbed attention over a bf16 (kv_fp8 == NULL) or e4m3*scale latent cache.
+/* MLA absorbed attention over a page-blocked bf16 latent cache (kv_fp8 == NULL; blocks of 64
+ * elements in pages of page_size rows) or a row-major e4m3*scale latent cache.
  * Query row t attends KV rows [max(0, kv_begin[b]), min(positions[t] + 1, kv_end[b]))
  * (kv_begin / kv_end may be NULL: the whole causal prefix).  Scores over 576 dims, values
  * the first 512, fp64 accumulation; out[T][heads][512] fp32, lse[T][heads]. */
@@ -276,7 +286,7 @@ void orc_mla_decode(const uint16_t* q, const uint16_t* kv_bf16, const uint8_t* k
           (int64_t)bt[(int64_t)b * bt_stride + p / page_size] * page_size + p % page_size;
       for (int d = 0; d < DK; ++d)
         k[(int64_t)j * DK + d] = kv_fp8 ? orc_e4m3_to_f32(kv_fp8[slot * DK + d]) * kv_scale[slot]
-                                        : bf16_to_f32(kv_bf16[slot * DK + d]);
+                                        : bf16_to_f32(kv_bf16[latent_off(slot, d, DK, page_size)]);
     }
 #pragma omp parallel for schedule(dynamic)
     for (int h = 0; h < heads; ++h) {

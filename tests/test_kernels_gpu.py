@@ -116,7 +116,8 @@ def test_append_rejects_bad_slot(hk, cuda):
                       dev(np.array([3, 64], np.int32), cuda), c)
     with pytest.raises(hk.HKError, match="append slot"):
         hk.check_errors()
-    assert int(c[3, 0]) == 1 and int(c.sum()) == 576
+    # page-blocked layout: element (slot 3, dim 0) sits at row 3 of block 0 of page 0
+    assert int(c.view(-1)[3 * 64]) == 1 and int(c.sum()) == 576
 
 
 # ------------------------------------------------------------------------------------------

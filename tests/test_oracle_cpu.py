@@ -121,13 +121,12 @@ def test_mla_oracle_matches_numpy(orc):
     T = lay.num_tokens
     got, lse = orc.mla_decode(inp["q"], lay.block_table, o["cu_seqlens"], o["positions"][:T], 64,
                               inp["scale"], kv_bf16=inp["kv_cache"])
-    cache = W.bf16_bits_to_f32(inp["kv_cache"]).astype(np.float64)
     q = W.bf16_bits_to_f32(inp["q"]).astype(np.float64)
     for t in range(T):
         b = t
         pos = int(o["positions"][t])
         slots = [int(lay.block_table[b, p // 64]) * 64 + p % 64 for p in range(pos + 1)]
-        k = cache[slots]
+        k = W.bf16_bits_to_f32(W.latent_rows(inp["kv_cache"], slots)).astype(np.float64)
         s = q[t] @ k.T * inp["scale"]
         p = np.exp(s - s.max(1, keepdims=True))
         want = (p @ k[:, :512]) / p.sum(1, keepdims=True)
@@ -144,3 +143,16 @@ def test_workload_generator_is_seeded():
     used = lay.block_table[lay.block_table > 0]
     assert len(np.unique(used)) == len(used), "pages shared between lanes"
     assert 0 not in used
+
+
+def test_latent_layout_append_roundtrip(orc):
+    """The page-blocked layout written by the oracle's append reads back through latent_rows."""
+    rng = W.Rng(8)
+    cache = np.zeros((4 * 64, 576), np.uint16)
+    rows = W.f32_to_bf16_bits(rng.normal(5 * 576).astype(np.float32)).reshape(5, 576)
+    slots = np.array([0, 63, 64, 130, 255], np.int32)
+    assert orc.kv_append_bf16(rows, slots, cache) == 0
+    assert np.array_equal(W.latent_rows(cache, slots), rows)
+    # one block of one page is a contiguous 64 x 64 tile
+    page1_block2 = cache.reshape(-1)[64 * 576 + 2 * 64 * 64: 64 * 576 + 3 * 64 * 64].reshape(64, 64)
+    assert np.array_equal(page1_block2[0], rows[2, 128:192])
