@@ -46,6 +46,7 @@ SIGNATURES = {
     "hk_permute": (C.c_int, [P, P, I32, I32, I32, P, P, P, P, P]),
     "hk_moe_workspace_size": (SZ, [I64, I32]),
     "hk_moe_grouped": (C.c_int, [P, P, I32, P, P, I64, I32, I32, I32, P, P, P, P, P, P, SZ, P]),
+    "hk_moe_grouped_noalloc": (C.c_int, [P, P, I32, P, P, I64, I32, I32, I32, P, P, P, P, P, P]),
     "hk_combine": (C.c_int, [P, I64, P, P, P, I32, I32, I32, P, P]),
     "hk_rope_table": (C.c_int, [I64, I32, F32, I32, F32, F32, F32, P]),
 }
@@ -302,6 +303,18 @@ def moe_grouped(xq, sx, offsets, perm_token, rows, hidden, inter, w13, s13, w2, 
     call("hk_moe_grouped", ptr(xq), ptr(sx), xq.shape[0], ptr(offsets), ptr(perm_token), rows, E,
          hidden, inter, ptr(w13), ptr(s13), ptr(w2), ptr(s2), ptr(out), ptr(workspace),
          workspace.numel(), stream_ptr(stream))
+    return out
+
+
+def moe_grouped_noalloc(xq, sx, offsets, perm_token, rows, hidden, inter, w13, s13, w2, s2,
+                        out=None, stream=None):
+    """hk_moe_grouped with the library's fixed scratch array (no workspace argument)."""
+    E = offsets.shape[0] - 1
+    if out is None:
+        out = torch.empty((max(rows, 1), hidden), dtype=torch.bfloat16, device=xq.device)
+    call("hk_moe_grouped_noalloc", ptr(xq), ptr(sx), xq.shape[0], ptr(offsets), ptr(perm_token),
+         rows, E, hidden, inter, ptr(w13), ptr(s13), ptr(w2), ptr(s2), ptr(out),
+         stream_ptr(stream))
     return out
 
 

@@ -15,6 +15,7 @@
 
 #include "common.cuh"
 #include "gemm_fp8.cuh"
+#include "moe.cuh"
 
 namespace {
 
@@ -414,6 +415,56 @@ size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 }  // namespace
 
+extern "C" size_t hk_moe_workspace_size(int64_t rows, int32_t inter);
+
+namespace hk {
+
+// The grouped FFN launcher behind hk_moe_grouped: `err` is the device error word the kernels
+// record bad rows in (nullptr: skipped without a record).
+int moe_grouped_run(const uint8_t* xq, const float* sx, int32_t tokens, const int32_t* offsets,
+                    const int32_t* perm_token, int64_t rows, int32_t num_experts, int32_t hidden,
+                    int32_t inter, const uint8_t* w13, const float* s13, const uint8_t* w2,
+                    const float* s2, uint16_t* y, void* workspace, size_t workspace_bytes,
+                    unsigned long long* err, cudaStream_t s) {
+  HK_TRY(hk::ensure_device());
+  HK_REQUIRE(xq && sx && offsets && perm_token && w13 && s13 && w2 && s2 && y,
+             "hk_moe_grouped: null pointer");
+  HK_REQUIRE(num_experts > 0 && num_experts <= kMaxExperts, "hk_moe_grouped: %d experts", num_experts);
+  HK_REQUIRE(hidden > 0 && hidden % 128 == 0 && inter > 0 && inter % 128 == 0,
+             "hk_moe_grouped: hidden %d and inter %d must be multiples of 128", hidden, inter);
+  HK_REQUIRE(((uintptr_t)xq | (uintptr_t)w13 | (uintptr_t)w2) % 16 == 0,
+             "hk_moe_grouped: operands must be 16-byte aligned");
+  HK_REQUIRE(tokens >= 0 && rows >= 0, "hk_moe_grouped: negative sizes");
+  if (rows == 0) return HK_OK;
+  const size_t need = hk_moe_workspace_size(rows, inter);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(HK_ESPACE, "hk_moe_grouped: workspace of %zu bytes, %zu needed", workspace_bytes, need);
+  const int64_t rows_cap = rows;
+  uint8_t* base = reinterpret_cast<uint8_t*>(workspace);
+  uint8_t* hq = base;
+  float* hs = reinterpret_cast<float*>(base + align256((size_t)rows_cap * inter));
+  int32_t* tiles = reinterpret_cast<int32_t*>(
+      reinterpret_cast<uint8_t*>(hs) + align256((size_t)rows_cap * (inter / 128) * sizeof(float)));
+  const int32_t max_tiles = (int32_t)(rows_cap / kTileRows + kMaxExperts + 1);
+  int32_t* tile_expert = tiles;
+  int32_t* tile_row = tiles + max_tiles;
+  int32_t* num_tiles = tiles + 2 * max_tiles;
+  tile_list_kernel<<<1, 32, 0, s>>>(offsets, num_experts, rows, max_tiles, tile_expert, tile_row,
+                                    num_tiles, err);
+  HK_TRY_LAUNCH("tile_list_kernel");
+  const int32_t tokens_limit = tokens;
+  moe_up_kernel<<<dim3(max_tiles, inter / 128), 256, 0, s>>>(
+      xq, sx, offsets, perm_token, tile_expert, tile_row, num_tiles, hidden, inter, tokens_limit,
+      w13, s13, hq, hs, err);
+  HK_TRY_LAUNCH("moe_up_kernel");
+  moe_down_kernel<<<dim3(max_tiles, hidden / 64), 256, 0, s>>>(
+      hq, hs, offsets, tile_expert, tile_row, num_tiles, hidden, inter, w2, s2, y);
+  HK_TRY_LAUNCH("moe_down_kernel");
+  return HK_OK;
+}
+
+}  // namespace hk
+
 extern "C" {
 
 int hk_route(const float* logits, const float* bias, int32_t tokens, int32_t num_experts,
@@ -457,42 +508,9 @@ int hk_moe_grouped(const uint8_t* xq, const float* sx, int32_t tokens, const int
                    int32_t inter, const uint8_t* w13, const float* s13, const uint8_t* w2,
                    const float* s2, uint16_t* y, void* workspace, size_t workspace_bytes,
                    void* stream) {
-  HK_TRY(hk::ensure_device());
-  HK_REQUIRE(xq && sx && offsets && perm_token && w13 && s13 && w2 && s2 && y,
-             "hk_moe_grouped: null pointer");
-  HK_REQUIRE(num_experts > 0 && num_experts <= kMaxExperts, "hk_moe_grouped: %d experts", num_experts);
-  HK_REQUIRE(hidden > 0 && hidden % 128 == 0 && inter > 0 && inter % 128 == 0,
-             "hk_moe_grouped: hidden %d and inter %d must be multiples of 128", hidden, inter);
-  HK_REQUIRE(((uintptr_t)xq | (uintptr_t)w13 | (uintptr_t)w2) % 16 == 0,
-             "hk_moe_grouped: operands must be 16-byte aligned");
-  HK_REQUIRE(tokens >= 0 && rows >= 0, "hk_moe_grouped: negative sizes");
-  if (rows == 0) return HK_OK;
-  const size_t need = hk_moe_workspace_size(rows, inter);
-  if (workspace == nullptr || workspace_bytes < need)
-    return hk::fail(HK_ESPACE, "hk_moe_grouped: workspace of %zu bytes, %zu needed", workspace_bytes, need);
-  const int64_t rows_cap = rows;
-  uint8_t* base = reinterpret_cast<uint8_t*>(workspace);
-  uint8_t* hq = base;
-  float* hs = reinterpret_cast<float*>(base + align256((size_t)rows_cap * inter));
-  int32_t* tiles = reinterpret_cast<int32_t*>(
-      reinterpret_cast<uint8_t*>(hs) + align256((size_t)rows_cap * (inter / 128) * sizeof(float)));
-  const int32_t max_tiles = (int32_t)(rows_cap / kTileRows + kMaxExperts + 1);
-  int32_t* tile_expert = tiles;
-  int32_t* tile_row = tiles + max_tiles;
-  int32_t* num_tiles = tiles + 2 * max_tiles;
-  cudaStream_t s = (cudaStream_t)stream;
-  tile_list_kernel<<<1, 32, 0, s>>>(offsets, num_experts, rows, max_tiles, tile_expert, tile_row,
-                                    num_tiles, hk::err_word());
-  HK_TRY_LAUNCH("tile_list_kernel");
-  const int32_t tokens_limit = tokens;
-  moe_up_kernel<<<dim3(max_tiles, inter / 128), 256, 0, s>>>(
-      xq, sx, offsets, perm_token, tile_expert, tile_row, num_tiles, hidden, inter, tokens_limit,
-      w13, s13, hq, hs, hk::err_word());
-  HK_TRY_LAUNCH("moe_up_kernel");
-  moe_down_kernel<<<dim3(max_tiles, hidden / 64), 256, 0, s>>>(
-      hq, hs, offsets, tile_expert, tile_row, num_tiles, hidden, inter, w2, s2, y);
-  HK_TRY_LAUNCH("moe_down_kernel");
-  return HK_OK;
+  return hk::moe_grouped_run(xq, sx, tokens, offsets, perm_token, rows, num_experts, hidden, inter,
+                             w13, s13, w2, s2, y, workspace, workspace_bytes, hk::err_word(),
+                             (cudaStream_t)stream);
 }
 
 int hk_combine(const uint16_t* y, int64_t rows, const float* perm_weight, const int32_t* inv,

@@ -209,6 +209,22 @@ int hk_moe_grouped(const uint8_t* xq, const float* sx, int32_t tokens, const int
                    const float* s2, uint16_t* y, void* workspace, size_t workspace_bytes,
                    void* stream);
 
+/* hk_moe_grouped without a workspace argument, for callers that cannot allocate device memory
+ * (an engine reaching this library only through the C ABI with no CUDA allocator of its own, a
+ * pool allocator that forbids raw cudaMalloc, a step loop that must not take cudaMalloc's
+ * device-wide synchronisation).  No counterpart in the reference.  Its scratch is a fixed
+ * 2,167,040-byte device array that every GPU loading this library holds until exit: at most
+ * 1024 permuted rows and inter <= 2048, larger problems are refused with HK_EINVAL.  It
+ * allocates nothing.  All calls share the array: calls that overlap on the GPU race and must
+ * be serialised.  The first call on a device looks the array up (cudaGetSymbolAddress) and
+ * should come before any stream capture.  Out-of-range rows are skipped but not recorded in
+ * the device error word. */
+int hk_moe_grouped_noalloc(const uint8_t* xq, const float* sx, int32_t tokens,
+                           const int32_t* offsets, const int32_t* perm_token, int64_t rows,
+                           int32_t num_experts, int32_t hidden, int32_t inter,
+                           const uint8_t* w13, const float* s13, const uint8_t* w2,
+                           const float* s2, uint16_t* y, void* stream);
+
 /* out[t][hidden] bf16 = sum_k perm_weight[inv[t,k]] * y[inv[t,k]] (+ shared[t] when not
  * NULL), fp32 accumulation in k order; y has `rows` rows. */
 int hk_combine(const uint16_t* y, int64_t rows, const float* perm_weight, const int32_t* inv,
