@@ -21,7 +21,7 @@ HEADER = PKG.parent / "include" / "hk.h"
 
 HK_OK, HK_EINVAL, HK_ENODEV, HK_ECUDA, HK_EDEVICE, HK_ESPACE, HK_ESTATE = 0, -1, -2, -3, -4, -5, -6
 
-P, I32, I64, F32, SZ = C.c_void_p, C.c_int32, C.c_int64, C.c_float, C.c_size_t
+P, I32, I64, F32, SZ, U64 = C.c_void_p, C.c_int32, C.c_int64, C.c_float, C.c_size_t, C.c_uint64
 
 # Prototypes of every entry point in include/hk.h (kept in header order).
 SIGNATURES = {
@@ -48,6 +48,24 @@ SIGNATURES = {
     "hk_moe_grouped": (C.c_int, [P, P, I32, P, P, I64, I32, I32, I32, P, P, P, P, P, P, SZ, P]),
     "hk_moe_grouped_noalloc": (C.c_int, [P, P, I32, P, P, I64, I32, I32, I32, P, P, P, P, P, P]),
     "hk_combine": (C.c_int, [P, I64, P, P, P, I32, I32, I32, P, P]),
+    "hk_open": (C.c_int, [P, P]),
+    "hk_close": (None, [P]),
+    "hk_pools": (C.c_int, [P, P, P]),
+    "hk_push": (C.c_int, [P, P]),
+    "hk_drain": (C.c_int, [P, P, SZ, P, P, SZ, P]),
+    "hk_encode_share": (C.c_int, [P, P, P, SZ, P]),
+    "hk_kernel_ops_of": (C.c_int, [P, P]),
+    "hk_engine_defaults": (None, [P]),
+    "hk_engine_create": (C.c_int, [P, P, P]),
+    "hk_engine_destroy": (None, [P]),
+    "hk_engine_submit": (C.c_int, [P, P, SZ, P, U64, P, SZ, P]),
+    "hk_engine_reset": (C.c_int, [P, P]),
+    "hk_engine_reset_answer": (C.c_int, [P, U64, I64, P]),
+    "hk_engine_close": (C.c_int, [P]),
+    "hk_engine_run": (C.c_int, [P]),
+    "hk_engine_hangup": (C.c_int, [P, U64]),
+    "hk_engine_outputs": (C.c_int, [P, U64, I64, P, SZ, P, P, SZ]),
+    "hk_engine_metrics": (C.c_int, [P, P, P, SZ, P, P, SZ, P]),
     "hk_rope_table": (C.c_int, [I64, I32, F32, I32, F32, F32, F32, P]),
 }
 

@@ -232,6 +232,214 @@ int hk_combine(const uint16_t* y, int64_t rows, const float* perm_weight, const 
                uint16_t* out, void* stream);
 
 /* ------------------------------------------------------------------------------------ */
+/* Kernel boundary: the reference's `Kernel` trait (src/gpu/mod.rs:42-46)                */
+/*   pools() -> hk_pools, push(&Share) -> hk_push, drain() -> hk_drain                   */
+/* Types mirror Share / Command / Event / Sampled (src/gpu/mod.rs:13-40) as flat arrays.  */
+/* ------------------------------------------------------------------------------------ */
+
+typedef struct hk_handle hk_handle;
+
+/* Sampling, src/engine/request.rs:142-149. */
+typedef struct {
+    float temperature;
+    float top_p;
+    uint32_t top_k;
+    uint32_t logprobs;
+    uint64_t seed;
+} hk_sampling;
+
+#define HK_CMD_END 0    /* End { lane } */
+#define HK_CMD_PAGES 1  /* Pages { lane, from, upto, row } */
+#define HK_CMD_SEAT 2   /* Seat { lane, pos, back, sampling } */
+#define HK_CMD_PROMPT 3 /* Prompt { lane, tokens } */
+#define HK_CMD_START 4  /* Start { lane } */
+
+/* One Command.  Pages: pos = from, upto, count = row length, arena = offset (in words) of
+ * the i32 row in hk_share.arena.  Seat: pos, back, sampling.  Prompt: count tokens (u32 bit
+ * patterns) at arena.  Unused fields are ignored. */
+typedef struct {
+    uint32_t kind;
+    uint32_t lane;
+    uint32_t pos;
+    uint32_t upto;
+    uint32_t count;
+    uint32_t arena;
+    int32_t back[3];
+    uint32_t reserved;
+    hk_sampling sampling;
+} hk_command;
+
+/* Share { at, horizon, commands }: the commands take effect at step `at`; the device may run
+ * steps up to `horizon`. */
+typedef struct {
+    uint32_t at;
+    uint32_t horizon;
+    const hk_command* commands;
+    size_t n_commands;
+    const int32_t* arena;
+    size_t arena_words;
+} hk_share;
+
+#define HK_EV_IDLE 0     /* Idle { step } */
+#define HK_EV_STEP 1     /* Step { step, lanes } */
+#define HK_EV_PROMPTED 2 /* Prompted { lane, token, clipped } */
+
+/* One Event.  Step: `ids` is the offset in the drain's id array of width * block sampled ids,
+ * lane-major; a lane's list ends at its first -2 (lanes that did not decode start with -2).
+ * Prompted: `token` (negative = the logits were not finite) and `clipped`.  Sampled
+ * logprob rows do not cross this boundary yet: every Sampled has an empty logprob list. */
+typedef struct {
+    uint32_t kind;
+    uint32_t step;
+    uint32_t lane;
+    int32_t token;
+    int32_t clipped;
+    uint32_t ids;
+} hk_event;
+
+/* The device model behind a handle.  HK_MODEL_FNV is the reference's test model
+ * (tests/engine.rs:56-62): the next token of a sequence is an FNV-style fold of its tokens,
+ * which the device reads back through the lane's block-table row from the paged token pool,
+ * checking that every position was written and that the window pages mirror the pages; a
+ * violation fails the next hk_drain.  A decode step emits 1 + ((step + lane) mod block)
+ * tokens per lane, the draft acceptance rule of the reference's test device, capped at the
+ * lane's reserved rows. */
+#define HK_MODEL_FNV 1
+
+typedef struct {
+    uint32_t model;          /* HK_MODEL_FNV */
+    uint32_t page_rows;      /* Pool.page_rows: token rows per page */
+    uint32_t entries;        /* Pool.entries: page entries of a block-table row */
+    uint32_t window;         /* Pool.window: window-page entries of a row */
+    uint32_t width;          /* lanes (Model.batches.last) */
+    uint32_t context;        /* Model.context */
+    uint32_t chunk;          /* Model.chunks[0]: most tokens of one Prompt */
+    uint32_t block;          /* Model.block: 1 + draft positions */
+    uint64_t pages;          /* page pool size, unit 0 = scratch (returned by hk_pools) */
+    uint64_t window_pages;   /* window page pool size, unit 0 = scratch */
+    int32_t clip;            /* the `clipped` flag the test model returns with prompt replies */
+    int32_t device;          /* CUDA device ordinal */
+} hk_config;
+
+/* Opens a device kernel: allocates the pools, the block-table rows and the lane state on
+ * `device` and returns its handle.  One handle per process and GPU; a handle's calls are
+ * not thread-safe. */
+int hk_open(const hk_config* config, hk_handle** handle);
+void hk_close(hk_handle* handle);
+/* Kernel::pools: (pages, window_pages). */
+int hk_pools(const hk_handle* handle, size_t* pages, size_t* window_pages);
+/* Kernel::push: copies the share (the caller keeps ownership of its arrays).  share->at must
+ * be the previous horizon + 1 (HK_ESTATE otherwise) and horizon >= at (HK_EINVAL). */
+int hk_push(hk_handle* handle, const hk_share* share);
+/* Kernel::drain: applies the commands due, runs the granted steps and returns the events
+ * (Prompted replies in push order).  *n / *ids_n receive the counts; when `cap` or `ids_cap`
+ * is too small it returns HK_ESPACE with the sizes needed and keeps the events for the next
+ * call.  A device-side violation returns HK_EDEVICE with the first one's message. */
+int hk_drain(hk_handle* handle, hk_event* events, size_t cap, size_t* n, int32_t* ids,
+             size_t ids_cap, size_t* ids_n);
+
+/* The request-ring encoding of a share (src/gpu/feed.rs:40-103, src/gpu/ring.rs:59-125):
+ * one slot per command (u32 message id at byte 0, the message body at byte 16, slot size
+ * 16 + widest body rounded up to 16 bytes) followed by the side blocks the messages' spans
+ * point at (Pages rows, Prompt tokens padded to `chunk` words).  Span addresses are byte
+ * offsets from the start of `out`.  hk_push sends exactly these bytes to the device.
+ * Host-only. */
+int hk_encode_share(const hk_config* config, const hk_share* share, uint8_t* out, size_t cap,
+                    size_t* bytes);
+
+/* ------------------------------------------------------------------------------------ */
+/* Engine: engine::run and its job channel (src/engine/mod.rs:38-359)                     */
+/* ------------------------------------------------------------------------------------ */
+
+typedef struct hk_engine hk_engine;
+
+/* A Kernel implementation as callbacks (what hk_engine_run drives).  drain's contract is
+ * hk_drain's, HK_ESPACE included; `error` returns the message after a failed call. */
+typedef struct {
+    void* self;
+    int (*pools)(void* self, size_t* pages, size_t* window_pages);
+    int (*push)(void* self, const hk_share* share);
+    int (*drain)(void* self, hk_event* events, size_t cap, size_t* n, int32_t* ids,
+                 size_t ids_cap, size_t* ids_n);
+    const char* (*error)(void* self);
+} hk_kernel_ops;
+
+/* Fills `ops` with the callbacks of a device handle. */
+int hk_kernel_ops_of(hk_handle* handle, hk_kernel_ops* ops);
+
+#define HK_UNBOUNDED UINT64_MAX
+
+/* Pool (src/bundle.rs), Model, Plan (src/engine/pacing.rs:1-13) and EngineConfig
+ * (src/engine/mod.rs:25-36) fields the engine reads. */
+typedef struct {
+    uint32_t page_rows, entries, window, window_keep;
+    uint32_t context, width, chunk, block;
+    int32_t pad;
+    uint32_t lead;
+    uint64_t budget;   /* Plan.budget, HK_UNBOUNDED = None */
+    uint64_t every, headroom;
+    uint64_t gap, ahead, max_draft_positions;
+} hk_engine_config;
+
+/* Plan::default() and EngineConfig::default() (budget None, every 1, headroom 2048; gap 16,
+ * lead 2, ahead 16, max_draft_positions 16); the pool and model fields are zeroed. */
+void hk_engine_defaults(hk_engine_config* config);
+
+/* The engine over a kernel.  The job calls below may come from any thread; hk_engine_run
+ * from one.  Fails with HK_EINVAL when block - 1 > max_draft_positions (run's check). */
+int hk_engine_create(const hk_engine_config* config, const hk_kernel_ops* kernel,
+                     hk_engine** engine);
+void hk_engine_destroy(hk_engine* engine);
+
+/* Job::Run(Request { prompt, sampling, limit, stop, out }): queues a request; *request
+ * names its output channel.  limit = HK_UNBOUNDED for no limit. */
+int hk_engine_submit(hk_engine* engine, const uint32_t* prompt, size_t n, const hk_sampling* s,
+                     uint64_t limit, const uint32_t* stop, size_t n_stop, uint64_t* request);
+/* Job::Reset: queues a prefix-cache reset; hk_engine_reset_answer waits up to timeout_ms
+ * (negative = forever) for the number of pages it freed (HK_ESTATE on timeout). */
+int hk_engine_reset(hk_engine* engine, uint64_t* ticket);
+int hk_engine_reset_answer(hk_engine* engine, uint64_t ticket, int64_t timeout_ms,
+                           uint64_t* freed);
+/* Drops the job sender: hk_engine_run returns once the engine is idle. */
+int hk_engine_close(hk_engine* engine);
+/* engine::run: 0 when the jobs closed and every request ended, else the kernel's error code
+ * (message in hk_last_error) after every held, waiting and queued request was refused. */
+int hk_engine_run(hk_engine* engine);
+/* The request's listener went away: its next token send fails and ends it (End::Stop). */
+int hk_engine_hangup(hk_engine* engine, uint64_t request);
+
+#define HK_OUT_SEATED 0 /* value = cached tokens */
+#define HK_OUT_TOKEN 1  /* value = token id */
+#define HK_OUT_END 2    /* end = HK_END_* */
+#define HK_END_STOP 0
+#define HK_END_LENGTH 1
+#define HK_END_REFUSED 2
+
+typedef struct {
+    uint32_t kind;
+    uint32_t end;
+    int64_t value;
+} hk_out;
+
+/* Takes up to `cap` of the request's outputs (Out::Seated / Token / End) in order, waiting
+ * up to timeout_ms (negative = forever, 0 = no wait) for the first.  The message of a
+ * Refused end is copied into `message` (NUL-terminated, truncated to message_cap). */
+int hk_engine_outputs(hk_engine* engine, uint64_t request, int64_t timeout_ms, hk_out* out,
+                      size_t cap, size_t* n, char* message, size_t message_cap);
+
+/* StepMetrics (src/engine/metrics.rs:4-19) summed over the run, as Metrics::total. */
+typedef struct {
+    uint64_t running, waiting, held_pages, pages, spec_tokens, prompt_tokens, cached_tokens,
+        prefill_tokens, generation_tokens, preemptions, top_p_clipped, drafts;
+} hk_step_metrics;
+
+/* Metrics::total plus accepted_per_pos (its length in *n_pos) and the iteration_tokens
+ * histogram (bounds 1, 8, 16, ..., 16384: 14 counts) with its sum. */
+int hk_engine_metrics(hk_engine* engine, hk_step_metrics* total, uint64_t* accepted_per_pos,
+                      size_t pos_cap, size_t* n_pos, uint64_t* counts, size_t counts_cap,
+                      double* sum);
+
+/* ------------------------------------------------------------------------------------ */
 /* RoPE table (pinned against the reference's fixtures; src/gpu/load.rs:824-846)         */
 /* ------------------------------------------------------------------------------------ */
 
