@@ -1,15 +1,289 @@
-// tcgen05 FP8 block-scaled GEMM: placeholder until the kernel lands; reports itself
-// unsupported so hk_gemm_fp8 takes the portable kernel.
+// a11 on the tensor cores: y[m][n] bf16 = sum_kb (xq . wq^T)_kb * sx[m][kb] * sw[n/128][kb],
+// e4m3 operands, fp32 block scales (activations 1x128, weights 128x128), fp32 accumulation.
+//
+// Persistent kernel, one CTA per SM, tile 128 tokens x 256 weight rows:
+//   warp 0      TMA producer: per 128-wide K block, the X tile (128 x 128 B) and the W tile
+//               (256 x 128 B), 128-byte swizzled, into a 4-stage ring (48 KB a stage);
+//   warp 1      MMA issuer: four tcgen05.mma kind::f8f6f4 (K = 32 each) per K block into a
+//               fresh fp32 accumulator in TMEM, double-buffered (2 x 256 columns);
+//   warps 2..9  scale promotion: each thread owns one row and 128 columns, which lie in one
+//               128-row weight scale block, so a K block's partial sums take one scalar
+//               sx[row][kb] * sw[group][kb]; acc += partial * scale in registers, then the
+//               TMEM buffer goes back to the MMA warp.  After the last K block, bf16 stores.
+// Registers: 10 warps put 3 warps on some SM sub-partitions, so a thread has at most 168; the
+// promotion loop reads TMEM 16 columns at a time to keep its 128 accumulators in registers.
+// Every wait is bounded (1 s); on a timeout the kernel records the error word, lets the
+// copies and MMAs in flight finish, frees TMEM and returns.
+#include <cuda.h>
+
 #include "common.cuh"
 #include "gemm_fp8.cuh"
+#include "sm100.cuh"
+
+namespace hk {
+namespace sm100 {
+
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+int make_map_u8(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+  EncodeTiledFn f = encode_tiled();
+  if (f == nullptr) return fail(HK_ECUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols};
+  cuuint32_t box[2] = {128, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = f(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(HK_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return HK_OK;
+}
+
+}  // namespace sm100
+}  // namespace hk
+
+namespace {
+
+using namespace hk::sm100;
+
+constexpr int kBM = 128, kBN = 256, kBK = 128;
+constexpr int kStages = 4;
+constexpr int kABytes = kBM * kBK;                  // 16 KB
+constexpr int kBBytes = kBN * kBK;                  // 32 KB
+constexpr int kStageBytes = kABytes + kBBytes;      // 48 KB
+constexpr int kOffCtl = kStages * kStageBytes;      // 192 KB
+constexpr int kSmemBytes = kOffCtl + 1024;
+constexpr int kThreads = 320;
+static_assert(kSmemBytes <= 232448, "shared memory budget");
+
+constexpr int kBarFull = 0;     // [kStages] TMA bytes of a stage landed
+constexpr int kBarEmpty = 64;   // [kStages] the stage's MMAs completed
+constexpr int kBarTFull = 128;  // [2] a TMEM accumulator holds a finished K block
+constexpr int kBarTEmpty = 144; // [2] the 8 promotion warps have read it
+constexpr int kTmemSlot = 160;
+constexpr int kAbort = 164;
+constexpr uint32_t kIdesc = idesc_e4m3(kBM, kBN);
+constexpr unsigned long long kDrainNs = 1000000000ull;
+
+struct Params {
+  int64_t m;
+  int32_t n, k;
+  int32_t tiles_m, tiles_n;
+  const float* sx;
+  const float* sw;
+  uint16_t* y;
+  unsigned long long* err;
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_fp8_sm100_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
+                          Params p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint8_t* ctl = smem + kOffCtl;
+  const uint32_t ctl_u = smem_u32(ctl);
+  volatile int* abort = reinterpret_cast<volatile int*>(ctl + kAbort);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if ((smem_u32(smem) & 1023u) != 0) {
+    if (threadIdx.x == 0) hk_flag(p.err, hk::kErrWaitTimeout, 950);
+    return;
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(ctl_u + kBarFull + 8 * s, 1);
+      mbar_init(ctl_u + kBarEmpty + 8 * s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(ctl_u + kBarTFull + 8 * b, 1);
+      mbar_init(ctl_u + kBarTEmpty + 8 * b, 8);
+    }
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) tmem_alloc(ctl_u + kTmemSlot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(ctl + kTmemSlot);
+  const int kblocks = p.k / kBK;
+  const int tiles = p.tiles_m * p.tiles_n;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int g = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
+        const int tm = t % p.tiles_m, tn = t / p.tiles_m;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          const int s = g % kStages, fill = g / kStages;
+          if (fill > 0 && !mbar_wait(ctl_u + kBarEmpty + 8 * s, (fill - 1) & 1, abort, p.err, 951)) {
+            ok = false;
+            break;
+          }
+          const uint32_t dst = smem_u32(smem + s * kStageBytes);
+          mbar_expect_tx(ctl_u + kBarFull + 8 * s, kStageBytes);
+          tma_load_2d(dst, &xmap, ctl_u + kBarFull + 8 * s, kb * kBK, tm * kBM);
+          tma_load_2d(dst + kABytes, &wmap, ctl_u + kBarFull + 8 * s, kb * kBK, tn * kBN);
+          ++g;
+        }
+      }
+      // Let the last fill of every stage land before the CTA can exit.
+      for (int i = g > kStages ? g - kStages : 0; i < g; ++i) {
+        const int s = i % kStages, fill = i / kStages;
+        const unsigned long long t0 = globaltimer();
+        while (!mbar_try_wait(ctl_u + kBarFull + 8 * s, fill & 1) && globaltimer() - t0 < kDrainNs) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int g = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
+        for (int kb = 0; kb < kblocks; ++kb) {
+          const int s = g % kStages, fill = g / kStages, buf = g & 1, use = g >> 1;
+          if (!mbar_wait(ctl_u + kBarFull + 8 * s, fill & 1, abort, p.err, 952) ||
+              (use > 0 && !mbar_wait(ctl_u + kBarTEmpty + 8 * buf, (use - 1) & 1, abort, p.err, 953))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a = smem_u32(smem + s * kStageBytes), b = a + kABytes;
+          const uint32_t d = tmem + (uint32_t)(buf * kBN);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 32; ++kk)
+            umma_f8(d, sdesc_sw128(a + 32 * kk, 16, 1024), sdesc_sw128(b + 32 * kk, 16, 1024), kIdesc,
+                    kk > 0 ? 1u : 0u);
+          umma_commit(ctl_u + kBarEmpty + 8 * s);
+          umma_commit(ctl_u + kBarTFull + 8 * buf);
+          ++g;
+        }
+      }
+      // MMAs complete in order: the last commit landing means none is in flight.
+      if (g > 0) {
+        const int last = g - 1;
+        const unsigned long long t0 = globaltimer();
+        while (!mbar_try_wait(ctl_u + kBarTFull + 8 * (last & 1), (last >> 1) & 1) &&
+               globaltimer() - t0 < kDrainNs) {
+        }
+      }
+    }
+  } else {
+    const int q = warp & 3;              // the TMEM lane quarter this warp may read
+    const int half = (warp - 2) >> 2;    // columns 0..127 or 128..255 of the tile
+    const int row = q * 32 + lane;
+    const int groups = (p.n + 127) / 128;
+    int g = 0;
+    bool live = true;
+    for (int t = blockIdx.x; live && t < tiles; t += gridDim.x) {
+      const int tm = t % p.tiles_m, tn = t / p.tiles_m;
+      const int64_t r = (int64_t)tm * kBM + row;
+      const int grp = tn * (kBN / 128) + half;
+      const bool use = r < p.m && grp < groups;
+      const float* sxr = p.sx + (use ? r * kblocks : 0);
+      const float* swr = p.sw + (use ? (int64_t)grp * kblocks : 0);
+      float acc[128];
+#pragma unroll
+      for (int i = 0; i < 128; ++i) acc[i] = 0.f;
+      float sc_next = use ? sxr[0] * swr[0] : 0.f;
+      for (int kb = 0; kb < kblocks; ++kb) {
+        const int buf = g & 1, u = g >> 1;
+        const float sc = sc_next;
+        if (use && kb + 1 < kblocks) sc_next = sxr[kb + 1] * swr[kb + 1];
+        bool ok = true;
+        if (lane == 0) ok = mbar_wait(ctl_u + kBarTFull + 8 * buf, u & 1, abort, p.err, 954);
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        if (!ok) {
+          live = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * kBN + half * 128);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          float v[16];
+          tmem_ld16(base + 16 * c, v);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) acc[16 * c + i] = fmaf(v[i], sc, acc[16 * c + i]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(ctl_u + kBarTEmpty + 8 * buf);
+        ++g;
+      }
+      if (!live) break;
+      if (r < p.m) {
+        const int col0 = tn * kBN + half * 128;
+        uint16_t* yr = p.y + r * p.n;
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          const int col = col0 + 8 * c;
+          if (col + 8 <= p.n) {
+            uint32_t w[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              w[i] = (uint32_t)f32_to_bf16_bits(acc[8 * c + 2 * i]) |
+                     ((uint32_t)f32_to_bf16_bits(acc[8 * c + 2 * i + 1]) << 16);
+            *reinterpret_cast<uint4*>(yr + col) = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace
 
 namespace hk {
 
-bool gemm_fp8_sm100_supported(int64_t, int32_t, int32_t) { return false; }
+bool gemm_fp8_sm100_supported(int64_t m, int32_t n, int32_t k) {
+  return m >= kBM && m < (1ll << 31) && n >= kBN && n % 16 == 0 && k % kBK == 0 && k >= kBK;
+}
 
-int gemm_fp8_sm100(const uint8_t*, const float*, const uint8_t*, const float*, int64_t, int32_t,
-                   int32_t, uint16_t*, cudaStream_t) {
-  return fail(HK_EINVAL, "gemm_fp8_sm100: not built");
+int gemm_fp8_sm100(const uint8_t* xq, const float* sx, const uint8_t* wq, const float* sw, int64_t m,
+                   int32_t n, int32_t k, uint16_t* y, cudaStream_t stream) {
+  HK_REQUIRE(gemm_fp8_sm100_supported(m, n, k), "gemm_fp8_sm100: shape m %lld n %d k %d", (long long)m, n, k);
+  HK_REQUIRE((uintptr_t)y % 16 == 0, "gemm_fp8_sm100: y must be 16-byte aligned");
+  CUtensorMap xmap, wmap;
+  HK_TRY(sm100::make_map_u8(&xmap, xq, (uint64_t)m, (uint64_t)k, kBM));
+  HK_TRY(sm100::make_map_u8(&wmap, wq, (uint64_t)n, (uint64_t)k, kBN));
+  static bool attr = false;
+  if (!attr) {
+    HK_TRY_CUDA(cudaFuncSetAttribute(gemm_fp8_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kSmemBytes));
+    attr = true;
+  }
+  Params p;
+  p.m = m;
+  p.n = n;
+  p.k = k;
+  p.tiles_m = (int32_t)((m + kBM - 1) / kBM);
+  p.tiles_n = (n + kBN - 1) / kBN;
+  p.sx = sx;
+  p.sw = sw;
+  p.y = y;
+  p.err = err_word();
+  const int64_t tiles = (int64_t)p.tiles_m * p.tiles_n;
+  HK_REQUIRE(tiles < (1ll << 31), "gemm_fp8_sm100: too many tiles");
+  const int grid = (int)std::min<int64_t>(tiles, sm_count());
+  gemm_fp8_sm100_kernel<<<grid, kThreads, kSmemBytes, stream>>>(xmap, wmap, p);
+  HK_TRY_LAUNCH("gemm_fp8_sm100_kernel");
+  return HK_OK;
 }
 
 }  // namespace hk
