@@ -56,20 +56,32 @@ namespace {
 
 using namespace hk::sm100;
 
-constexpr int kBM = 128, kBN = 256, kBK = 128;
-constexpr int kStages = 4;
+// Tile width (weight rows) and the TMEM columns read per wait in the promotion loop.
+#ifndef HK_GEMM_BN
+#define HK_GEMM_BN 256
+#endif
+#ifndef HK_GEMM_LDC
+#define HK_GEMM_LDC 16
+#endif
+constexpr int kBM = 128, kBN = HK_GEMM_BN, kBK = 128;
+constexpr int kLdCols = HK_GEMM_LDC;
+constexpr int kEpiWarps = 4 * (kBN / 128);          // one warp per lane quarter and 128 columns
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kABytes = kBM * kBK;                  // 16 KB
-constexpr int kBBytes = kBN * kBK;                  // 32 KB
-constexpr int kStageBytes = kABytes + kBBytes;      // 48 KB
-constexpr int kOffCtl = kStages * kStageBytes;      // 192 KB
+constexpr int kBBytes = kBN * kBK;                  // 16 or 32 KB
+constexpr int kStageBytes = kABytes + kBBytes;
+constexpr int kStages = 196608 / kStageBytes < 8 ? 196608 / kStageBytes : 8;
+constexpr int kOffCtl = kStages * kStageBytes;
 constexpr int kSmemBytes = kOffCtl + 1024;
-constexpr int kThreads = 320;
+constexpr uint32_t kTmemCols = 2 * kBN;
+static_assert(kBN == 128 || kBN == 256, "tile width");
+static_assert(kLdCols == 16 || kLdCols == 32 || kLdCols == 64, "TMEM load width");
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 constexpr int kBarFull = 0;     // [kStages] TMA bytes of a stage landed
 constexpr int kBarEmpty = 64;   // [kStages] the stage's MMAs completed
 constexpr int kBarTFull = 128;  // [2] a TMEM accumulator holds a finished K block
-constexpr int kBarTEmpty = 144; // [2] the 8 promotion warps have read it
+constexpr int kBarTEmpty = 144; // [2] every promotion warp has read it
 constexpr int kTmemSlot = 160;
 constexpr int kAbort = 164;
 constexpr uint32_t kIdesc = idesc_e4m3(kBM, kBN);
@@ -104,12 +116,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(ctl_u + kBarTFull + 8 * b, 1);
-      mbar_init(ctl_u + kBarTEmpty + 8 * b, 8);
+      mbar_init(ctl_u + kBarTEmpty + 8 * b, kEpiWarps);
     }
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 1) tmem_alloc(ctl_u + kTmemSlot, 512);
+  if (warp == 1) tmem_alloc(ctl_u + kTmemSlot, kTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -209,11 +221,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * kBN + half * 128);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          float v[16];
-          tmem_ld16(base + 16 * c, v);
+        for (int c = 0; c < 128 / kLdCols; ++c) {
+          float v[kLdCols];
+          if constexpr (kLdCols == 16) tmem_ld16(base + 16 * c, v);
+          if constexpr (kLdCols == 32) tmem_ld32(base + 32 * c, v);
+          if constexpr (kLdCols == 64) tmem_ld64(base + 64 * c, v);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) acc[16 * c + i] = fmaf(v[i], sc, acc[16 * c + i]);
+          for (int i = 0; i < kLdCols; ++i) acc[kLdCols * c + i] = fmaf(v[i], sc, acc[kLdCols * c + i]);
         }
         tc_fence_before();
         __syncwarp();
@@ -243,7 +257,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc(tmem, kTmemCols);
   }
 }
 
