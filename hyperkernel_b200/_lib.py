@@ -44,7 +44,7 @@ SIGNATURES = {
     "hk_gemm_fp8": (C.c_int, [P, P, P, P, I64, I32, I32, P, P]),
     "hk_route": (C.c_int, [P, P, I32, I32, I32, F32, P, P, P]),
     "hk_permute": (C.c_int, [P, P, I32, I32, I32, P, P, P, P, P]),
-    "hk_moe_workspace_size": (SZ, [I64, I32]),
+    "hk_moe_workspace_size": (SZ, [I64, I32, I32]),
     "hk_moe_grouped": (C.c_int, [P, P, I32, P, P, I64, I32, I32, I32, P, P, P, P, P, P, SZ, P]),
     "hk_moe_grouped_noalloc": (C.c_int, [P, P, I32, P, P, I64, I32, I32, I32, P, P, P, P, P, P]),
     "hk_combine": (C.c_int, [P, I64, P, P, P, I32, I32, I32, P, P]),
@@ -306,8 +306,8 @@ def permute(ids, weights, num_experts, stream=None):
     return offsets, perm_token, perm_weight, inv
 
 
-def moe_workspace_size(rows, inter) -> int:
-    return lib().hk_moe_workspace_size(rows, inter)
+def moe_workspace_size(rows, hidden, inter) -> int:
+    return lib().hk_moe_workspace_size(rows, hidden, inter)
 
 
 def moe_grouped(xq, sx, offsets, perm_token, rows, hidden, inter, w13, s13, w2, s2, out=None,
@@ -317,7 +317,7 @@ def moe_grouped(xq, sx, offsets, perm_token, rows, hidden, inter, w13, s13, w2, 
     if out is None:
         out = torch.empty((max(rows, 1), hidden), dtype=torch.bfloat16, device=dev)
     if workspace is None:
-        workspace = torch.empty(moe_workspace_size(max(rows, 1), inter), dtype=torch.uint8, device=dev)
+        workspace = torch.empty(moe_workspace_size(max(rows, 1), hidden, inter), dtype=torch.uint8, device=dev)
     call("hk_moe_grouped", ptr(xq), ptr(sx), xq.shape[0], ptr(offsets), ptr(perm_token), rows, E,
          hidden, inter, ptr(w13), ptr(s13), ptr(w2), ptr(s2), ptr(out), ptr(workspace),
          workspace.numel(), stream_ptr(stream))

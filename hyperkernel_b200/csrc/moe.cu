@@ -415,9 +415,18 @@ size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 }  // namespace
 
-extern "C" size_t hk_moe_workspace_size(int64_t rows, int32_t inter);
-
 namespace hk {
+
+size_t moe_portable_workspace(int64_t rows, int32_t inter) {
+  const int64_t max_tiles = rows / kTileRows + kMaxExperts + 1;
+  return align256((size_t)rows * inter) + align256((size_t)rows * (inter / 128) * sizeof(float)) +
+         align256((size_t)max_tiles * 2 * sizeof(int32_t) + sizeof(int32_t));
+}
+
+size_t moe_full_workspace(int64_t rows, int32_t hidden, int32_t inter) {
+  return moe_portable_workspace(rows, inter) + align256((size_t)rows * hidden) +
+         align256((size_t)rows * (hidden / 128) * sizeof(float));
+}
 
 // The grouped FFN launcher behind hk_moe_grouped: `err` is the device error word the kernels
 // record bad rows in (nullptr: skipped without a record).
@@ -425,7 +434,7 @@ int moe_grouped_run(const uint8_t* xq, const float* sx, int32_t tokens, const in
                     const int32_t* perm_token, int64_t rows, int32_t num_experts, int32_t hidden,
                     int32_t inter, const uint8_t* w13, const float* s13, const uint8_t* w2,
                     const float* s2, uint16_t* y, void* workspace, size_t workspace_bytes,
-                    unsigned long long* err, cudaStream_t s) {
+                    bool portable_only, unsigned long long* err, cudaStream_t s) {
   HK_TRY(hk::ensure_device());
   HK_REQUIRE(xq && sx && offsets && perm_token && w13 && s13 && w2 && s2 && y,
              "hk_moe_grouped: null pointer");
@@ -436,29 +445,35 @@ int moe_grouped_run(const uint8_t* xq, const float* sx, int32_t tokens, const in
              "hk_moe_grouped: operands must be 16-byte aligned");
   HK_REQUIRE(tokens >= 0 && rows >= 0, "hk_moe_grouped: negative sizes");
   if (rows == 0) return HK_OK;
-  const size_t need = hk_moe_workspace_size(rows, inter);
+  const bool tc = !portable_only && moe_sm100_supported(num_experts, hidden, inter) && rows < (1ll << 31);
+  const size_t need = tc ? moe_full_workspace(rows, hidden, inter) : moe_portable_workspace(rows, inter);
   if (workspace == nullptr || workspace_bytes < need)
     return fail(HK_ESPACE, "hk_moe_grouped: workspace of %zu bytes, %zu needed", workspace_bytes, need);
-  const int64_t rows_cap = rows;
+  HK_REQUIRE((uintptr_t)workspace % 256 == 0, "hk_moe_grouped: workspace must be 256-byte aligned");
   uint8_t* base = reinterpret_cast<uint8_t*>(workspace);
-  uint8_t* hq = base;
-  float* hs = reinterpret_cast<float*>(base + align256((size_t)rows_cap * inter));
-  int32_t* tiles = reinterpret_cast<int32_t*>(
-      reinterpret_cast<uint8_t*>(hs) + align256((size_t)rows_cap * (inter / 128) * sizeof(float)));
-  const int32_t max_tiles = (int32_t)(rows_cap / kTileRows + kMaxExperts + 1);
-  int32_t* tile_expert = tiles;
-  int32_t* tile_row = tiles + max_tiles;
-  int32_t* num_tiles = tiles + 2 * max_tiles;
-  tile_list_kernel<<<1, 32, 0, s>>>(offsets, num_experts, rows, max_tiles, tile_expert, tile_row,
-                                    num_tiles, err);
+  MoeScratch ws{};
+  ws.hq = base;
+  ws.hs = reinterpret_cast<float*>(base + align256((size_t)rows * inter));
+  int32_t* tiles = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(ws.hs) +
+                                              align256((size_t)rows * (inter / 128) * sizeof(float)));
+  ws.max_tiles = (int32_t)(rows / kTileRows + kMaxExperts + 1);
+  ws.tile_expert = tiles;
+  ws.tile_row = tiles + ws.max_tiles;
+  ws.num_tiles = tiles + 2 * ws.max_tiles;
+  ws.xp = base + moe_portable_workspace(rows, inter);
+  ws.sxp = reinterpret_cast<float*>(ws.xp + align256((size_t)rows * hidden));
+  tile_list_kernel<<<1, 32, 0, s>>>(offsets, num_experts, rows, ws.max_tiles, ws.tile_expert, ws.tile_row,
+                                    ws.num_tiles, err);
   HK_TRY_LAUNCH("tile_list_kernel");
-  const int32_t tokens_limit = tokens;
-  moe_up_kernel<<<dim3(max_tiles, inter / 128), 256, 0, s>>>(
-      xq, sx, offsets, perm_token, tile_expert, tile_row, num_tiles, hidden, inter, tokens_limit,
-      w13, s13, hq, hs, err);
+  if (tc)
+    return moe_sm100_run(xq, sx, tokens, offsets, perm_token, rows, num_experts, hidden, inter, w13, s13, w2,
+                         s2, y, ws, err, s);
+  moe_up_kernel<<<dim3(ws.max_tiles, inter / 128), 256, 0, s>>>(
+      xq, sx, offsets, perm_token, ws.tile_expert, ws.tile_row, ws.num_tiles, hidden, inter, tokens, w13, s13,
+      ws.hq, ws.hs, err);
   HK_TRY_LAUNCH("moe_up_kernel");
-  moe_down_kernel<<<dim3(max_tiles, hidden / 64), 256, 0, s>>>(
-      hq, hs, offsets, tile_expert, tile_row, num_tiles, hidden, inter, w2, s2, y);
+  moe_down_kernel<<<dim3(ws.max_tiles, hidden / 64), 256, 0, s>>>(
+      ws.hq, ws.hs, offsets, ws.tile_expert, ws.tile_row, ws.num_tiles, hidden, inter, w2, s2, y);
   HK_TRY_LAUNCH("moe_down_kernel");
   return HK_OK;
 }
@@ -497,10 +512,9 @@ int hk_permute(const int32_t* ids, const float* weights, int32_t tokens, int32_t
   return HK_OK;
 }
 
-size_t hk_moe_workspace_size(int64_t rows, int32_t inter) {
-  const int64_t max_tiles = rows / kTileRows + kMaxExperts + 1;
-  return align256((size_t)rows * inter) + align256((size_t)rows * (inter / 128) * sizeof(float)) +
-         align256((size_t)max_tiles * 2 * sizeof(int32_t) + sizeof(int32_t));
+size_t hk_moe_workspace_size(int64_t rows, int32_t hidden, int32_t inter) {
+  if (rows <= 0 || hidden <= 0 || inter <= 0) return 0;
+  return hk::moe_full_workspace(rows, hidden, inter);
 }
 
 int hk_moe_grouped(const uint8_t* xq, const float* sx, int32_t tokens, const int32_t* offsets,
@@ -509,7 +523,7 @@ int hk_moe_grouped(const uint8_t* xq, const float* sx, int32_t tokens, const int
                    const float* s2, uint16_t* y, void* workspace, size_t workspace_bytes,
                    void* stream) {
   return hk::moe_grouped_run(xq, sx, tokens, offsets, perm_token, rows, num_experts, hidden, inter,
-                             w13, s13, w2, s2, y, workspace, workspace_bytes, hk::err_word(),
+                             w13, s13, w2, s2, y, workspace, workspace_bytes, false, hk::err_word(),
                              (cudaStream_t)stream);
 }
 

@@ -34,7 +34,8 @@ constexpr int64_t kMaxRows = 1024;
 constexpr int32_t kMaxInter = 2048;
 constexpr int kMaxExperts = 512;  // hk_moe_grouped's expert limit (tile list capacity)
 constexpr size_t al256(size_t x) { return (x + 255) & ~(size_t)255; }
-// The same arithmetic as hk_moe_workspace_size(kMaxRows, kMaxInter).
+// The same arithmetic as hk::moe_portable_workspace(kMaxRows, kMaxInter): the scratch of the
+// CUDA-core expert kernels, which this entry point runs.
 constexpr size_t kScratchBytes =
     al256((size_t)kMaxRows * kMaxInter) + al256((size_t)kMaxRows * (kMaxInter / 128) * 4) +
     al256((size_t)(kMaxRows / 64 + kMaxExperts + 1) * 2 * 4 + 4);
@@ -76,11 +77,11 @@ extern "C" int hk_moe_grouped_noalloc(const uint8_t* xq, const float* sx, int32_
              (long long)rows, (long long)kMaxRows);
   HK_REQUIRE(inter > 0 && inter <= kMaxInter,
              "hk_moe_grouped_noalloc: inter %d, at most %d (use hk_moe_grouped)", inter, kMaxInter);
-  HK_REQUIRE(hk_moe_workspace_size(rows, inter) <= kScratchBytes,
+  HK_REQUIRE(hk::moe_portable_workspace(rows, inter) <= kScratchBytes,
              "hk_moe_grouped_noalloc: scratch of %zu bytes too small", kScratchBytes);
   void* scratch = nullptr;
   HK_TRY(scratch_of_device(&scratch));
   return hk::moe_grouped_run(xq, sx, tokens, offsets, perm_token, rows, num_experts, hidden, inter,
-                             w13, s13, w2, s2, y, scratch, kScratchBytes, nullptr,
+                             w13, s13, w2, s2, y, scratch, kScratchBytes, true, nullptr,
                              (cudaStream_t)stream);
 }

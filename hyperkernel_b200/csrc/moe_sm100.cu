@@ -1,0 +1,382 @@
+// a14 on the tensor cores: the grouped FP8 expert FFN in swap-AB form.
+//
+// Decode-sized MoE gives each expert a handful of rows (config 4: ~16 of 4096 permuted rows
+// per expert), so the expert weights are the large operand and the kernel is HBM-bound on
+// them.  Weights therefore take the MMA's M side (128 weight rows, one 128x128 scale block)
+// and the expert's rows the N side (a tile of up to 64 rows), and each work unit streams one
+// 128-row block of one expert's weights exactly once per row tile.
+//
+//  gather   xp[p] = xq[perm_token[p]], sxp[p] = sx[perm_token[p]]: the routed rows laid out
+//           contiguously in permuted order, so TMA can load a row tile (out-of-range
+//           indices are recorded and give a zero row).
+//  up       unit = (row tile, 128-column block nb of h): D_g = Wg[nb] . X^T and
+//           D_u = Wu[nb] . X^T per 128-wide K block (tcgen05 kind::f8f6f4, M 128, N 64) into
+//           double-buffered TMEM; promotion warps add partial * sw * sx[row] in registers;
+//           at the end h = silu(g) * u is requantised to e4m3 with one scale per (row, nb)
+//           (amax over the block's 128 columns across the four warps).
+//  down     unit = (row tile, 128-column block of y): D = W2[nb] . hq^T over inter, promoted
+//           with sw * hs[row], stored as bf16.
+// Roles per CTA (6 warps): warp 0 TMA, warp 1 MMA and TMEM owner, warps 2..5 promotion (one
+// per TMEM lane quarter; thread = weight row).  Persistent over the units of the device-built
+// tile list; every wait bounded (1 s) with the error word, in-flight copies and MMAs drained
+// before exit.
+#include <cuda.h>
+#include <math.h>
+
+#include "common.cuh"
+#include "moe.cuh"
+#include "sm100.cuh"
+
+namespace {
+
+using namespace hk::sm100;
+
+constexpr int kRowsTile = 64;   // rows (tokens) per unit: the MMA's N
+constexpr int kWRows = 128;     // weight rows per unit: the MMA's M
+constexpr int kBK = 128;
+constexpr int kThreads = 192;
+constexpr int kWBytes = kWRows * kBK;      // 16 KB
+constexpr int kXBytes = kRowsTile * kBK;   // 8 KB
+constexpr uint32_t kIdesc = idesc_e4m3(kWRows, kRowsTile);
+constexpr unsigned long long kDrainNs = 1000000000ull;
+
+// Control block offsets (after the ring and the scale table).
+constexpr int kBarFull = 0;      // [8]
+constexpr int kBarEmpty = 64;    // [8]
+constexpr int kBarTFull = 128;   // [2]
+constexpr int kBarTEmpty = 144;  // [2]
+constexpr int kTmemSlot = 160;
+constexpr int kAbort = 164;
+constexpr int kRed = 256;        // [4][64] floats: per-warp column amax (up epilogue)
+constexpr int kCtlBytes = kRed + 4 * kRowsTile * 4;
+
+template <bool kUp>
+struct Cfg {
+  static constexpr int kStageBytes = (kUp ? 2 : 1) * kWBytes + kXBytes;
+  static constexpr int kMaxKb = kUp ? 64 : 32;  // scale-table capacity in K blocks
+  static constexpr int kStages = kUp ? 5 : 8;
+  static constexpr int kOffScales = kStages * kStageBytes;
+  static constexpr int kOffCtl = kOffScales + kMaxKb * kRowsTile * 4;
+  static constexpr int kSmem = kOffCtl + kCtlBytes;
+  static constexpr uint32_t kTmemCols = kUp ? 256 : 128;
+  static_assert(kSmem <= 232448, "shared memory budget");
+};
+
+struct Params {
+  const int32_t* offsets;
+  const int32_t* tile_expert;
+  const int32_t* tile_row;
+  const int32_t* num_tiles;
+  int32_t hidden, inter, num_experts;
+  int64_t rows;
+  const float* act_scale;  // up: sxp [rows][hidden/128]; down: hs [rows][inter/128]
+  const float* w_scale;    // up: s13; down: s2
+  uint8_t* hq;             // up output
+  float* hs;               // up output
+  uint16_t* y;             // down output
+  unsigned long long* err;
+};
+
+__global__ void gather_rows_kernel(const uint8_t* __restrict__ xq, const float* __restrict__ sx,
+                                   const int32_t* __restrict__ perm_token, int64_t rows, int32_t tokens,
+                                   int32_t hidden, uint8_t* __restrict__ xp, float* __restrict__ sxp,
+                                   unsigned long long* err) {
+  const int64_t p = blockIdx.x;
+  if (p >= rows) return;
+  const int32_t src = perm_token[p];
+  const bool ok = src >= 0 && src < tokens;
+  if (!ok && threadIdx.x == 0) hk_flag(err, hk::kErrMoeRow, (unsigned)p);
+  const int vecs = hidden / 16;
+  const uint4* s = reinterpret_cast<const uint4*>(xq + (int64_t)(ok ? src : 0) * hidden);
+  uint4* d = reinterpret_cast<uint4*>(xp + p * hidden);
+  for (int i = threadIdx.x; i < vecs; i += blockDim.x) d[i] = ok ? s[i] : make_uint4(0, 0, 0, 0);
+  const int kb = hidden / 128;
+  for (int i = threadIdx.x; i < kb; i += blockDim.x) sxp[p * kb + i] = ok ? sx[(int64_t)src * kb + i] : 0.f;
+}
+
+// Named barrier `id` over `count` threads that also ANDs a predicate across them.
+__device__ __forceinline__ bool bar_and(int id, int count, bool v) {
+  int out;
+  asm volatile(
+      "{\n.reg .pred p, q;\nsetp.ne.b32 p, %1, 0;\nbar.red.and.pred q, %2, %3, p;\nselp.s32 %0, 1, 0, q;\n}"
+      : "=r"(out)
+      : "r"((int)v), "r"(id), "r"(count)
+      : "memory");
+  return out != 0;
+}
+
+template <bool kUp>
+__global__ void __launch_bounds__(kThreads, 1)
+    moe_sm100_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap, Params p) {
+  using C = Cfg<kUp>;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint8_t* ctl = smem + C::kOffCtl;
+  float* scales = reinterpret_cast<float*>(smem + C::kOffScales);  // [kb][64]
+  const uint32_t ctl_u = smem_u32(ctl);
+  volatile int* abort = reinterpret_cast<volatile int*>(ctl + kAbort);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if ((smem_u32(smem) & 1023u) != 0) {
+    if (threadIdx.x == 0) hk_flag(p.err, hk::kErrWaitTimeout, 960);
+    return;
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(ctl_u + kBarFull + 8 * s, 1);
+      mbar_init(ctl_u + kBarEmpty + 8 * s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(ctl_u + kBarTFull + 8 * b, 1);
+      mbar_init(ctl_u + kBarTEmpty + 8 * b, 4);
+    }
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) tmem_alloc(ctl_u + kTmemSlot, C::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(ctl + kTmemSlot);
+
+  // up: K = hidden, units per tile = inter / 128; down: K = inter, units per tile = hidden / 128
+  const int kblocks = (kUp ? p.hidden : p.inter) / kBK;
+  const int nblocks = (kUp ? p.inter : p.hidden) / 128;
+  const int units = *p.num_tiles * nblocks;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int g = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
+        const int tile = u / nblocks, nb = u % nblocks;
+        const int e = p.tile_expert[tile], r0 = p.tile_row[tile];
+        // weight rows of this unit (gate block, and up block inter rows later)
+        const int wrow = kUp ? e * 2 * p.inter + nb * 128 : e * p.hidden + nb * 128;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          const int s = g % C::kStages, fill = g / C::kStages;
+          if (fill > 0 && !mbar_wait(ctl_u + kBarEmpty + 8 * s, (fill - 1) & 1, abort, p.err, 961)) {
+            ok = false;
+            break;
+          }
+          const uint32_t dst = smem_u32(smem + s * C::kStageBytes);
+          const uint32_t full = ctl_u + kBarFull + 8 * s;
+          mbar_expect_tx(full, C::kStageBytes);
+          tma_load_2d(dst, &wmap, full, kb * kBK, wrow);
+          if (kUp) tma_load_2d(dst + kWBytes, &wmap, full, kb * kBK, wrow + p.inter);
+          tma_load_2d(dst + (kUp ? 2 : 1) * kWBytes, &xmap, full, kb * kBK, r0);
+          ++g;
+        }
+      }
+      for (int i = g > C::kStages ? g - C::kStages : 0; i < g; ++i) {
+        const int s = i % C::kStages, fill = i / C::kStages;
+        const unsigned long long t0 = globaltimer();
+        while (!mbar_try_wait(ctl_u + kBarFull + 8 * s, fill & 1) && globaltimer() - t0 < kDrainNs) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int g = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
+        for (int kb = 0; kb < kblocks; ++kb) {
+          const int s = g % C::kStages, fill = g / C::kStages, buf = g & 1, use = g >> 1;
+          if (!mbar_wait(ctl_u + kBarFull + 8 * s, fill & 1, abort, p.err, 962) ||
+              (use > 0 && !mbar_wait(ctl_u + kBarTEmpty + 8 * buf, (use - 1) & 1, abort, p.err, 963))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a = smem_u32(smem + s * C::kStageBytes);
+          const uint32_t x = a + (kUp ? 2 : 1) * kWBytes;
+          const uint32_t d = tmem + (uint32_t)(buf * (kUp ? 128 : 64));
+#pragma unroll
+          for (int kk = 0; kk < kBK / 32; ++kk) {
+            const uint64_t bdesc = sdesc_sw128(x + 32 * kk, 16, 1024);
+            umma_f8(d, sdesc_sw128(a + 32 * kk, 16, 1024), bdesc, kIdesc, kk > 0 ? 1u : 0u);
+            if (kUp) umma_f8(d + 64, sdesc_sw128(a + kWBytes + 32 * kk, 16, 1024), bdesc, kIdesc, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(ctl_u + kBarEmpty + 8 * s);
+          umma_commit(ctl_u + kBarTFull + 8 * buf);
+          ++g;
+        }
+      }
+      if (g > 0) {
+        const int last = g - 1;
+        const unsigned long long t0 = globaltimer();
+        while (!mbar_try_wait(ctl_u + kBarTFull + 8 * (last & 1), (last >> 1) & 1) &&
+               globaltimer() - t0 < kDrainNs) {
+        }
+      }
+    }
+  } else {
+    const int q = warp & 3;           // TMEM lane quarter
+    const int m = q * 32 + lane;      // weight row inside the unit's 128-row block
+    const int et = threadIdx.x - 64;  // 0..127 among the promotion threads
+    float* red = reinterpret_cast<float*>(ctl + kRed);
+    int g = 0;
+    bool live = true;
+    for (int u = blockIdx.x; live && u < units; u += gridDim.x) {
+      const int tile = u / nblocks, nb = u % nblocks;
+      const int e = p.tile_expert[tile], r0 = p.tile_row[tile];
+      const int count = min(kRowsTile, p.offsets[e + 1] - r0);
+      // Per-row activation scales of the tile for every K block: scales[kb][n].
+      asm volatile("bar.sync 1, 128;" ::: "memory");  // the previous unit is done reading them
+      for (int i = et; i < kblocks * kRowsTile; i += 128) {
+        const int n = i % kRowsTile, kb = i / kRowsTile;
+        scales[kb * kRowsTile + n] = n < count ? p.act_scale[(int64_t)(r0 + n) * kblocks + kb] : 0.f;
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      const float* wsc = kUp ? p.w_scale + ((int64_t)e * (2 * p.inter / 128) + nb) * kblocks
+                             : p.w_scale + ((int64_t)e * (p.hidden / 128) + nb) * kblocks;
+      const float* wsu = kUp ? wsc + (int64_t)(p.inter / 128) * kblocks : wsc;
+      float acc_g[kRowsTile], acc_u[kUp ? kRowsTile : 1];
+#pragma unroll
+      for (int i = 0; i < kRowsTile; ++i) acc_g[i] = 0.f;
+#pragma unroll
+      for (int i = 0; i < (kUp ? kRowsTile : 1); ++i) acc_u[i] = 0.f;
+      // A warp whose wait fails stops waiting but stays in step, so the four promotion warps
+      // always meet at the named barriers and leave the unit loop together.
+      for (int kb = 0; kb < kblocks; ++kb, ++g) {
+        if (!live) continue;
+        const int buf = g & 1, use = g >> 1;
+        const float sg = wsc[kb];
+        const float su = kUp ? wsu[kb] : 0.f;
+        bool ok = true;
+        if (lane == 0) ok = mbar_wait(ctl_u + kBarTFull + 8 * buf, use & 1, abort, p.err, 964);
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        if (!ok) {
+          live = false;
+          continue;
+        }
+        tc_fence_after();
+        const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * (kUp ? 128 : 64));
+        const float4* sc4 = reinterpret_cast<const float4*>(scales + kb * kRowsTile);
+#pragma unroll
+        for (int c = 0; c < kRowsTile / 16; ++c) {
+          float v[16];
+          tmem_ld16(base + 16 * c, v);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float4 s4 = sc4[4 * c + j];
+            const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              acc_g[16 * c + 4 * j + i] = fmaf(v[4 * j + i], sv[i] * sg, acc_g[16 * c + 4 * j + i]);
+          }
+          if constexpr (kUp) {
+            tmem_ld16(base + 64 + 16 * c, v);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float4 s4 = sc4[4 * c + j];
+              const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                acc_u[16 * c + 4 * j + i] = fmaf(v[4 * j + i], sv[i] * su, acc_u[16 * c + 4 * j + i]);
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(ctl_u + kBarTEmpty + 8 * buf);
+      }
+      if (!bar_and(1, 128, live)) break;
+      if constexpr (kUp) {
+        // h = silu(g) * u, then one e4m3 scale per (row, nb) from the amax over this block's
+        // 128 columns (the 128 promotion threads).
+#pragma unroll
+        for (int n = 0; n < kRowsTile; ++n) {
+          const float gv = acc_g[n];
+          acc_g[n] = gv / (1.f + expf(-gv)) * acc_u[n];
+          float a = fabsf(acc_g[n]);
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+          if (lane == 0) red[q * kRowsTile + n] = a;
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        const int inter_blocks = p.inter / 128;
+#pragma unroll
+        for (int n = 0; n < kRowsTile; ++n) {
+          if (n < count) {
+            const float amax =
+                fmaxf(fmaxf(red[n], red[kRowsTile + n]), fmaxf(red[2 * kRowsTile + n], red[3 * kRowsTile + n]));
+            const float s = __fdiv_rn(fmaxf(amax, 1e-12f), 448.0f);
+            const int64_t row = r0 + n;
+            p.hq[row * p.inter + nb * 128 + m] = f32_to_e4m3(__fdiv_rn(acc_g[n], s));
+            if (m == 0) p.hs[row * inter_blocks + nb] = s;
+          }
+        }
+      } else {
+#pragma unroll
+        for (int n = 0; n < kRowsTile; ++n)
+          if (n < count) p.y[(int64_t)(r0 + n) * p.hidden + nb * 128 + m] = f32_to_bf16_bits(acc_g[n]);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::kTmemCols);
+  }
+}
+
+template <bool kUp>
+int launch(const CUtensorMap& wmap, const CUtensorMap& xmap, const Params& p, int grid, cudaStream_t s) {
+  static bool attr = false;
+  if (!attr) {
+    HK_TRY_CUDA(cudaFuncSetAttribute(moe_sm100_kernel<kUp>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     Cfg<kUp>::kSmem));
+    attr = true;
+  }
+  moe_sm100_kernel<kUp><<<grid, kThreads, Cfg<kUp>::kSmem, s>>>(wmap, xmap, p);
+  HK_TRY_LAUNCH(kUp ? "moe_sm100_kernel<up>" : "moe_sm100_kernel<down>");
+  return HK_OK;
+}
+
+}  // namespace
+
+namespace hk {
+
+bool moe_sm100_supported(int32_t num_experts, int32_t hidden, int32_t inter) {
+  return hidden % 128 == 0 && inter % 128 == 0 && hidden / 128 <= Cfg<true>::kMaxKb &&
+         inter / 128 <= Cfg<false>::kMaxKb && (int64_t)num_experts * 2 * inter < (1ll << 31) &&
+         (int64_t)num_experts * hidden < (1ll << 31);
+}
+
+int moe_sm100_run(const uint8_t* xq, const float* sx, int32_t tokens, const int32_t* offsets,
+                  const int32_t* perm_token, int64_t rows, int32_t num_experts, int32_t hidden, int32_t inter,
+                  const uint8_t* w13, const float* s13, const uint8_t* w2, const float* s2, uint16_t* y,
+                  const MoeScratch& ws, unsigned long long* err, cudaStream_t s) {
+  HK_REQUIRE(moe_sm100_supported(num_experts, hidden, inter), "moe_sm100: hidden %d inter %d", hidden, inter);
+  HK_REQUIRE(rows < (1ll << 31), "moe_sm100: %lld rows", (long long)rows);
+  gather_rows_kernel<<<(unsigned)rows, 128, 0, s>>>(xq, sx, perm_token, rows, tokens, hidden, ws.xp, ws.sxp, err);
+  HK_TRY_LAUNCH("gather_rows_kernel");
+  CUtensorMap w13map, xmap, w2map, hmap;
+  HK_TRY(sm100::make_map_u8(&w13map, w13, (uint64_t)num_experts * 2 * inter, (uint64_t)hidden, kWRows));
+  HK_TRY(sm100::make_map_u8(&xmap, ws.xp, (uint64_t)rows, (uint64_t)hidden, kRowsTile));
+  HK_TRY(sm100::make_map_u8(&w2map, w2, (uint64_t)num_experts * hidden, (uint64_t)inter, kWRows));
+  HK_TRY(sm100::make_map_u8(&hmap, ws.hq, (uint64_t)rows, (uint64_t)inter, kRowsTile));
+  Params p{};
+  p.offsets = offsets;
+  p.tile_expert = ws.tile_expert;
+  p.tile_row = ws.tile_row;
+  p.num_tiles = ws.num_tiles;
+  p.hidden = hidden;
+  p.inter = inter;
+  p.num_experts = num_experts;
+  p.rows = rows;
+  p.err = err;
+  const int grid = sm_count();
+  p.act_scale = ws.sxp;
+  p.w_scale = s13;
+  p.hq = ws.hq;
+  p.hs = ws.hs;
+  HK_TRY(launch<true>(w13map, xmap, p, grid, s));
+  p.act_scale = ws.hs;
+  p.w_scale = s2;
+  p.y = y;
+  HK_TRY(launch<false>(w2map, hmap, p, grid, s));
+  return HK_OK;
+}
+
+}  // namespace hk

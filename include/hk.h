@@ -201,8 +201,10 @@ int hk_permute(const int32_t* ids, const float* weights, int32_t tokens, int32_t
  * y[p] = h Wd^T (w2[e][hidden][inter]), all weights e4m3 with 128x128 fp32 block scales
  * (s13[e][2*inter/128][hidden/128], s2[e][hidden/128][inter/128]); h is re-quantised to
  * e4m3 1x128 blocks before the down projection.  y[P][hidden] bf16.
- * `workspace` holds h: see hk_moe_workspace_size. */
-size_t hk_moe_workspace_size(int64_t rows, int32_t inter);
+ * On sm_100 the expert GEMMs run on the tensor cores (weights on the MMA's M side, up to 64
+ * routed rows of an expert on N).  `workspace` (256-byte aligned, hk_moe_workspace_size
+ * bytes) holds h, its scales, the tile list and the routed rows gathered in permuted order. */
+size_t hk_moe_workspace_size(int64_t rows, int32_t hidden, int32_t inter);
 int hk_moe_grouped(const uint8_t* xq, const float* sx, int32_t tokens, const int32_t* offsets,
                    const int32_t* perm_token, int64_t rows, int32_t num_experts, int32_t hidden,
                    int32_t inter, const uint8_t* w13, const float* s13, const uint8_t* w2,
@@ -215,7 +217,8 @@ int hk_moe_grouped(const uint8_t* xq, const float* sx, int32_t tokens, const int
  * device-wide synchronisation).  No counterpart in the reference.  Its scratch is a fixed
  * 2,167,040-byte device array that every GPU loading this library holds until exit: at most
  * 1024 permuted rows and inter <= 2048, larger problems are refused with HK_EINVAL.  It
- * allocates nothing.  All calls share the array: calls that overlap on the GPU race and must
+ * allocates nothing and runs the CUDA-core expert kernels (the scratch has no room for the
+ * gathered rows the tensor-core kernels read).  All calls share the array: calls that overlap on the GPU race and must
  * be serialised.  The first call on a device looks the array up (cudaGetSymbolAddress) and
  * should come before any stream capture.  Out-of-range rows are skipped but not recorded in
  * the device error word. */

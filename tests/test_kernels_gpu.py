@@ -362,8 +362,9 @@ def _moe_case(tokens, experts, hidden, inter, top_k, seed):
     return inp
 
 
-def test_moe_layer_matches_oracle(hk, orc, cuda):
-    T, E, H, I, K = 96, 8, 256, 256, 2
+@pytest.mark.parametrize("T,E,H,I,K", [(96, 8, 256, 256, 2), (200, 4, 384, 256, 2), (128, 32, 1024, 512, 8)])
+def test_moe_layer_matches_oracle(hk, orc, cuda, T, E, H, I, K):
+    """Routed rows per expert: ~24 (one row tile), ~100 (two tiles) and ~32 with top-8."""
     inp = _moe_case(T, E, H, I, K, seed=52)
     ids, w = orc.route(inp["logits"], None, K, 1.0)
     off, tok, pw, inv = orc.permute(ids, w, E)
