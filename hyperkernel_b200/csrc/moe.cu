@@ -159,31 +159,46 @@ __global__ void __launch_bounds__(kPermThreads) permute_kernel(
   }
 }
 
-// Builds the list of (expert, first row) tiles of kTileRows rows.
+// Builds the list of (expert, first row) tiles of kTileRows rows.  One warp: lanes take
+// experts in rounds of 32, a warp scan of their tile counts places each expert's tiles.
 __global__ void tile_list_kernel(const int32_t* __restrict__ offsets, int32_t E, int64_t rows,
                                  int32_t max_tiles, int32_t* __restrict__ tile_expert,
                                  int32_t* __restrict__ tile_row, int32_t* __restrict__ num_tiles,
                                  unsigned long long* err) {
-  if (threadIdx.x != 0) return;
+  const int lane = threadIdx.x;
+  if (lane >= 32) return;
   // Offsets must be non-decreasing and end within the caller's row buffers.
-  bool ok = offsets[0] == 0 && offsets[E] <= rows;
-  for (int e = 0; e < E && ok; ++e) ok = offsets[e] <= offsets[e + 1];
-  if (!ok) {
-    hk_flag(err, hk::kErrMoeRow, (unsigned)offsets[E]);
-    *num_tiles = 0;
+  bool bad = false;
+  for (int e = lane; e < E; e += 32) bad |= offsets[e] > offsets[e + 1];
+  bad = __any_sync(0xffffffffu, bad) || offsets[0] != 0 || offsets[E] > rows;
+  if (bad) {
+    if (lane == 0) {
+      hk_flag(err, hk::kErrMoeRow, (unsigned)offsets[E]);
+      *num_tiles = 0;
+    }
     return;
   }
-  int n = 0;
-  for (int e = 0; e < E; ++e) {
-    for (int r = offsets[e]; r < offsets[e + 1]; r += kTileRows) {
-      if (n < max_tiles) {
-        tile_expert[n] = e;
-        tile_row[n] = r;
-      }
-      ++n;
+  int base = 0;
+  for (int e0 = 0; e0 < E; e0 += 32) {
+    const int e = e0 + lane;
+    const int lo = e < E ? offsets[e] : 0, hi = e < E ? offsets[e + 1] : 0;
+    const int n = (hi - lo + kTileRows - 1) / kTileRows;
+    int incl = n;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
     }
+    const int first = base + incl - n;
+    for (int i = 0; i < n; ++i) {
+      if (first + i < max_tiles) {
+        tile_expert[first + i] = e;
+        tile_row[first + i] = lo + i * kTileRows;
+      }
+    }
+    base += __shfl_sync(0xffffffffu, incl, 31);
   }
-  *num_tiles = n < max_tiles ? n : max_tiles;
+  if (lane == 0) *num_tiles = base < max_tiles ? base : max_tiles;
 }
 
 // Gate/up GEMM for one (row tile, 128-column block of h): g and u accumulate in fp32,

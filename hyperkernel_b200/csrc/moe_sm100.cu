@@ -14,10 +14,11 @@
 //           double-buffered TMEM; promotion warps add partial * sw * sx[row] in registers;
 //           at the end h = silu(g) * u is requantised to e4m3 with one scale per (row, nb)
 //           (amax over the block's 128 columns across the four warps).
-//  down     unit = (row tile, 128-column block of y): D = W2[nb] . hq^T over inter, promoted
-//           with sw * hs[row], stored as bf16.
-// Roles per CTA (6 warps): warp 0 TMA, warp 1 MMA and TMEM owner, warps 2..5 promotion (one
-// per TMEM lane quarter; thread = weight row).  Persistent over the units of the device-built
+//  down     unit = (row tile, 256-column block of y as two 128-row blocks of W2):
+//           D = W2[block] . hq^T over inter, promoted with sw * hs[row], stored as bf16.
+// Roles per CTA (10 warps): warp 0 TMA, warp 1 MMA and TMEM owner, warps 2..9 promotion (two
+// per TMEM lane quarter, each with 32 of the 64 token columns; thread = weight row), so a K
+// block costs each promotion warp one TMEM round trip.  Persistent over the units of the device-built
 // tile list; every wait bounded (1 s) with the error word, in-flight copies and MMAs drained
 // before exit.
 #include <cuda.h>
@@ -34,31 +35,40 @@ using namespace hk::sm100;
 constexpr int kRowsTile = 64;   // rows (tokens) per unit: the MMA's N
 constexpr int kWRows = 128;     // weight rows per unit: the MMA's M
 constexpr int kBK = 128;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;       // TMA, MMA, 8 promotion warps
+constexpr int kCols = 32;           // token columns per promotion warp
 constexpr int kWBytes = kWRows * kBK;      // 16 KB
 constexpr int kXBytes = kRowsTile * kBK;   // 8 KB
 constexpr uint32_t kIdesc = idesc_e4m3(kWRows, kRowsTile);
 constexpr unsigned long long kDrainNs = 1000000000ull;
+// TMEM accumulator buffers: the MMA runs this many K blocks ahead of the promotion warps, which
+// covers their per-unit work (scale table at the start, requantisation or stores at the end).
+#ifndef HK_MOE_TBUFS
+#define HK_MOE_TBUFS 4
+#endif
+constexpr int kTBufs = HK_MOE_TBUFS;
+static_assert(kTBufs == 2 || kTBufs == 4, "TMEM buffers");
+
 
 // Control block offsets (after the ring and the scale table).
 constexpr int kBarFull = 0;      // [8]
 constexpr int kBarEmpty = 64;    // [8]
-constexpr int kBarTFull = 128;   // [2]
-constexpr int kBarTEmpty = 144;  // [2]
-constexpr int kTmemSlot = 160;
-constexpr int kAbort = 164;
+constexpr int kBarTFull = 128;   // [kTBufs]
+constexpr int kBarTEmpty = 160;  // [kTBufs]
+constexpr int kTmemSlot = 192;
+constexpr int kAbort = 196;
 constexpr int kRed = 256;        // [4][64] floats: per-warp column amax (up epilogue)
 constexpr int kCtlBytes = kRed + 4 * kRowsTile * 4;
 
 template <bool kUp>
 struct Cfg {
-  static constexpr int kStageBytes = (kUp ? 2 : 1) * kWBytes + kXBytes;
+  static constexpr int kStageBytes = 2 * kWBytes + kXBytes;  // two weight blocks, one row tile
   static constexpr int kMaxKb = kUp ? 64 : 32;  // scale-table capacity in K blocks
-  static constexpr int kStages = kUp ? 5 : 8;
+  static constexpr int kStages = 5;
   static constexpr int kOffScales = kStages * kStageBytes;
   static constexpr int kOffCtl = kOffScales + kMaxKb * kRowsTile * 4;
   static constexpr int kSmem = kOffCtl + kCtlBytes;
-  static constexpr uint32_t kTmemCols = kUp ? 256 : 128;
+  static constexpr uint32_t kTmemCols = kTBufs * 128;
   static_assert(kSmem <= 232448, "shared memory budget");
 };
 
@@ -124,9 +134,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(ctl_u + kBarFull + 8 * s, 1);
       mbar_init(ctl_u + kBarEmpty + 8 * s, 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kTBufs; ++b) {
       mbar_init(ctl_u + kBarTFull + 8 * b, 1);
-      mbar_init(ctl_u + kBarTEmpty + 8 * b, 4);
+      mbar_init(ctl_u + kBarTEmpty + 8 * b, 8);
     }
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -139,7 +149,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // up: K = hidden, units per tile = inter / 128; down: K = inter, units per tile = hidden / 128
   const int kblocks = (kUp ? p.hidden : p.inter) / kBK;
-  const int nblocks = (kUp ? p.inter : p.hidden) / 128;
+  // up: one unit per 128-column block of h (its gate and up row blocks); down: one unit per
+  // pair of 128-row blocks of W2 (256 output columns; the second is empty past hidden).
+  const int nblocks = kUp ? p.inter / 128 : (p.hidden / 128 + 1) / 2;
   const int units = *p.num_tiles * nblocks;
 
   if (warp == 0) {
@@ -150,7 +162,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int tile = u / nblocks, nb = u % nblocks;
         const int e = p.tile_expert[tile], r0 = p.tile_row[tile];
         // weight rows of this unit (gate block, and up block inter rows later)
-        const int wrow = kUp ? e * 2 * p.inter + nb * 128 : e * p.hidden + nb * 128;
+        const int wrow = kUp ? e * 2 * p.inter + nb * 128 : e * p.hidden + nb * 256;
         for (int kb = 0; kb < kblocks; ++kb) {
           const int s = g % C::kStages, fill = g / C::kStages;
           if (fill > 0 && !mbar_wait(ctl_u + kBarEmpty + 8 * s, (fill - 1) & 1, abort, p.err, 961)) {
@@ -161,8 +173,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t full = ctl_u + kBarFull + 8 * s;
           mbar_expect_tx(full, C::kStageBytes);
           tma_load_2d(dst, &wmap, full, kb * kBK, wrow);
-          if (kUp) tma_load_2d(dst + kWBytes, &wmap, full, kb * kBK, wrow + p.inter);
-          tma_load_2d(dst + (kUp ? 2 : 1) * kWBytes, &xmap, full, kb * kBK, r0);
+          tma_load_2d(dst + kWBytes, &wmap, full, kb * kBK, wrow + (kUp ? p.inter : 128));
+          tma_load_2d(dst + 2 * kWBytes, &xmap, full, kb * kBK, r0);
           ++g;
         }
       }
@@ -179,7 +191,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
         for (int kb = 0; kb < kblocks; ++kb) {
-          const int s = g % C::kStages, fill = g / C::kStages, buf = g & 1, use = g >> 1;
+          const int s = g % C::kStages, fill = g / C::kStages, buf = g % kTBufs, use = g / kTBufs;
           if (!mbar_wait(ctl_u + kBarFull + 8 * s, fill & 1, abort, p.err, 962) ||
               (use > 0 && !mbar_wait(ctl_u + kBarTEmpty + 8 * buf, (use - 1) & 1, abort, p.err, 963))) {
             ok = false;
@@ -187,13 +199,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
           const uint32_t a = smem_u32(smem + s * C::kStageBytes);
-          const uint32_t x = a + (kUp ? 2 : 1) * kWBytes;
-          const uint32_t d = tmem + (uint32_t)(buf * (kUp ? 128 : 64));
+          const uint32_t x = a + 2 * kWBytes;
+          const uint32_t d = tmem + (uint32_t)(buf * 128);
 #pragma unroll
           for (int kk = 0; kk < kBK / 32; ++kk) {
             const uint64_t bdesc = sdesc_sw128(x + 32 * kk, 16, 1024);
             umma_f8(d, sdesc_sw128(a + 32 * kk, 16, 1024), bdesc, kIdesc, kk > 0 ? 1u : 0u);
-            if (kUp) umma_f8(d + 64, sdesc_sw128(a + kWBytes + 32 * kk, 16, 1024), bdesc, kIdesc, kk > 0 ? 1u : 0u);
+            umma_f8(d + 64, sdesc_sw128(a + kWBytes + 32 * kk, 16, 1024), bdesc, kIdesc, kk > 0 ? 1u : 0u);
           }
           umma_commit(ctl_u + kBarEmpty + 8 * s);
           umma_commit(ctl_u + kBarTFull + 8 * buf);
@@ -203,15 +215,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (g > 0) {
         const int last = g - 1;
         const unsigned long long t0 = globaltimer();
-        while (!mbar_try_wait(ctl_u + kBarTFull + 8 * (last & 1), (last >> 1) & 1) &&
+        while (!mbar_try_wait(ctl_u + kBarTFull + 8 * (last % kTBufs), (last / kTBufs) & 1) &&
                globaltimer() - t0 < kDrainNs) {
         }
       }
     }
   } else {
-    const int q = warp & 3;           // TMEM lane quarter
-    const int m = q * 32 + lane;      // weight row inside the unit's 128-row block
-    const int et = threadIdx.x - 64;  // 0..127 among the promotion threads
+    const int q = warp & 3;            // TMEM lane quarter
+    const int half = (warp - 2) >> 2;  // token columns [half * 32, half * 32 + 32)
+    const int m = q * 32 + lane;       // weight row inside the unit's 128-row block
+    const int et = threadIdx.x - 64;   // 0..255 among the promotion threads
     float* red = reinterpret_cast<float*>(ctl + kRed);
     int g = 0;
     bool live = true;
@@ -220,27 +233,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int e = p.tile_expert[tile], r0 = p.tile_row[tile];
       const int count = min(kRowsTile, p.offsets[e + 1] - r0);
       // Per-row activation scales of the tile for every K block: scales[kb][n].
-      asm volatile("bar.sync 1, 128;" ::: "memory");  // the previous unit is done reading them
-      for (int i = et; i < kblocks * kRowsTile; i += 128) {
+      asm volatile("bar.sync 1, 256;" ::: "memory");  // the previous unit is done reading them
+      for (int i = et; i < kblocks * kRowsTile; i += 256) {
         const int n = i % kRowsTile, kb = i / kRowsTile;
         scales[kb * kRowsTile + n] = n < count ? p.act_scale[(int64_t)(r0 + n) * kblocks + kb] : 0.f;
       }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      // Weight scales of the unit's two row blocks (g: gate or first block, u: up or second).
+      const int hb = p.hidden / 128;
+      const bool second = kUp || 2 * nb + 1 < hb;
       const float* wsc = kUp ? p.w_scale + ((int64_t)e * (2 * p.inter / 128) + nb) * kblocks
-                             : p.w_scale + ((int64_t)e * (p.hidden / 128) + nb) * kblocks;
-      const float* wsu = kUp ? wsc + (int64_t)(p.inter / 128) * kblocks : wsc;
-      float acc_g[kRowsTile], acc_u[kUp ? kRowsTile : 1];
+                             : p.w_scale + ((int64_t)e * hb + 2 * nb) * kblocks;
+      const float* wsu = kUp ? wsc + (int64_t)(p.inter / 128) * kblocks : (second ? wsc + kblocks : wsc);
+      float acc_g[kCols], acc_u[kCols];
 #pragma unroll
-      for (int i = 0; i < kRowsTile; ++i) acc_g[i] = 0.f;
+      for (int i = 0; i < kCols; ++i) acc_g[i] = 0.f;
 #pragma unroll
-      for (int i = 0; i < (kUp ? kRowsTile : 1); ++i) acc_u[i] = 0.f;
-      // A warp whose wait fails stops waiting but stays in step, so the four promotion warps
-      // always meet at the named barriers and leave the unit loop together.
+      for (int i = 0; i < kCols; ++i) acc_u[i] = 0.f;
+      // A warp whose wait fails stops waiting but stays in step, so the promotion warps always
+      // meet at the named barriers and leave the unit loop together.
       for (int kb = 0; kb < kblocks; ++kb, ++g) {
         if (!live) continue;
-        const int buf = g & 1, use = g >> 1;
+        const int buf = g % kTBufs, use = g / kTBufs;
         const float sg = wsc[kb];
-        const float su = kUp ? wsu[kb] : 0.f;
+        const float su = wsu[kb];
         bool ok = true;
         if (lane == 0) ok = mbar_wait(ctl_u + kBarTFull + 8 * buf, use & 1, abort, p.err, 964);
         ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
@@ -249,66 +265,61 @@ __global__ void __launch_bounds__(kThreads, 1)
           continue;
         }
         tc_fence_after();
-        const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * (kUp ? 128 : 64));
-        const float4* sc4 = reinterpret_cast<const float4*>(scales + kb * kRowsTile);
+        const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * 128 + half * kCols);
+        float vg[kCols], vu[kCols];
+        tmem_ld32x2(base, base + 64, vg, vu);  // both blocks' columns of this half, one wait
+        const float4* sc4 = reinterpret_cast<const float4*>(scales + kb * kRowsTile + half * kCols);
 #pragma unroll
-        for (int c = 0; c < kRowsTile / 16; ++c) {
-          float v[16];
-          tmem_ld16(base + 16 * c, v);
+        for (int j = 0; j < kCols / 4; ++j) {
+          const float4 s4 = sc4[j];
+          const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float4 s4 = sc4[4 * c + j];
-            const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-              acc_g[16 * c + 4 * j + i] = fmaf(v[4 * j + i], sv[i] * sg, acc_g[16 * c + 4 * j + i]);
-          }
-          if constexpr (kUp) {
-            tmem_ld16(base + 64 + 16 * c, v);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const float4 s4 = sc4[4 * c + j];
-              const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
-#pragma unroll
-              for (int i = 0; i < 4; ++i)
-                acc_u[16 * c + 4 * j + i] = fmaf(v[4 * j + i], sv[i] * su, acc_u[16 * c + 4 * j + i]);
-            }
+          for (int i = 0; i < 4; ++i) {
+            acc_g[4 * j + i] = fmaf(vg[4 * j + i], sv[i] * sg, acc_g[4 * j + i]);
+            acc_u[4 * j + i] = fmaf(vu[4 * j + i], sv[i] * su, acc_u[4 * j + i]);
           }
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(ctl_u + kBarTEmpty + 8 * buf);
       }
-      if (!bar_and(1, 128, live)) break;
+      if (!bar_and(1, 256, live)) break;
       if constexpr (kUp) {
         // h = silu(g) * u, then one e4m3 scale per (row, nb) from the amax over this block's
-        // 128 columns (the 128 promotion threads).
+        // 128 columns: the four warps of this column half, one per lane quarter.
 #pragma unroll
-        for (int n = 0; n < kRowsTile; ++n) {
-          const float gv = acc_g[n];
-          acc_g[n] = gv / (1.f + expf(-gv)) * acc_u[n];
-          float a = fabsf(acc_g[n]);
+        for (int i = 0; i < kCols; ++i) {
+          const float gv = acc_g[i];
+          acc_g[i] = gv / (1.f + expf(-gv)) * acc_u[i];
+          float a = fabsf(acc_g[i]);
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
-          if (lane == 0) red[q * kRowsTile + n] = a;
+          if (lane == 0) red[q * kRowsTile + half * kCols + i] = a;
         }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
+        asm volatile("bar.sync 1, 256;" ::: "memory");
         const int inter_blocks = p.inter / 128;
 #pragma unroll
-        for (int n = 0; n < kRowsTile; ++n) {
+        for (int i = 0; i < kCols; ++i) {
+          const int n = half * kCols + i;
           if (n < count) {
             const float amax =
                 fmaxf(fmaxf(red[n], red[kRowsTile + n]), fmaxf(red[2 * kRowsTile + n], red[3 * kRowsTile + n]));
             const float s = __fdiv_rn(fmaxf(amax, 1e-12f), 448.0f);
             const int64_t row = r0 + n;
-            p.hq[row * p.inter + nb * 128 + m] = f32_to_e4m3(__fdiv_rn(acc_g[n], s));
+            p.hq[row * p.inter + nb * 128 + m] = f32_to_e4m3(__fdiv_rn(acc_g[i], s));
             if (m == 0) p.hs[row * inter_blocks + nb] = s;
           }
         }
       } else {
 #pragma unroll
-        for (int n = 0; n < kRowsTile; ++n)
-          if (n < count) p.y[(int64_t)(r0 + n) * p.hidden + nb * 128 + m] = f32_to_bf16_bits(acc_g[n]);
+        for (int i = 0; i < kCols; ++i) {
+          const int n = half * kCols + i;
+          if (n < count) {
+            uint16_t* yr = p.y + (int64_t)(r0 + n) * p.hidden + nb * 256 + m;
+            yr[0] = f32_to_bf16_bits(acc_g[i]);
+            if (second) yr[128] = f32_to_bf16_bits(acc_u[i]);
+          }
+        }
       }
     }
   }
