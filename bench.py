@@ -16,6 +16,11 @@ without an explicit flush.  Inputs are synthetic (seeded), see hyperkernel_b200/
 --impl reference times the CPU restatement of the same step (oracle/, the reference has no
 runnable implementation of this path on this box) on all host cores, on a bounded sample of
 lanes per step scaled to the whole batch.
+
+--workload moe | linear measures the other two layers of the step on one GPU, each as its own
+JSON line: config 4 (MoE layer: quantise, route, permute, grouped FP8 expert FFN over 256
+routed experts + the shared expert, combine; 512 tokens, hidden 7168, inter 2048) and config 3
+(the MLA FP8 projections q_a, q_b, kv_a, o over the 4144-token mixed prefill + decode batch).
 """
 from __future__ import annotations
 
@@ -170,10 +175,13 @@ def main(argv=None):
     ap.add_argument("--ctx-min", type=int, default=1024, help="profiling override of config 2")
     ap.add_argument("--ctx-max", type=int, default=131072, help="profiling override of config 2")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host round trip leg")
+    ap.add_argument("--workload", default="decode", choices=["decode", "moe", "linear"])
     args = ap.parse_args(argv)
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload != "decode":
+        return run_layer(args)
 
     import torch
     import torch.distributed as dist
@@ -311,6 +319,279 @@ def main(argv=None):
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+# ------------------------------------------------------------------------------------------
+# config 3 and config 4 layers (--workload linear | moe), one GPU
+# ------------------------------------------------------------------------------------------
+
+MOE_T, MOE_E, MOE_H, MOE_I, MOE_K = 512, 256, 7168, 2048, 8
+# MLA projections of one layer (DeepSeek-V3 shapes): (name, out features, in features)
+LINEAR_T = 48 + 2 * 2048
+LINEAR_PROJ = [("q_a", 1536, 7168), ("q_b", 128 * 192, 1536), ("kv_a", 576, 7168), ("o", 7168, 128 * 128)]
+
+
+def _peaks():
+    try:
+        pk = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        return float(pk["hbm_gbs"]), 2.0 * float(pk["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 2 * 1590.0, "fallback"
+
+
+def _rand_e4m3(torch, shape, gen, device):
+    """Seeded random e4m3 bytes (the two NaN encodings avoided)."""
+    b = torch.randint(0, 256, shape, generator=gen, device=device, dtype=torch.uint8)
+    return torch.where((b & 0x7F) == 0x7F, b ^ 1, b)
+
+
+def _timed(torch, fn, steps, stream, inner=True):
+    """Times `steps` calls of fn on `stream`; returns (total ms, mean ms of the region fn marks
+    with its event pair, or None when inner is False)."""
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record(stream)
+    for i in range(steps):
+        fn(ev[i])
+    end.record(stream)
+    torch.cuda.synchronize()
+    inner_ms = float(np.mean([a.elapsed_time(b) for a, b in ev])) if inner else None
+    return start.elapsed_time(end), inner_ms
+
+
+def run_layer(args):
+    import torch
+
+    from hyperkernel_b200 import _lib as hk
+    from hyperkernel_b200.clocks import ClockSampler
+
+    world, rank, local = _dist()
+    if world > 1:
+        print(json.dumps({"workload": args.workload, "unavailable": "layer workloads run on one GPU"}))
+        return 0
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    stream = torch.cuda.current_stream()
+    gen = torch.Generator(device=device)
+    gen.manual_seed(7)
+    hbm_peak, fp8_peak, peak_src = _peaks()
+    if args.workload == "moe":
+        T, E, H, I, K = MOE_T, MOE_E, MOE_H, MOE_I, MOE_K
+        w13 = _rand_e4m3(torch, (E, 2 * I, H), gen, device)
+        w2 = _rand_e4m3(torch, (E, H, I), gen, device)
+        s13 = torch.rand((E, 2 * I // 128, H // 128), generator=gen, device=device) * 1e-3
+        s2 = torch.rand((E, H // 128, I // 128), generator=gen, device=device) * 1e-3
+        sh13 = _rand_e4m3(torch, (1, 2 * I, H), gen, device)
+        sh2 = _rand_e4m3(torch, (1, H, I), gen, device)
+        shs13 = torch.rand((1, 2 * I // 128, H // 128), generator=gen, device=device) * 1e-3
+        shs2 = torch.rand((1, H // 128, I // 128), generator=gen, device=device) * 1e-3
+        x = torch.randn((T, H), generator=gen, device=device).to(torch.bfloat16)
+        logits = torch.randn((T, E), generator=gen, device=device)
+        rows = T * K
+        ws = torch.empty(hk.moe_workspace_size(rows, H, I), dtype=torch.uint8, device=device)
+        ws_sh = torch.empty(hk.moe_workspace_size(T, H, I), dtype=torch.uint8, device=device)
+        y = torch.empty((rows, H), dtype=torch.bfloat16, device=device)
+        y_sh = torch.empty((T, H), dtype=torch.bfloat16, device=device)
+        sh_off = torch.tensor([0, T], dtype=torch.int32, device=device)
+        sh_tok = torch.arange(T, dtype=torch.int32, device=device)
+
+        def step(x_in, logits_in, ev=None):
+            xq, sx = hk.quant_fp8(x_in)
+            ids, w = hk.route(logits_in, None, K, 1.0)
+            off, tok, pw, inv = hk.permute(ids, w, E)
+            if ev is not None:
+                ev[0].record(stream)
+            hk.moe_grouped(xq, sx, off, tok, rows, H, I, w13, s13, w2, s2, out=y, workspace=ws)
+            hk.moe_grouped(xq, sx, sh_off, sh_tok, T, H, I, sh13, shs13, sh2, shs2, out=y_sh, workspace=ws_sh)
+            if ev is not None:
+                ev[1].record(stream)
+            return hk.combine(y, pw, inv, y_sh, T, K), off
+
+        for _ in range(args.warmup):
+            _, off = step(x, logits)
+        torch.cuda.synchronize()
+        hk.check_errors()
+        counts = (off[1:] - off[:-1]).cpu().numpy()
+        hit = int((counts > 0).sum())
+        wbytes = (hit + 1) * 3 * H * I + (hit + 1) * (2 * I // 128 * H // 128 + H // 128 * I // 128) * 4
+        abytes = wbytes + (rows + T) * (H + 2 * 2 * I + 2 * H)  # x rows, h write+read, y write
+        flops = 2 * (rows + T) * 3 * H * I
+        sampler = ClockSampler(local).start()
+        launches0 = hk.kernel_launches()
+        t0 = time.perf_counter()
+        ms, ffn_ms = _timed(torch, lambda ev: step(x, logits, ev), args.steps, stream)
+        t1 = time.perf_counter()
+        launches = hk.kernel_launches() - launches0
+        sampler.stop()
+        clocks = sampler.summary(t0, t1)
+        hk.check_errors()
+        # end to end: pinned host activations and router logits in, the layer output back
+        hx = torch.empty((T, H), dtype=torch.bfloat16).pin_memory().copy_(x.cpu())
+        hl = torch.empty((T, E), dtype=torch.float32).pin_memory().copy_(logits.cpu())
+        hout = torch.empty((T, H), dtype=torch.bfloat16).pin_memory()
+        dx, dl = torch.empty_like(x), torch.empty_like(logits)
+
+        def e2e(ev):
+            dx.copy_(hx, non_blocking=True)
+            dl.copy_(hl, non_blocking=True)
+            out, _ = step(dx, dl)
+            hout.copy_(out, non_blocking=True)
+
+        e2e_ms, _ = _timed(torch, e2e, args.steps, stream, inner=False)
+        cpu = None if args.no_cpu_baseline else _moe_cpu_baseline(x, logits, w13, s13, w2, s2, sh13, shs13,
+                                                                   sh2, shs2)
+        value = T * args.steps / (ms / 1e3)
+        achieved = abytes / (ffn_ms / 1e3) / 1e9
+        line = {
+            "metric": "MoE layer tokens/s (config 4)", "value": value, "unit": "tokens/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "e4m3 x e4m3 -> f32",
+            "data": "synthetic (seeded): e4m3 weights, N(0,1) activations and router logits",
+            "config": {"workload": "config4: 512 tokens, 256 routed experts top-8 + 1 shared, hidden 7168, "
+                                   "inter 2048, FP8 128x128 block scales; quant+route+permute+grouped FFN+combine",
+                       "experts_hit": hit, "l2": "11.4 GB of expert weights per step, no flush"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": achieved / hbm_peak, "traffic": None,
+                         "kernel": "grouped expert FFN (hk_moe_grouped: routed + shared)", "kernel_ms": ffn_ms,
+                         "algorithmic_bytes": abytes, "peak_source": peak_src,
+                         "tflops": flops / (ffn_ms / 1e3) / 1e12, "tensor_frac_of_fp8_peak":
+                             flops / (ffn_ms / 1e3) / 1e12 / fp8_peak},
+            "cpu_baseline": cpu,
+            "e2e": {"value": T * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": T * H * 2 + T * E * 4, "d2h_bytes_per_step": T * H * 2},
+            "gpu_launches": int(launches), "clocks": clocks,
+        }
+    else:
+        T = LINEAR_T
+        ws = {}
+        for name, n, k in LINEAR_PROJ:
+            ws[name] = (_rand_e4m3(torch, (n, k), gen, device),
+                        torch.rand(((n + 127) // 128, k // 128), generator=gen, device=device) * 1e-2)
+        x = torch.randn((T, 7168), generator=gen, device=device).to(torch.bfloat16)
+        attn = torch.randn((T, 128 * 128), generator=gen, device=device).to(torch.bfloat16)
+
+        def lin(a_bf16, name):
+            aq, sa = hk.quant_fp8(a_bf16)
+            w, sw = ws[name]
+            return hk.gemm_fp8(aq, sa, w, sw)
+
+        def step(x_in, attn_in, ev=None):
+            if ev is not None:
+                ev[0].record(stream)
+            qa = lin(x_in, "q_a")
+            qb = lin(qa, "q_b")
+            kva = lin(x_in, "kv_a")
+            o = lin(attn_in, "o")
+            if ev is not None:
+                ev[1].record(stream)
+            return qb, kva, o
+
+        for _ in range(args.warmup):
+            step(x, attn)
+        torch.cuda.synchronize()
+        hk.check_errors()
+        flops = sum(2 * T * n * k for _, n, k in LINEAR_PROJ)
+        sampler = ClockSampler(local).start()
+        launches0 = hk.kernel_launches()
+        t0 = time.perf_counter()
+        ms, lin_ms = _timed(torch, lambda ev: step(x, attn, ev), args.steps, stream)
+        t1 = time.perf_counter()
+        launches = hk.kernel_launches() - launches0
+        sampler.stop()
+        clocks = sampler.summary(t0, t1)
+        hk.check_errors()
+        hx = torch.empty_like(x, device="cpu").pin_memory().copy_(x.cpu())
+        ha = torch.empty_like(attn, device="cpu").pin_memory().copy_(attn.cpu())
+        outs = [torch.empty((T, n), dtype=torch.bfloat16).pin_memory() for nm, n, _k in LINEAR_PROJ if nm != "q_a"]
+        dx, da = torch.empty_like(x), torch.empty_like(attn)
+
+        def e2e(ev):
+            dx.copy_(hx, non_blocking=True)
+            da.copy_(ha, non_blocking=True)
+            for h, d in zip(outs, step(dx, da)):
+                h.copy_(d, non_blocking=True)
+
+        e2e_ms, _ = _timed(torch, e2e, args.steps, stream, inner=False)
+        cpu = None if args.no_cpu_baseline else _linear_cpu_baseline(x, attn, ws)
+        tflops = flops / (lin_ms / 1e3) / 1e12
+        line = {
+            "metric": "MLA FP8 projection tokens/s (config 3)", "value": T * args.steps / (ms / 1e3),
+            "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "e4m3 x e4m3 -> f32", "data": "synthetic (seeded)",
+            "config": {"workload": "config3: 4144 tokens (48 decode + 2 x 2048 prefill), projections "
+                                   "q_a 7168->1536, q_b 1536->24576, kv_a 7168->576, o 16384->7168, "
+                                   "activation quantisation included",
+                       "l2": "weights 60 MB and activations re-read from L2; no flush (tensor-bound)"},
+            "roofline": {"bound": "tensor", "achieved": tflops, "peak": fp8_peak, "unit": "TFLOP/s",
+                         "frac": tflops / fp8_peak, "traffic": None, "kernel": "hk_gemm_fp8 (+ hk_quant_fp8)",
+                         "kernel_ms": lin_ms, "algorithmic_flops": flops,
+                         "peak_source": f"{peak_src}: 2 x cuBLAS bf16 burst (dense FP8 = 2 x bf16)"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": T * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": x.numel() * 2 + attn.numel() * 2,
+                    "d2h_bytes_per_step": T * sum(n for nm, n, _ in LINEAR_PROJ if nm != "q_a") * 2},
+            "gpu_launches": int(launches), "clocks": clocks,
+        }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def _moe_cpu_baseline(x, logits, w13, s13, w2, s2, sh13, shs13, sh2, shs2, sample_experts=6):
+    """The oracle's layer on the host cores: quantise, route and permute all 512 tokens, then
+    the grouped FFN of the first `sample_experts` hit experts, scaled to all rows (the FFN is
+    linear in rows) plus the shared expert scaled likewise."""
+    import oracle
+
+    xb = x.view(torch_int16()).cpu().numpy().view(np.uint16)
+    lg = logits.cpu().numpy()
+    t0 = time.perf_counter()
+    xq, sx = oracle.quant_fp8(xb)
+    ids, w = oracle.route(lg, None, MOE_K, 1.0)
+    off, tok, pw, inv = oracle.permute(ids, w, MOE_E)
+    t_route = time.perf_counter() - t0
+    hit = [e for e in range(MOE_E) if off[e + 1] > off[e]][:sample_experts]
+    rows_sample = 0
+    t_ffn = 0.0
+    for e in hit:
+        r0, r1 = int(off[e]), int(off[e + 1])
+        sub_off = np.array([0, r1 - r0], np.int32)
+        a13, b13 = w13[e:e + 1].cpu().numpy(), s13[e:e + 1].cpu().numpy()
+        a2, b2 = w2[e:e + 1].cpu().numpy(), s2[e:e + 1].cpu().numpy()
+        t0 = time.perf_counter()
+        oracle.moe_grouped(xq, sx, sub_off, tok[r0:r1], MOE_H, MOE_I, a13, b13, a2, b2)
+        t_ffn += time.perf_counter() - t0
+        rows_sample += r1 - r0
+    per_row = t_ffn / max(rows_sample, 1)
+    total = t_route + per_row * (MOE_T * MOE_K + MOE_T)
+    threads = os.cpu_count() or 1
+    return {"value": MOE_T / total, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"route+permute of all 512 tokens, grouped FFN of {len(hit)} experts ({rows_sample} rows) "
+                      f"scaled per row to {MOE_T * MOE_K} routed + {MOE_T} shared rows"}
+
+
+def _linear_cpu_baseline(x, attn, ws, sample_tokens=8):
+    """The oracle's FP8 projections on the host cores for `sample_tokens` tokens, scaled."""
+    import oracle
+
+    xb = x[:sample_tokens].view(torch_int16()).cpu().numpy().view(np.uint16)
+    ab = attn[:sample_tokens].view(torch_int16()).cpu().numpy().view(np.uint16)
+    wt = {k: (w.cpu().numpy(), s.cpu().numpy()) for k, (w, s) in ws.items()}
+    t0 = time.perf_counter()
+    for name, src in (("q_a", xb), ("kv_a", xb), ("o", ab)):
+        aq, sa = oracle.quant_fp8(src)
+        oracle.gemm_fp8(aq, sa, *wt[name])
+    aq, sa = oracle.quant_fp8(np.zeros((sample_tokens, 1536), np.uint16))
+    oracle.gemm_fp8(aq, sa, *wt["q_b"])
+    dt = time.perf_counter() - t0
+    return {"value": sample_tokens / dt, "unit": "tokens/s", "cores": os.cpu_count() or 1, "kind": "port",
+            "sample": f"the four projections for {sample_tokens} of the {LINEAR_T} tokens"}
+
+
+def torch_int16():
+    import torch
+    return torch.int16
 
 
 if __name__ == "__main__":
