@@ -199,7 +199,8 @@ def main(argv=None):
 
         dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
 
-    lay = W.config2_layout(seed=rank, lanes=args.lanes, lo=args.ctx_min, hi=args.ctx_max)
+    # Every rank runs the same lane lengths (equal work per GPU: weak scaling) on its own data.
+    lay = W.config2_layout(seed=0, lanes=args.lanes, lo=args.ctx_min, hi=args.ctx_max)
     T = lay.num_tokens
     max_kv = int(lay.kv_len.max())
     gen = torch.Generator(device=device)
