@@ -47,6 +47,8 @@ SIGNATURES = {
     "hk_moe_workspace_size": (SZ, [I64, I32, I32]),
     "hk_moe_grouped": (C.c_int, [P, P, I32, P, P, I64, I32, I32, I32, P, P, P, P, P, P, SZ, P]),
     "hk_moe_grouped_noalloc": (C.c_int, [P, P, I32, P, P, I64, I32, I32, I32, P, P, P, P, P, P]),
+    "hk_gather_rows": (C.c_int, [P, I64, P, I64, I32, P, P]),
+    "hk_scatter_rows": (C.c_int, [P, I64, P, I64, I32, P, P]),
     "hk_combine": (C.c_int, [P, I64, P, P, P, I32, I32, I32, P, P]),
     "hk_open": (C.c_int, [P, P]),
     "hk_close": (None, [P]),
@@ -333,6 +335,24 @@ def moe_grouped_noalloc(xq, sx, offsets, perm_token, rows, hidden, inter, w13, s
     call("hk_moe_grouped_noalloc", ptr(xq), ptr(sx), xq.shape[0], ptr(offsets), ptr(perm_token),
          rows, E, hidden, inter, ptr(w13), ptr(s13), ptr(w2), ptr(s2), ptr(out),
          stream_ptr(stream))
+    return out
+
+
+def gather_rows(src, idx, out=None, stream=None):
+    """out[i] = src[idx[i]] (rows of src as bytes; 16-byte multiples)."""
+    rows = idx.shape[0]
+    if out is None:
+        out = torch.empty((rows,) + tuple(src.shape[1:]), dtype=src.dtype, device=src.device)
+    row_bytes = src[0].numel() * src.element_size() if src.shape[0] else out[0].numel() * out.element_size()
+    call("hk_gather_rows", ptr(src), src.shape[0], ptr(idx), rows, row_bytes, ptr(out), stream_ptr(stream))
+    return out
+
+
+def scatter_rows(src, idx, out, stream=None):
+    """out[idx[i]] = src[i]."""
+    rows = idx.shape[0]
+    row_bytes = out[0].numel() * out.element_size()
+    call("hk_scatter_rows", ptr(src), rows, ptr(idx), out.shape[0], row_bytes, ptr(out), stream_ptr(stream))
     return out
 
 

@@ -1,0 +1,158 @@
+"""Multi-GPU decomposition of the decode step over torch.distributed (NCCL over NVLink on the
+B200s; any backend whose all_to_all_single / all_gather the tensors support).
+
+Two shards have a real exchange step:
+
+  * expert parallelism for the MoE layer (config 4): rank r owns experts
+    [r E/N, (r+1) E/N).  After routing and the global permutation, the permuted rows of
+    destination d are contiguous (rows offsets[d E/N] .. offsets[(d+1) E/N]), so dispatch is
+    one exchange of per-(destination, expert) counts and one all-to-allv of the routed e4m3
+    rows and their 1x128 scales.  The receiver runs the grouped FFN over what it got, its
+    rows ordered expert-major through a local permutation (the grouped FFN gathers through
+    perm_token, so no extra copy), and combine is the reverse all-to-allv followed by the
+    weighted sum of hk_combine on the sender.
+
+  * context parallelism for a long lane (config 5): the lane's KV positions are split into
+    page-aligned contiguous ranges, one per rank; each rank computes (o, lse) partials over
+    its range (hk_mla_partial_fp8), the partials are all-gathered and merged by
+    log-sum-exp (hk_lse_merge).
+
+The decode attention itself shards by lane with no exchange (each rank runs its own lanes).
+The row movement defaults to libhk's kernels (hk_gather_rows / hk_scatter_rows) and the merge
+to hk_lse_merge; `gather`, `scatter` and `merge` are parameters only so the host-side plan and
+exchange can be exercised with CPU tensors.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from . import _lib
+
+
+# ------------------------------------------------------------------------------------------
+# expert parallelism
+# ------------------------------------------------------------------------------------------
+
+def expert_range(num_experts: int, world: int, rank: int) -> tuple[int, int]:
+    """Experts owned by `rank`: a contiguous block of num_experts / world."""
+    if num_experts % world:
+        raise ValueError(f"{num_experts} experts do not split over {world} ranks")
+    per = num_experts // world
+    return rank * per, (rank + 1) * per
+
+
+@dataclass
+class EpPlan:
+    """One dispatch: rows sent to / received from every rank and the local expert order."""
+    send_counts: list          # rows this rank sends to each rank (its permuted-row blocks)
+    recv_counts: list          # rows this rank receives from each rank
+    recv_expert_counts: np.ndarray  # [world][local experts] rows received per source and expert
+    local_offsets: np.ndarray  # [local experts + 1] exclusive scan of the rows per local expert
+    local_perm: np.ndarray     # row j of the expert-major order = received row local_perm[j]
+
+
+def ep_plan(offsets: np.ndarray, num_experts: int, group=None, device=None) -> EpPlan:
+    """Exchanges the per-(destination, expert) row counts; offsets is the host copy of the
+    global permutation's expert offsets [num_experts + 1]; the counts travel on `device`
+    (the process group's device)."""
+    world = dist.get_world_size(group)
+    per = num_experts // world
+    counts = np.diff(np.asarray(offsets, dtype=np.int64)).reshape(world, per)
+    send = torch.from_numpy(np.ascontiguousarray(counts)).to(device or "cpu")
+    recv = torch.empty_like(send)
+    dist.all_to_all_single(recv, send, group=group)
+    recv_np = recv.cpu().numpy()
+    send_counts = counts.sum(1).tolist()
+    recv_counts = recv_np.sum(1).tolist()
+    # received layout: source-major, and expert-major inside each source's block
+    src_base = np.concatenate([[0], np.cumsum(recv_counts)[:-1]]).astype(np.int64)
+    seg = np.concatenate([np.zeros((world, 1), np.int64), np.cumsum(recv_np, axis=1)[:, :-1]], axis=1)
+    perm = []
+    for e in range(per):
+        for s in range(world):
+            start = src_base[s] + seg[s, e]
+            perm.append(np.arange(start, start + recv_np[s, e], dtype=np.int64))
+    local_perm = np.concatenate(perm).astype(np.int32) if perm else np.zeros(0, np.int32)
+    local_offsets = np.concatenate([[0], np.cumsum(recv_np.sum(0))]).astype(np.int32)
+    return EpPlan(send_counts, recv_counts, recv_np, local_offsets, local_perm)
+
+
+def _default_gather(src, idx):
+    return _lib.gather_rows(src, idx)
+
+
+def _default_scatter(src, idx, out):
+    return _lib.scatter_rows(src, idx, out)
+
+
+def ep_dispatch(xq, sx, offsets, perm_token, num_experts: int, group=None, gather=None):
+    """Sends every routed row to the rank owning its expert.
+
+    xq [tokens][hidden] e4m3 and sx [tokens][hidden/128] are this rank's quantised tokens;
+    offsets / perm_token are the global permutation (hk_permute over all experts).  Returns
+    (xq_recv, sx_recv, local_offsets, local_perm, plan): the rows of this rank's experts from
+    every rank, the expert offsets and permutation to run the grouped FFN over them."""
+    gather = gather or _default_gather
+    plan = ep_plan(offsets.cpu().numpy(), num_experts, group, device=xq.device)
+    x_send = gather(xq, perm_token)
+    s_send = gather(sx, perm_token)
+    rows_in = int(sum(plan.recv_counts))
+    x_recv = torch.empty((rows_in,) + tuple(xq.shape[1:]), dtype=xq.dtype, device=xq.device)
+    s_recv = torch.empty((rows_in,) + tuple(sx.shape[1:]), dtype=sx.dtype, device=sx.device)
+    dist.all_to_all_single(x_recv, x_send, plan.recv_counts, plan.send_counts, group=group)
+    dist.all_to_all_single(s_recv, s_send, plan.recv_counts, plan.send_counts, group=group)
+    dev = xq.device
+    local_offsets = torch.from_numpy(plan.local_offsets).to(dev)
+    local_perm = torch.from_numpy(plan.local_perm).to(dev)
+    return x_recv, s_recv, local_offsets, local_perm, plan
+
+
+def ep_return(y_local, plan: EpPlan, local_perm, group=None, scatter=None):
+    """Sends the expert outputs back: y_local holds the grouped FFN's rows in the local
+    expert-major order; the result holds this rank's routed rows in its global permuted order
+    (what hk_combine reads through inv)."""
+    scatter = scatter or _default_scatter
+    rows_in = int(sum(plan.recv_counts))
+    y_src = torch.empty((rows_in,) + tuple(y_local.shape[1:]), dtype=y_local.dtype, device=y_local.device)
+    scatter(y_local[:rows_in], local_perm, y_src)
+    rows_out = int(sum(plan.send_counts))
+    y_back = torch.empty((rows_out,) + tuple(y_local.shape[1:]), dtype=y_local.dtype, device=y_local.device)
+    dist.all_to_all_single(y_back, y_src, plan.send_counts, plan.recv_counts, group=group)
+    return y_back
+
+
+# ------------------------------------------------------------------------------------------
+# context parallelism
+# ------------------------------------------------------------------------------------------
+
+def cp_ranges(kv_len: int, world: int, page: int = 64) -> list[tuple[int, int]]:
+    """Page-aligned contiguous KV ranges [begin, end) covering [0, kv_len), one per rank,
+    balanced to within a page."""
+    pages = (kv_len + page - 1) // page
+    out = []
+    for r in range(world):
+        p0 = pages * r // world
+        p1 = pages * (r + 1) // world
+        out.append((min(p0 * page, kv_len), min(p1 * page, kv_len)))
+    return out
+
+
+def _default_merge(o_parts, lse_parts):
+    return _lib.lse_merge(o_parts, lse_parts)
+
+
+def cp_merge(o_part, lse_part, group=None, merge=None):
+    """All-gathers every rank's (o [rows][dv] fp32, lse [rows]) partial for the same query rows
+    and merges them by log-sum-exp; every rank gets the merged (out, lse)."""
+    merge = merge or _default_merge
+    world = dist.get_world_size(group)
+    # flat outputs: every backend takes a 1-D concatenation
+    o_all = torch.empty(world * o_part.numel(), dtype=o_part.dtype, device=o_part.device)
+    lse_all = torch.empty(world * lse_part.numel(), dtype=lse_part.dtype, device=lse_part.device)
+    dist.all_gather_into_tensor(o_all, o_part.contiguous().view(-1), group=group)
+    dist.all_gather_into_tensor(lse_all, lse_part.contiguous().view(-1), group=group)
+    return merge(o_all.view((world,) + tuple(o_part.shape)), lse_all.view((world,) + tuple(lse_part.shape)))

@@ -228,6 +228,16 @@ int hk_moe_grouped_noalloc(const uint8_t* xq, const float* sx, int32_t tokens,
                            const uint8_t* w13, const float* s13, const uint8_t* w2,
                            const float* s2, uint16_t* y, void* stream);
 
+/* Row movement around the expert-parallel all-to-all (dispatch gathers the routed rows of
+ * each destination's experts, combine scatters returning rows back into permuted order):
+ * gather dst[i] = src[idx[i]] for i < rows (idx < src_rows); scatter dst[idx[i]] = src[i]
+ * (idx < dst_rows).  Rows of row_bytes bytes (a multiple of 4, 4-byte aligned buffers).
+ * An out-of-range index skips its row and sets the device error word. */
+int hk_gather_rows(const void* src, int64_t src_rows, const int32_t* idx, int64_t rows,
+                   int32_t row_bytes, void* dst, void* stream);
+int hk_scatter_rows(const void* src, int64_t rows, const int32_t* idx, int64_t dst_rows,
+                    int32_t row_bytes, void* dst, void* stream);
+
 /* out[t][hidden] bf16 = sum_k perm_weight[inv[t,k]] * y[inv[t,k]] (+ shared[t] when not
  * NULL), fp32 accumulation in k order; y has `rows` rows. */
 int hk_combine(const uint16_t* y, int64_t rows, const float* perm_weight, const int32_t* inv,

@@ -1,0 +1,130 @@
+"""Expert and context parallelism on B200s over NCCL (hyperkernel_b200/parallel.py).
+
+The row gather / scatter kernels run on one GPU; the two-rank tests need two GPUs (skipped
+otherwise) and run each rank as its own process on its own device.  Expert parallelism must
+reproduce, bit for bit, the rows the one-GPU grouped FFN computes for the same tokens (a row's
+output does not depend on the other rows of its tile); context parallelism must merge to the
+whole-lane attention within the bf16 tolerance.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from hyperkernel_b200 import workload as W
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-2
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def test_gather_and_scatter_rows(hk, cuda):
+    g = torch.Generator(device=cuda)
+    g.manual_seed(5)
+    for cols, dtype in [(7168, torch.uint8), (56, torch.float32), (2, torch.float32), (512, torch.bfloat16)]:
+        src = torch.randint(0, 255, (300, cols), generator=g, device=cuda).to(dtype)
+        idx = torch.randperm(300, generator=g, device=cuda)[:200].to(torch.int32)
+        out = hk.gather_rows(src, idx)
+        assert torch.equal(out, src[idx.long()])
+        back = torch.zeros_like(src)
+        hk.scatter_rows(out, idx, back)
+        assert torch.equal(back[idx.long()], out)
+    hk.check_errors()
+
+
+def _two_gpus():
+    return torch.cuda.is_available() and torch.cuda.device_count() >= 2
+
+
+def _rank_main(rank, port, what):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    import datetime
+
+    dist.init_process_group("nccl", rank=rank, world_size=2, device_id=dev,
+                            timeout=datetime.timedelta(seconds=120))
+    try:
+        if what == "ep":
+            _ep(rank, dev)
+        else:
+            _cp(rank, dev)
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _ep(rank, dev):
+    from hyperkernel_b200 import _lib as hk
+    from hyperkernel_b200 import parallel as P
+
+    T, E, H, I, K = 64, 8, 512, 256, 4
+    inp = W.moe_inputs(T * 2, E, H, I, top_k=K, seed=90)
+    d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    x = torch.from_numpy(inp["x"][rank * T:(rank + 1) * T].view(np.int16)).to(dev).view(torch.bfloat16)
+    ids, w = hk.route(d(inp["logits"][rank * T:(rank + 1) * T]), None, K, 1.0)
+    off, tok, pw, inv = hk.permute(ids, w, E)
+    xq, sx = hk.quant_fp8(x)
+    w13, s13, w2, s2 = d(inp["w13"]), d(inp["s13"]), d(inp["w2"]), d(inp["s2"])
+    want = hk.moe_grouped(xq, sx, off, tok, T * K, H, I, w13, s13, w2, s2)[:T * K]
+    x_recv, s_recv, loc_off, loc_perm, plan = P.ep_dispatch(xq, sx, off, tok, E)
+    e0, e1 = P.expert_range(E, 2, rank)
+    rows = x_recv.shape[0]
+    y_local = hk.moe_grouped(x_recv, s_recv, loc_off, loc_perm, rows, H, I, w13[e0:e1].contiguous(),
+                             s13[e0:e1].contiguous(), w2[e0:e1].contiguous(), s2[e0:e1].contiguous())
+    y_back = P.ep_return(y_local, plan, loc_perm)
+    torch.cuda.synchronize()
+    hk.check_errors()
+    assert torch.equal(y_back.view(torch.int16), want.view(torch.int16)), f"rank {rank}: EP rows differ"
+
+
+def _cp(rank, dev):
+    from hyperkernel_b200 import _lib as hk
+    from hyperkernel_b200 import parallel as P
+    import oracle
+
+    heads = 128
+    rng = W.Rng(91)
+    lay = W.paged_layout(rng, np.array([20000]), np.array([5]), 64)
+    inp = W.mla_inputs(lay, heads, seed=92)
+    T = lay.num_tokens
+    p = oracle.pack(lay.new_rows, lay.context, lay.block_table, 64, lay.num_pages, T)
+    c8 = np.zeros((lay.num_slots, 576), np.uint8)
+    s8 = np.zeros(lay.num_slots, np.float32)
+    oracle.kv_append_fp8(inp["kv_cache"], np.arange(lay.num_slots, dtype=np.int32), c8, s8)
+    d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    q = torch.from_numpy(inp["q"].view(np.int16)).to(dev).view(torch.bfloat16)
+    args = (q, d(c8), d(s8), d(lay.block_table), d(p["cu_seqlens"]), d(p["positions"][:T].copy()))
+    kv = int(lay.kv_len[0])
+    full, full_lse = hk.mla_decode_fp8(*args, 64, kv, inp["scale"])
+    b, e = P.cp_ranges(kv, 2)[rank]
+    o, l = hk.mla_partial_fp8(*args, d(np.array([b], np.int32)), d(np.array([e], np.int32)), 64, kv, inp["scale"])
+    out, lse = P.cp_merge(o.reshape(T * heads, 512), l.reshape(T * heads))
+    torch.cuda.synchronize()
+    hk.check_errors()
+    a = out.float().cpu().numpy()
+    f = full.reshape(-1, 512).float().cpu().numpy()
+    assert np.abs(a - f).max() / np.abs(f).max() <= TOL
+    assert (lse.cpu() - full_lse.reshape(-1).cpu()).abs().max().item() <= 1e-3
+
+
+@pytest.mark.skipif(not _two_gpus(), reason="needs two GPUs")
+def test_expert_parallel_on_two_gpus():
+    mp.spawn(_rank_main, args=(_port(), "ep"), nprocs=2, join=True)
+
+
+@pytest.mark.skipif(not _two_gpus(), reason="needs two GPUs")
+def test_context_parallel_on_two_gpus():
+    mp.spawn(_rank_main, args=(_port(), "cp"), nprocs=2, join=True)
