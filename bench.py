@@ -175,7 +175,7 @@ def main(argv=None):
     ap.add_argument("--ctx-min", type=int, default=1024, help="profiling override of config 2")
     ap.add_argument("--ctx-max", type=int, default=131072, help="profiling override of config 2")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host round trip leg")
-    ap.add_argument("--workload", default="decode", choices=["decode", "moe", "linear"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "moe", "linear", "longctx"])
     args = ap.parse_args(argv)
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -361,182 +361,341 @@ def _timed(torch, fn, steps, stream, inner=True):
     return start.elapsed_time(end), inner_ms
 
 
+def _reduce_max(torch, dist, world, device, *vals):
+    """Max over ranks of the given floats (device timings are taken as the slowest rank)."""
+    if world == 1:
+        return vals
+    t = torch.tensor(vals, device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return tuple(float(v) for v in t.tolist())
+
+
 def run_layer(args):
+    import datetime
+
     import torch
+    import torch.distributed as dist
 
     from hyperkernel_b200 import _lib as hk
+    from hyperkernel_b200 import parallel as par
     from hyperkernel_b200.clocks import ClockSampler
 
     world, rank, local = _dist()
-    if world > 1:
-        print(json.dumps({"workload": args.workload, "unavailable": "layer workloads run on one GPU"}))
-        return 0
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
     stream = torch.cuda.current_stream()
     gen = torch.Generator(device=device)
-    gen.manual_seed(7)
+    gen.manual_seed(7 + rank)
     hbm_peak, fp8_peak, peak_src = _peaks()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
     if args.workload == "moe":
-        T, E, H, I, K = MOE_T, MOE_E, MOE_H, MOE_I, MOE_K
-        w13 = _rand_e4m3(torch, (E, 2 * I, H), gen, device)
-        w2 = _rand_e4m3(torch, (E, H, I), gen, device)
-        s13 = torch.rand((E, 2 * I // 128, H // 128), generator=gen, device=device) * 1e-3
-        s2 = torch.rand((E, H // 128, I // 128), generator=gen, device=device) * 1e-3
-        sh13 = _rand_e4m3(torch, (1, 2 * I, H), gen, device)
-        sh2 = _rand_e4m3(torch, (1, H, I), gen, device)
-        shs13 = torch.rand((1, 2 * I // 128, H // 128), generator=gen, device=device) * 1e-3
-        shs2 = torch.rand((1, H // 128, I // 128), generator=gen, device=device) * 1e-3
-        x = torch.randn((T, H), generator=gen, device=device).to(torch.bfloat16)
-        logits = torch.randn((T, E), generator=gen, device=device)
-        rows = T * K
-        ws = torch.empty(hk.moe_workspace_size(rows, H, I), dtype=torch.uint8, device=device)
-        ws_sh = torch.empty(hk.moe_workspace_size(T, H, I), dtype=torch.uint8, device=device)
-        y = torch.empty((rows, H), dtype=torch.bfloat16, device=device)
-        y_sh = torch.empty((T, H), dtype=torch.bfloat16, device=device)
-        sh_off = torch.tensor([0, T], dtype=torch.int32, device=device)
-        sh_tok = torch.arange(T, dtype=torch.int32, device=device)
-
-        def step(x_in, logits_in, ev=None):
-            xq, sx = hk.quant_fp8(x_in)
-            ids, w = hk.route(logits_in, None, K, 1.0)
-            off, tok, pw, inv = hk.permute(ids, w, E)
-            if ev is not None:
-                ev[0].record(stream)
-            hk.moe_grouped(xq, sx, off, tok, rows, H, I, w13, s13, w2, s2, out=y, workspace=ws)
-            hk.moe_grouped(xq, sx, sh_off, sh_tok, T, H, I, sh13, shs13, sh2, shs2, out=y_sh, workspace=ws_sh)
-            if ev is not None:
-                ev[1].record(stream)
-            return hk.combine(y, pw, inv, y_sh, T, K), off
-
-        for _ in range(args.warmup):
-            _, off = step(x, logits)
-        torch.cuda.synchronize()
-        hk.check_errors()
-        counts = (off[1:] - off[:-1]).cpu().numpy()
-        hit = int((counts > 0).sum())
-        wbytes = (hit + 1) * 3 * H * I + (hit + 1) * (2 * I // 128 * H // 128 + H // 128 * I // 128) * 4
-        abytes = wbytes + (rows + T) * (H + 2 * 2 * I + 2 * H)  # x rows, h write+read, y write
-        flops = 2 * (rows + T) * 3 * H * I
-        sampler = ClockSampler(local).start()
-        launches0 = hk.kernel_launches()
-        t0 = time.perf_counter()
-        ms, ffn_ms = _timed(torch, lambda ev: step(x, logits, ev), args.steps, stream)
-        t1 = time.perf_counter()
-        launches = hk.kernel_launches() - launches0
-        sampler.stop()
-        clocks = sampler.summary(t0, t1)
-        hk.check_errors()
-        # end to end: pinned host activations and router logits in, the layer output back
-        hx = torch.empty((T, H), dtype=torch.bfloat16).pin_memory().copy_(x.cpu())
-        hl = torch.empty((T, E), dtype=torch.float32).pin_memory().copy_(logits.cpu())
-        hout = torch.empty((T, H), dtype=torch.bfloat16).pin_memory()
-        dx, dl = torch.empty_like(x), torch.empty_like(logits)
-
-        def e2e(ev):
-            dx.copy_(hx, non_blocking=True)
-            dl.copy_(hl, non_blocking=True)
-            out, _ = step(dx, dl)
-            hout.copy_(out, non_blocking=True)
-
-        e2e_ms, _ = _timed(torch, e2e, args.steps, stream, inner=False)
-        cpu = None if args.no_cpu_baseline else _moe_cpu_baseline(x, logits, w13, s13, w2, s2, sh13, shs13,
-                                                                   sh2, shs2)
-        value = T * args.steps / (ms / 1e3)
-        achieved = abytes / (ffn_ms / 1e3) / 1e9
-        line = {
-            "metric": "MoE layer tokens/s (config 4)", "value": value, "unit": "tokens/s", "n_gpus": 1,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "e4m3 x e4m3 -> f32",
-            "data": "synthetic (seeded): e4m3 weights, N(0,1) activations and router logits",
-            "config": {"workload": "config4: 512 tokens, 256 routed experts top-8 + 1 shared, hidden 7168, "
-                                   "inter 2048, FP8 128x128 block scales; quant+route+permute+grouped FFN+combine",
-                       "experts_hit": hit, "l2": "11.4 GB of expert weights per step, no flush"},
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                         "frac": achieved / hbm_peak, "traffic": None,
-                         "kernel": "grouped expert FFN (hk_moe_grouped: routed + shared)", "kernel_ms": ffn_ms,
-                         "algorithmic_bytes": abytes, "peak_source": peak_src,
-                         "tflops": flops / (ffn_ms / 1e3) / 1e12, "tensor_frac_of_fp8_peak":
-                             flops / (ffn_ms / 1e3) / 1e12 / fp8_peak},
-            "cpu_baseline": cpu,
-            "e2e": {"value": T * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
-                    "h2d_bytes_per_step": T * H * 2 + T * E * 4, "d2h_bytes_per_step": T * H * 2},
-            "gpu_launches": int(launches), "clocks": clocks,
-        }
+        line = _run_moe(args, torch, dist, hk, par, ClockSampler, world, rank, local, device, stream, gen,
+                        hbm_peak, fp8_peak, peak_src, barrier)
+    elif args.workload == "longctx":
+        line = _run_longctx(args, torch, dist, hk, par, ClockSampler, world, rank, local, device, stream, gen,
+                            hbm_peak, peak_src, barrier)
     else:
-        T = LINEAR_T
-        ws = {}
-        for name, n, k in LINEAR_PROJ:
-            ws[name] = (_rand_e4m3(torch, (n, k), gen, device),
-                        torch.rand(((n + 127) // 128, k // 128), generator=gen, device=device) * 1e-2)
-        x = torch.randn((T, 7168), generator=gen, device=device).to(torch.bfloat16)
-        attn = torch.randn((T, 128 * 128), generator=gen, device=device).to(torch.bfloat16)
-
-        def lin(a_bf16, name):
-            aq, sa = hk.quant_fp8(a_bf16)
-            w, sw = ws[name]
-            return hk.gemm_fp8(aq, sa, w, sw)
-
-        def step(x_in, attn_in, ev=None):
-            if ev is not None:
-                ev[0].record(stream)
-            qa = lin(x_in, "q_a")
-            qb = lin(qa, "q_b")
-            kva = lin(x_in, "kv_a")
-            o = lin(attn_in, "o")
-            if ev is not None:
-                ev[1].record(stream)
-            return qb, kva, o
-
-        for _ in range(args.warmup):
-            step(x, attn)
-        torch.cuda.synchronize()
-        hk.check_errors()
-        flops = sum(2 * T * n * k for _, n, k in LINEAR_PROJ)
-        sampler = ClockSampler(local).start()
-        launches0 = hk.kernel_launches()
-        t0 = time.perf_counter()
-        ms, lin_ms = _timed(torch, lambda ev: step(x, attn, ev), args.steps, stream)
-        t1 = time.perf_counter()
-        launches = hk.kernel_launches() - launches0
-        sampler.stop()
-        clocks = sampler.summary(t0, t1)
-        hk.check_errors()
-        hx = torch.empty_like(x, device="cpu").pin_memory().copy_(x.cpu())
-        ha = torch.empty_like(attn, device="cpu").pin_memory().copy_(attn.cpu())
-        outs = [torch.empty((T, n), dtype=torch.bfloat16).pin_memory() for nm, n, _k in LINEAR_PROJ if nm != "q_a"]
-        dx, da = torch.empty_like(x), torch.empty_like(attn)
-
-        def e2e(ev):
-            dx.copy_(hx, non_blocking=True)
-            da.copy_(ha, non_blocking=True)
-            for h, d in zip(outs, step(dx, da)):
-                h.copy_(d, non_blocking=True)
-
-        e2e_ms, _ = _timed(torch, e2e, args.steps, stream, inner=False)
-        cpu = None if args.no_cpu_baseline else _linear_cpu_baseline(x, attn, ws)
-        tflops = flops / (lin_ms / 1e3) / 1e12
-        line = {
-            "metric": "MLA FP8 projection tokens/s (config 3)", "value": T * args.steps / (ms / 1e3),
-            "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "e4m3 x e4m3 -> f32", "data": "synthetic (seeded)",
-            "config": {"workload": "config3: 4144 tokens (48 decode + 2 x 2048 prefill), projections "
-                                   "q_a 7168->1536, q_b 1536->24576, kv_a 7168->576, o 16384->7168, "
-                                   "activation quantisation included",
-                       "l2": "weights 60 MB and activations re-read from L2; no flush (tensor-bound)"},
-            "roofline": {"bound": "tensor", "achieved": tflops, "peak": fp8_peak, "unit": "TFLOP/s",
-                         "frac": tflops / fp8_peak, "traffic": None, "kernel": "hk_gemm_fp8 (+ hk_quant_fp8)",
-                         "kernel_ms": lin_ms, "algorithmic_flops": flops,
-                         "peak_source": f"{peak_src}: 2 x cuBLAS bf16 burst (dense FP8 = 2 x bf16)"},
-            "cpu_baseline": cpu,
-            "e2e": {"value": T * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
-                    "h2d_bytes_per_step": x.numel() * 2 + attn.numel() * 2,
-                    "d2h_bytes_per_step": T * sum(n for nm, n, _ in LINEAR_PROJ if nm != "q_a") * 2},
-            "gpu_launches": int(launches), "clocks": clocks,
-        }
-    print(json.dumps(line), flush=True)
+        line = _run_linear(args, torch, dist, hk, ClockSampler, world, rank, local, device, stream, gen,
+                           fp8_peak, peak_src, barrier)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
     return 0
+
+
+def _run_moe(args, torch, dist, hk, par, ClockSampler, world, rank, local, device, stream, gen, hbm_peak,
+             fp8_peak, peak_src, barrier):
+    """Config 4.  N > 1: expert parallel, rank r owning experts [r E/N, (r+1) E/N) and its own
+    512 tokens (weak scaling); dispatch and return are NCCL all-to-allv (hyperkernel_b200/
+    parallel.py), the shared expert is replicated."""
+    T, E, H, I, K = MOE_T, MOE_E, MOE_H, MOE_I, MOE_K
+    e0, e1 = par.expert_range(E, world, rank)
+    El = e1 - e0
+    w13 = _rand_e4m3(torch, (El, 2 * I, H), gen, device)
+    w2 = _rand_e4m3(torch, (El, H, I), gen, device)
+    s13 = torch.rand((El, 2 * I // 128, H // 128), generator=gen, device=device) * 1e-3
+    s2 = torch.rand((El, H // 128, I // 128), generator=gen, device=device) * 1e-3
+    sh13 = _rand_e4m3(torch, (1, 2 * I, H), gen, device)
+    sh2 = _rand_e4m3(torch, (1, H, I), gen, device)
+    shs13 = torch.rand((1, 2 * I // 128, H // 128), generator=gen, device=device) * 1e-3
+    shs2 = torch.rand((1, H // 128, I // 128), generator=gen, device=device) * 1e-3
+    x = torch.randn((T, H), generator=gen, device=device).to(torch.bfloat16)
+    logits = torch.randn((T, E), generator=gen, device=device)
+    rows = T * K
+    rows_max = rows * world  # the most rows one rank's experts can receive
+    ws = torch.empty(hk.moe_workspace_size(rows_max, H, I), dtype=torch.uint8, device=device)
+    ws_sh = torch.empty(hk.moe_workspace_size(T, H, I), dtype=torch.uint8, device=device)
+    y_buf = torch.empty((rows_max, H), dtype=torch.bfloat16, device=device)
+    y_sh = torch.empty((T, H), dtype=torch.bfloat16, device=device)
+    sh_off = torch.tensor([0, T], dtype=torch.int32, device=device)
+    sh_tok = torch.arange(T, dtype=torch.int32, device=device)
+    info = {}
+
+    def step(x_in, logits_in, ev=None):
+        xq, sx = hk.quant_fp8(x_in)
+        ids, w = hk.route(logits_in, None, K, 1.0)
+        off, tok, pw, inv = hk.permute(ids, w, E)
+        if world > 1:
+            xr, sr, loff, lperm, plan = par.ep_dispatch(xq, sx, off, tok, E)
+            n_in = xr.shape[0]
+            info["rows_in"] = n_in
+            info["hit"] = int((plan.recv_expert_counts.sum(0) > 0).sum())
+        if ev is not None:
+            ev[0].record(stream)
+        if world > 1:
+            y_local = hk.moe_grouped(xr, sr, loff, lperm, n_in, H, I, w13, s13, w2, s2, out=y_buf, workspace=ws)
+        else:
+            y_local = hk.moe_grouped(xq, sx, off, tok, rows, H, I, w13, s13, w2, s2, out=y_buf, workspace=ws)
+            info["rows_in"] = rows
+        hk.moe_grouped(xq, sx, sh_off, sh_tok, T, H, I, sh13, shs13, sh2, shs2, out=y_sh, workspace=ws_sh)
+        if ev is not None:
+            ev[1].record(stream)
+        y = par.ep_return(y_local, plan, lperm) if world > 1 else y_local
+        return hk.combine(y, pw, inv, y_sh, T, K), off
+
+    for _ in range(args.warmup):
+        _, off = step(x, logits)
+    torch.cuda.synchronize()
+    hk.check_errors()
+    if world == 1:
+        counts = (off[1:] - off[:-1]).cpu().numpy()
+        info["hit"] = int((counts > 0).sum())
+    hit, rows_in = info["hit"], info["rows_in"]
+    wbytes = (hit + 1) * 3 * H * I + (hit + 1) * (2 * I // 128 * H // 128 + H // 128 * I // 128) * 4
+    abytes = wbytes + (rows_in + T) * (H + 2 * 2 * I + 2 * H)
+    flops = 2 * (rows_in + T) * 3 * H * I
+    sampler = ClockSampler(local).start()
+    launches0 = hk.kernel_launches()
+    barrier()
+    t0 = time.perf_counter()
+    ms, ffn_ms = _timed(torch, lambda ev: step(x, logits, ev), args.steps, stream)
+    t1 = time.perf_counter()
+    barrier()
+    launches = hk.kernel_launches() - launches0
+    sampler.stop()
+    clocks = sampler.summary(t0, t1)
+    hk.check_errors()
+    ms, ffn_ms = _reduce_max(torch, dist, world, device, ms, ffn_ms)
+    hx = torch.empty((T, H), dtype=torch.bfloat16).pin_memory().copy_(x.cpu())
+    hl = torch.empty((T, E), dtype=torch.float32).pin_memory().copy_(logits.cpu())
+    hout = torch.empty((T, H), dtype=torch.bfloat16).pin_memory()
+    dx, dl = torch.empty_like(x), torch.empty_like(logits)
+
+    def e2e(ev):
+        dx.copy_(hx, non_blocking=True)
+        dl.copy_(hl, non_blocking=True)
+        out, _ = step(dx, dl)
+        hout.copy_(out, non_blocking=True)
+
+    barrier()
+    e2e_ms, _ = _timed(torch, e2e, args.steps, stream, inner=False)
+    (e2e_ms,) = _reduce_max(torch, dist, world, device, e2e_ms)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = _moe_cpu_baseline(x, logits, w13, s13, w2, s2, sh13, shs13, sh2, shs2)
+    achieved = abytes / (ffn_ms / 1e3) / 1e9
+    return {
+        "metric": "MoE layer tokens/s (config 4)", "value": T * world * args.steps / (ms / 1e3),
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "e4m3 x e4m3 -> f32",
+        "data": "synthetic (seeded): e4m3 weights, N(0,1) activations and router logits",
+        "config": {"workload": "config4: 512 tokens per GPU, 256 routed experts top-8 + 1 shared, hidden 7168, "
+                               "inter 2048, FP8 128x128 block scales; quant+route+permute+grouped FFN+combine",
+                   "parallelism": f"ep{world}" if world > 1 else "single",
+                   "experts_per_gpu": El, "experts_hit_rank0": hit, "rows_in_rank0": rows_in,
+                   "l2": "11.4 GB / N of expert weights per GPU per step, no flush"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                     "frac": achieved / hbm_peak, "traffic": None,
+                     "kernel": "grouped expert FFN on rank 0 (hk_moe_grouped: local experts + shared)",
+                     "kernel_ms": ffn_ms, "algorithmic_bytes": abytes, "peak_source": peak_src,
+                     "tflops": flops / (ffn_ms / 1e3) / 1e12,
+                     "tensor_frac_of_fp8_peak": flops / (ffn_ms / 1e3) / 1e12 / fp8_peak},
+        "cpu_baseline": cpu,
+        "e2e": {"value": T * world * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": T * H * 2 + T * E * 4, "d2h_bytes_per_step": T * H * 2},
+        "gpu_launches": int(launches), "clocks": clocks,
+    }
+
+
+def _run_longctx(args, torch, dist, hk, par, ClockSampler, world, rank, local, device, stream, gen, hbm_peak,
+                 peak_src, barrier):
+    """Config 5: one lane at 1M cached tokens and 7 at U[4K, 64K], each verifying 1 + 4 rows,
+    FP8 latent cache.  N > 1: the long lane's KV is split into page-aligned position ranges, one
+    per rank (context parallel), the short lanes go round-robin; every rank runs one partial
+    attention launch over its ranges, then the long lane's partials are all-gathered and merged
+    by LSE (strong scaling: the total work is fixed)."""
+    from hyperkernel_b200 import workload as W
+
+    lay = W.config5_layout(seed=0)
+    T, L, H = lay.num_tokens, lay.lanes, HEADS
+    kv = lay.kv_len.astype(np.int64)
+    begin = np.zeros(L, np.int32)
+    end = np.zeros(L, np.int32)
+    b0, e0 = par.cp_ranges(int(kv[0]), world)[rank]
+    begin[0], end[0] = b0, e0
+    for ln in range(1, L):
+        if (ln - 1) % world == rank:
+            end[ln] = kv[ln]
+    my_rows = int(sum(int(end[i]) - int(begin[i]) for i in range(L)))
+    cache = _rand_e4m3(torch, (lay.num_slots, DK), gen, device)
+    scales = torch.rand((lay.num_slots,), generator=gen, device=device) * 0.01 + 0.001
+    q = torch.randn((T, H, DK), generator=gen, device=device).to(torch.bfloat16)
+    kv_new = torch.randn((T, DK), generator=gen, device=device).to(torch.bfloat16)
+    lane_tokens = torch.from_numpy(lay.new_rows.astype(np.int32)).to(device)
+    lane_pos = torch.from_numpy(lay.context.astype(np.int32)).to(device)
+    bt = torch.from_numpy(lay.block_table).to(device)
+    kb = torch.from_numpy(begin).to(device)
+    ke = torch.from_numpy(end).to(device)
+    max_kv = int(kv.max())
+    scale = 1.0 / math.sqrt(DK)
+    long_rows = int(lay.new_rows[0]) * H
+
+    def step(ev=None):
+        pk = hk.pack(lane_tokens, lane_pos, bt, PAGE, lay.num_pages, T)
+        hk.kv_append_fp8(kv_new, pk["slot_mapping"], cache, scales)
+        if ev is not None:
+            ev[0].record(stream)
+        o, lse = hk.mla_partial_fp8(q, cache, scales, bt, pk["cu_seqlens"], pk["positions"], kb, ke, PAGE, max_kv,
+                                    scale)
+        if ev is not None:
+            ev[1].record(stream)
+        if world > 1:
+            return par.cp_merge(o.view(T * H, 512)[:long_rows], lse.view(T * H)[:long_rows])
+        return o, lse
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    hk.check_errors()
+    sampler = ClockSampler(local).start()
+    launches0 = hk.kernel_launches()
+    barrier()
+    t0 = time.perf_counter()
+    ms, attn_ms = _timed(torch, step, args.steps, stream)
+    t1 = time.perf_counter()
+    barrier()
+    launches = hk.kernel_launches() - launches0
+    sampler.stop()
+    clocks = sampler.summary(t0, t1)
+    hk.check_errors()
+    ms, attn_ms = _reduce_max(torch, dist, world, device, ms, attn_ms)
+    abytes = my_rows * (DK + 4) + T * H * (DK * 2 + 512 * 4 + 4)
+    (tot_bytes,) = _reduce_max(torch, dist, world, device, float(abytes))
+    achieved = abytes / (attn_ms / 1e3) / 1e9
+    flops = 2 * H * (DK + 512) * sum(int(end[i]) - int(begin[i]) for i in range(L)) * int(lay.new_rows[0])
+    return {
+        "metric": "long-context spec-verify rows/s (config 5)", "value": T * args.steps / (ms / 1e3),
+        "unit": "query rows/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "e4m3 KV, bf16 q, fp32 accumulation", "data": "synthetic (seeded)",
+        "config": {"workload": "config5: 1 lane at 1,048,576 + 7 at U[4K,64K] cached rows, 1+4 rows each, "
+                               "FP8 latent KV, 128 heads; pack+append+attention (+ LSE merge of the long "
+                               "lane's partials across GPUs)",
+                   "parallelism": f"cp{world}" if world > 1 else "single",
+                   "kv_rows_total": int(kv.sum()), "kv_rows_rank0": my_rows,
+                   "l2": "0.75 GB of FP8 KV, no flush"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                     "frac": achieved / hbm_peak, "traffic": None,
+                     "kernel": "partial attention on rank 0 (hk_mla_partial_fp8)", "kernel_ms": attn_ms,
+                     "algorithmic_bytes": abytes, "peak_source": peak_src,
+                     "tflops": flops / (attn_ms / 1e3) / 1e12},
+        "cpu_baseline": None,
+        "e2e": None,
+        "gpu_launches": int(launches), "clocks": clocks,
+    }
+
+
+def _run_linear(args, torch, dist, hk, ClockSampler, world, rank, local, device, stream, gen, fp8_peak,
+                peak_src, barrier):
+    """Config 3.  N > 1 runs independent replicas (the projections have no exchange here)."""
+    T = LINEAR_T
+    ws = {}
+    for name, n, k in LINEAR_PROJ:
+        ws[name] = (_rand_e4m3(torch, (n, k), gen, device),
+                    torch.rand(((n + 127) // 128, k // 128), generator=gen, device=device) * 1e-2)
+    x = torch.randn((T, 7168), generator=gen, device=device).to(torch.bfloat16)
+    attn = torch.randn((T, 128 * 128), generator=gen, device=device).to(torch.bfloat16)
+
+    def lin(a_bf16, name):
+        aq, sa = hk.quant_fp8(a_bf16)
+        w, sw = ws[name]
+        return hk.gemm_fp8(aq, sa, w, sw)
+
+    def step(x_in, attn_in, ev=None):
+        if ev is not None:
+            ev[0].record(stream)
+        qa = lin(x_in, "q_a")
+        qb = lin(qa, "q_b")
+        kva = lin(x_in, "kv_a")
+        o = lin(attn_in, "o")
+        if ev is not None:
+            ev[1].record(stream)
+        return qb, kva, o
+
+    for _ in range(args.warmup):
+        step(x, attn)
+    torch.cuda.synchronize()
+    hk.check_errors()
+    flops = sum(2 * T * n * k for _, n, k in LINEAR_PROJ)
+    sampler = ClockSampler(local).start()
+    launches0 = hk.kernel_launches()
+    barrier()
+    t0 = time.perf_counter()
+    ms, lin_ms = _timed(torch, lambda ev: step(x, attn, ev), args.steps, stream)
+    t1 = time.perf_counter()
+    barrier()
+    launches = hk.kernel_launches() - launches0
+    sampler.stop()
+    clocks = sampler.summary(t0, t1)
+    hk.check_errors()
+    ms, lin_ms = _reduce_max(torch, dist, world, device, ms, lin_ms)
+    hx = torch.empty_like(x, device="cpu").pin_memory().copy_(x.cpu())
+    ha = torch.empty_like(attn, device="cpu").pin_memory().copy_(attn.cpu())
+    outs = [torch.empty((T, n), dtype=torch.bfloat16).pin_memory() for nm, n, _k in LINEAR_PROJ if nm != "q_a"]
+    dx, da = torch.empty_like(x), torch.empty_like(attn)
+
+    def e2e(ev):
+        dx.copy_(hx, non_blocking=True)
+        da.copy_(ha, non_blocking=True)
+        for h, d in zip(outs, step(dx, da)):
+            h.copy_(d, non_blocking=True)
+
+    barrier()
+    e2e_ms, _ = _timed(torch, e2e, args.steps, stream, inner=False)
+    (e2e_ms,) = _reduce_max(torch, dist, world, device, e2e_ms)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = _linear_cpu_baseline(x, attn, ws)
+    tflops = flops / (lin_ms / 1e3) / 1e12
+    return {
+        "metric": "MLA FP8 projection tokens/s (config 3)", "value": T * world * args.steps / (ms / 1e3),
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "e4m3 x e4m3 -> f32", "data": "synthetic (seeded)",
+        "config": {"workload": "config3: 4144 tokens (48 decode + 2 x 2048 prefill), projections "
+                               "q_a 7168->1536, q_b 1536->24576, kv_a 7168->576, o 16384->7168, "
+                               "activation quantisation included",
+                   "parallelism": f"replicas{world}" if world > 1 else "single",
+                   "l2": "weights 60 MB and activations re-read from L2; no flush (tensor-bound)"},
+        "roofline": {"bound": "tensor", "achieved": tflops, "peak": fp8_peak, "unit": "TFLOP/s",
+                     "frac": tflops / fp8_peak, "traffic": None, "kernel": "hk_gemm_fp8 (+ hk_quant_fp8)",
+                     "kernel_ms": lin_ms, "algorithmic_flops": flops,
+                     "peak_source": f"{peak_src}: 2 x cuBLAS bf16 burst (dense FP8 = 2 x bf16)"},
+        "cpu_baseline": cpu,
+        "e2e": {"value": T * world * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": x.numel() * 2 + attn.numel() * 2,
+                "d2h_bytes_per_step": T * sum(n for nm, n, _ in LINEAR_PROJ if nm != "q_a") * 2},
+        "gpu_launches": int(launches), "clocks": clocks,
+    }
 
 
 def _moe_cpu_baseline(x, logits, w13, s13, w2, s2, sh13, shs13, sh2, shs2, sample_experts=6):
