@@ -176,6 +176,7 @@ def main(argv=None):
     ap.add_argument("--ctx-max", type=int, default=131072, help="profiling override of config 2")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host round trip leg")
     ap.add_argument("--workload", default="decode", choices=["decode", "moe", "linear", "longctx"])
+    ap.add_argument("--experts", type=int, default=None, help="profiling override of config 4's 256 experts")
     args = ap.parse_args(argv)
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -416,7 +417,7 @@ def _run_moe(args, torch, dist, hk, par, ClockSampler, world, rank, local, devic
     """Config 4.  N > 1: expert parallel, rank r owning experts [r E/N, (r+1) E/N) and its own
     512 tokens (weak scaling); dispatch and return are NCCL all-to-allv (hyperkernel_b200/
     parallel.py), the shared expert is replicated."""
-    T, E, H, I, K = MOE_T, MOE_E, MOE_H, MOE_I, MOE_K
+    T, E, H, I, K = MOE_T, args.experts or MOE_E, MOE_H, MOE_I, MOE_K
     e0, e1 = par.expert_range(E, world, rank)
     El = e1 - e0
     w13 = _rand_e4m3(torch, (El, 2 * I, H), gen, device)
