@@ -626,18 +626,18 @@ def _run_linear(args, torch, dist, hk, ClockSampler, world, rank, local, device,
     x = torch.randn((T, 7168), generator=gen, device=device).to(torch.bfloat16)
     attn = torch.randn((T, 128 * 128), generator=gen, device=device).to(torch.bfloat16)
 
-    def lin(a_bf16, name):
-        aq, sa = hk.quant_fp8(a_bf16)
+    def lin(aq_sa, name):
         w, sw = ws[name]
-        return hk.gemm_fp8(aq, sa, w, sw)
+        return hk.gemm_fp8(aq_sa[0], aq_sa[1], w, sw)
 
     def step(x_in, attn_in, ev=None):
         if ev is not None:
             ev[0].record(stream)
-        qa = lin(x_in, "q_a")
-        qb = lin(qa, "q_b")
-        kva = lin(x_in, "kv_a")
-        o = lin(attn_in, "o")
+        xq = hk.quant_fp8(x_in)  # shared by q_a and kv_a
+        qa = lin(xq, "q_a")
+        qb = lin(hk.quant_fp8(qa), "q_b")
+        kva = lin(xq, "kv_a")
+        o = lin(hk.quant_fp8(attn_in), "o")
         if ev is not None:
             ev[1].record(stream)
         return qb, kva, o

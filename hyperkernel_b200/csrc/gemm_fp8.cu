@@ -1,7 +1,7 @@
 // a11: FP8 block-scaled linear.
 //
-//  * hk_quant_fp8: bf16 activations -> e4m3 in 1x128 blocks (one warp per block, 8-byte
-//    loads, amax by warp shuffle).
+//  * hk_quant_fp8: bf16 activations -> e4m3 in 1x128 blocks (a half-warp per block,
+//    16-byte loads, amax by shuffle).
 //  * hk_gemm_fp8: y = sum_kb (xq . wq)_kb * sx * sw.  The portable kernel here runs on CUDA
 //    cores with an smem e4m3->fp32 table; the tcgen05 kernel (gemm_fp8_sm100.cu) takes over
 //    the shapes it supports.
@@ -12,25 +12,38 @@ namespace {
 
 constexpr int kBM = 64, kBN = 64, kBK = 128;
 
-__global__ void quant_fp8_kernel(const uint2* __restrict__ x, int64_t rows, int32_t k,
-                                 uint32_t* __restrict__ xq, float* __restrict__ sx) {
-  // One warp per (row, 128-block): each lane converts 4 consecutive values.
+__global__ void quant_fp8_kernel(const uint4* __restrict__ x, int64_t rows, int32_t k,
+                                 uint2* __restrict__ xq, float* __restrict__ sx) {
+  // One half-warp per (row, 128-block): each lane converts 8 consecutive values (16-byte load,
+  // 8-byte store); the block amax is reduced over the 16 lanes.
   const int64_t blocks_per_row = k / 128;
-  const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (w >= rows * blocks_per_row) return;
-  const int64_t r = w / blocks_per_row, kb = w % blocks_per_row;
-  const uint2 u = x[(r * k + kb * 128) / 4 + lane];
-  const float v[4] = {__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u),
-                      __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u)};
-  float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t w = t >> 4;
+  const int lane = threadIdx.x & 15;
+  const bool on = w < rows * blocks_per_row;  // whole half-warps are on or off together
+  const int64_t r = on ? w / blocks_per_row : 0, kb = on ? w % blocks_per_row : 0;
+  uint4 u = make_uint4(0, 0, 0, 0);
+  if (on) u = x[(r * k + kb * 128) / 8 + lane];
+  const uint32_t wd[4] = {u.x, u.y, u.z, u.w};
+  float v[8];
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = __uint_as_float(wd[i] << 16);
+    v[2 * i + 1] = __uint_as_float(wd[i] & 0xffff0000u);
+  }
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if (!on) return;
   const float s = __fdiv_rn(fmaxf(amax, 1e-12f), 448.0f);
-  uint32_t q = 0;
+  uint32_t lo = 0, hi = 0;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) q |= (uint32_t)f32_to_e4m3(__fdiv_rn(v[i], s)) << (8 * i);
-  xq[(r * k + kb * 128) / 4 + lane] = q;
+  for (int i = 0; i < 4; ++i) lo |= (uint32_t)f32_to_e4m3(__fdiv_rn(v[i], s)) << (8 * i);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) hi |= (uint32_t)f32_to_e4m3(__fdiv_rn(v[4 + i], s)) << (8 * i);
+  xq[(r * k + kb * 128) / 8 + lane] = make_uint2(lo, hi);
   if (lane == 0) sx[r * blocks_per_row + kb] = s;
 }
 
@@ -111,10 +124,10 @@ int gemm_fp8_portable(const uint8_t* xq, const float* sx, const uint8_t* wq, con
 
 int quant_fp8_launch(const uint16_t* x, int64_t rows, int32_t k, uint8_t* xq, float* sx,
                      cudaStream_t stream) {
-  const int64_t threads = rows * (k / 128) * 32;
+  const int64_t threads = rows * (k / 128) * 16;
   if (threads == 0) return HK_OK;
   quant_fp8_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(
-      (const uint2*)x, rows, k, (uint32_t*)xq, sx);
+      (const uint4*)x, rows, k, (uint2*)xq, sx);
   HK_TRY_LAUNCH("quant_fp8_kernel");
   return HK_OK;
 }
@@ -128,7 +141,7 @@ int hk_quant_fp8(const uint16_t* x, int64_t rows, int32_t k, uint8_t* xq, float*
   HK_TRY(hk::ensure_device());
   HK_REQUIRE(x && xq && sx, "hk_quant_fp8: null pointer");
   HK_REQUIRE(rows >= 0 && k > 0 && k % 128 == 0, "hk_quant_fp8: k %d must be a multiple of 128", k);
-  HK_REQUIRE(((uintptr_t)x % 8 == 0) && ((uintptr_t)xq % 4 == 0), "hk_quant_fp8: misaligned buffers");
+  HK_REQUIRE(((uintptr_t)x % 16 == 0) && ((uintptr_t)xq % 8 == 0), "hk_quant_fp8: misaligned buffers");
   return hk::quant_fp8_launch(x, rows, k, xq, sx, (cudaStream_t)stream);
 }
 
