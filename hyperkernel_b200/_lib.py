@@ -33,6 +33,7 @@ SIGNATURES = {
     "hk_pack": (C.c_int, [P, P, P, I32, I32, I32, I32, I32, P, P, P, P, P, P, P]),
     "hk_kv_append_bf16": (C.c_int, [P, P, I32, I32, I32, P, I64, P]),
     "hk_kv_append_fp8": (C.c_int, [P, P, I32, I32, P, P, I64, P]),
+    "hk_kv_dequant_fp8": (C.c_int, [P, P, I64, I32, I32, P, P]),
     "hk_kv_append_f32": (C.c_int, [P, P, P, I32, I32, P, P, I64, P]),
     "hk_gqa_decode_f32": (C.c_int, [P, P, P, P, I32, P, P, I32, I32, I32, I32, I32, I32, I64, F32, P, P, P]),
     "hk_mla_workspace_size": (SZ, [I32, I32, I32, I32]),
@@ -188,6 +189,16 @@ def kv_append_fp8(kv_new, slot_mapping, kv_cache, kv_scale, num_tokens=None, str
     n = kv_new.shape[0] if num_tokens is None else num_tokens
     call("hk_kv_append_fp8", ptr(kv_new), ptr(slot_mapping), n, kv_new.shape[-1], ptr(kv_cache),
          ptr(kv_scale), kv_cache.shape[0], stream_ptr(stream))
+
+
+def kv_dequant_fp8(kv_cache, kv_scale, page_rows=64, out=None, stream=None):
+    """The FP8 cache [slots][576] as the page-blocked bf16 cache of hk_mla_decode."""
+    slots, row = kv_cache.shape
+    if out is None:
+        out = torch.empty((slots, row), dtype=torch.bfloat16, device=kv_cache.device)
+    call("hk_kv_dequant_fp8", ptr(kv_cache), ptr(kv_scale), slots, row, page_rows, ptr(_u16(out)),
+         stream_ptr(stream))
+    return out
 
 
 def kv_append_f32(k_new, v_new, slot_mapping, k_cache, v_cache, stream=None):

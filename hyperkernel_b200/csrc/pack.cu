@@ -160,6 +160,32 @@ __global__ void append_kv_kernel(const uint4* __restrict__ k_src, const uint4* _
 }
 
 // e4m3 row quantisation: scale = max(amax, 1e-12) / 448, q = e4m3_rn_satfinite(x / scale).
+// FP8 rows -> the page-blocked bf16 layout: one warp per cache row, bf16(e4m3 * scale).
+__global__ void dequant_fp8_blocked_kernel(const uint2* __restrict__ src, const float* __restrict__ scales,
+                                           int64_t num_slots, int32_t row_vec, int32_t page_rows,
+                                           uint4* __restrict__ dst) {
+  const int64_t s = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (s >= num_slots) return;
+  const float sc = scales[s];
+  const uint2* in = src + s * row_vec;
+  uint4* page = dst + (s / page_rows) * page_rows * row_vec;
+  const int64_t r = s % page_rows;
+  for (int v = lane; v < row_vec; v += 32) {
+    const uint2 u = in[v];
+    const uint32_t b[2] = {u.x, u.y};
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t word = b[i >> 1] >> (16 * (i & 1));
+      const float lo = e4m3_to_f32((uint8_t)(word & 0xff)) * sc;
+      const float hi = e4m3_to_f32((uint8_t)((word >> 8) & 0xff)) * sc;
+      w[i] = (uint32_t)f32_to_bf16_bits(lo) | ((uint32_t)f32_to_bf16_bits(hi) << 16);
+    }
+    page[(int64_t)(v >> 3) * page_rows * 8 + r * 8 + (v & 7)] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
 __global__ void append_fp8_kernel(const uint4* __restrict__ src, const int32_t* __restrict__ slot,
                                   int32_t num_tokens, int32_t row_vec, uint2* __restrict__ cache,
                                   float* __restrict__ scales, int64_t num_slots,
@@ -248,6 +274,22 @@ int hk_kv_append_bf16(const uint16_t* kv_new, const int32_t* slot_mapping, int32
         (uint4*)kv_cache, num_slots, hk::err_word());
     HK_TRY_LAUNCH("append_blocked_kernel");
   }
+  return HK_OK;
+}
+
+int hk_kv_dequant_fp8(const uint8_t* kv_fp8, const float* kv_scale, int64_t num_slots, int32_t row_elems,
+                      int32_t page_rows, uint16_t* kv_bf16, void* stream) {
+  HK_TRY(hk::ensure_device());
+  HK_REQUIRE(kv_fp8 && kv_scale && kv_bf16, "hk_kv_dequant_fp8: null pointer");
+  HK_REQUIRE(num_slots >= 0 && page_rows > 0 && num_slots % page_rows == 0 && row_elems > 0 && row_elems % 64 == 0,
+             "hk_kv_dequant_fp8: num_slots %lld (a multiple of page_rows %d), row_elems %d (a multiple of 64)",
+             (long long)num_slots, page_rows, row_elems);
+  HK_REQUIRE(((uintptr_t)kv_fp8 % 8 == 0) && ((uintptr_t)kv_bf16 % 16 == 0), "hk_kv_dequant_fp8: misaligned buffers");
+  if (num_slots == 0) return HK_OK;
+  const int64_t threads = num_slots * 32;
+  dequant_fp8_blocked_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+      (const uint2*)kv_fp8, kv_scale, num_slots, row_elems / 8, page_rows, (uint4*)kv_bf16);
+  HK_TRY_LAUNCH("dequant_fp8_blocked_kernel");
   return HK_OK;
 }
 

@@ -98,6 +98,13 @@ int hk_kv_append_fp8(const uint16_t* kv_new, const int32_t* slot_mapping, int32_
                      int32_t row_elems, uint8_t* kv_cache, float* kv_scale, int64_t num_slots,
                      void* stream);
 
+/* The FP8 latent cache (row-major [num_slots][row_elems] e4m3 with one scale per row) as the
+ * page-blocked bf16 cache hk_mla_decode reads: element (slot, e) = bf16(e4m3(q) * scale[slot])
+ * at the blocked position of hk_kv_append_bf16.  num_slots a multiple of page_rows, row_elems a
+ * multiple of 64.  Lets FP8-stored KV use the tcgen05 bf16 attention kernel. */
+int hk_kv_dequant_fp8(const uint8_t* kv_fp8, const float* kv_scale, int64_t num_slots,
+                      int32_t row_elems, int32_t page_rows, uint16_t* kv_bf16, void* stream);
+
 /* GQA rows (config 1): k_new/v_new[T][kv_heads*head_dim] fp32 -> k_cache/v_cache[slot][..]. */
 int hk_kv_append_f32(const float* k_new, const float* v_new, const int32_t* slot_mapping,
                      int32_t num_tokens, int32_t row_elems, float* k_cache, float* v_cache,

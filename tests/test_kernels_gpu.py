@@ -394,3 +394,47 @@ def test_combine_matches_oracle(hk, orc, cuda):
     want = orc.combine(y, pw, inv, shared, T, K)
     out = hk.combine(bf16_dev(y, cuda), dev(pw, cuda), dev(inv, cuda), bf16_dev(shared, cuda), T, K)
     assert rel_err(to_np_bf16(out), want) <= 1e-2
+
+
+# ------------------------------------------------------------------------------------------
+# FP8 latent cache on the tensor-core kernel (config 5 shapes)
+# ------------------------------------------------------------------------------------------
+
+def test_kv_dequant_fp8_bit_exact(hk, orc, cuda):
+    rng = W.Rng(95)
+    slots = 64 * 5
+    q = rng.integers(0, 256, slots * 576).astype(np.uint8).reshape(slots, 576)
+    q[(q & 0x7F) == 0x7F] ^= 1  # no NaN encodings
+    sc = (rng.uniform(slots) * 0.01 + 1e-4).astype(np.float32)
+    lut = np.array([orc.e4m3_to_f32(v) for v in range(256)], np.float32)
+    rows = W.f32_to_bf16_bits((lut[q] * sc[:, None]).astype(np.float32))
+    want = np.zeros_like(rows)
+    for s in range(slots):  # page-blocked placement, as hk_kv_append_bf16 writes it
+        page, r = divmod(s, 64)
+        for blk in range(9):
+            base = (page * 576 * 64 + blk * 64 * 64 + r * 64)
+            want.reshape(-1)[base:base + 64] = rows[s, blk * 64:(blk + 1) * 64]
+    got = hk.kv_dequant_fp8(dev(q, cuda), dev(sc, cuda))
+    assert np.array_equal(got.view(torch.int16).cpu().numpy().view(np.uint16), want)
+
+
+def test_fp8_cache_through_the_tcgen05_kernel_matches_oracle(hk, orc, cuda):
+    """Config 5 shape (1 long lane + short lanes, 1 + 4 rows each, 128 heads, FP8 cache):
+    dequantise the pool to the blocked bf16 layout and run the tcgen05 kernel; compare with the
+    oracle's FP8 attention."""
+    lay, inp = _mla_case(seed=96, lanes=4, lo=600, hi=5000, heads=128, rows=5, long_ctx=40000)
+    T = lay.num_tokens
+    p = orc.pack(lay.new_rows, lay.context, lay.block_table, 64, lay.num_pages, T)
+    c8 = np.zeros((lay.num_slots, 576), np.uint8)
+    s8 = np.zeros(lay.num_slots, np.float32)
+    orc.kv_append_fp8(inp["kv_cache"], np.arange(lay.num_slots, dtype=np.int32), c8, s8)
+    want, want_lse = orc.mla_decode(inp["q"], lay.block_table, p["cu_seqlens"], p["positions"][:T],
+                                    64, inp["scale"], kv_fp8=c8, kv_scale=s8)
+    g = hk.pack(dev(lay.new_rows.astype(np.int32), cuda), dev(lay.context.astype(np.int32), cuda),
+                dev(lay.block_table, cuda), 64, lay.num_pages, T)
+    kv = hk.kv_dequant_fp8(dev(c8, cuda), dev(s8, cuda))
+    out, lse = hk.mla_decode(bf16_dev(inp["q"], cuda), kv, dev(lay.block_table, cuda), g["cu_seqlens"],
+                             g["positions"], 64, int(lay.kv_len.max()), inp["scale"], impl=2)
+    hk.check_errors()
+    assert rel_err(to_np_bf16(out), want) <= TOL
+    assert np.abs(lse.cpu().numpy() - want_lse).max() <= 1e-2
