@@ -50,6 +50,10 @@ SIGNATURES = {
     "hk_moe_grouped_noalloc": (C.c_int, [P, P, I32, P, P, I64, I32, I32, I32, P, P, P, P, P, P]),
     "hk_gather_rows": (C.c_int, [P, I64, P, I64, I32, P, P]),
     "hk_scatter_rows": (C.c_int, [P, I64, P, I64, I32, P, P]),
+    "hk_ep_counts": (C.c_int, [P, I32, I32, I32, P, P, C.c_uint32, I32, P, P, P, P]),
+    "hk_ep_dispatch": (C.c_int, [P, P, I32, P, P, I32, I32, I32, I32, I32, I32, P, P, P, P, P, C.c_uint32, P]),
+    "hk_ep_return": (C.c_int, [P, I32, I32, I32, I32, P, P, P, I32, I32, P, P, P, C.c_uint32, P]),
+    "hk_ep_wait": (C.c_int, [P, I32, I32, C.c_uint32, I32, P]),
     "hk_combine": (C.c_int, [P, I64, P, P, P, I32, I32, I32, P, P]),
     "hk_open": (C.c_int, [P, P]),
     "hk_close": (None, [P]),

@@ -24,6 +24,7 @@ exchange can be exercised with CPU tensors.
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 
 import numpy as np
@@ -156,3 +157,84 @@ def cp_merge(o_part, lse_part, group=None, merge=None):
     dist.all_gather_into_tensor(o_all, o_part.contiguous().view(-1), group=group)
     dist.all_gather_into_tensor(lse_all, lse_part.contiguous().view(-1), group=group)
     return merge(o_all.view((world,) + tuple(o_part.shape)), lse_all.view((world,) + tuple(lse_part.shape)))
+
+
+# ------------------------------------------------------------------------------------------
+# expert parallelism over NVLink peer memory
+# ------------------------------------------------------------------------------------------
+
+class EpPeer:
+    """Expert-parallel dispatch and return written straight into the other ranks' memory
+    (hk_ep_counts / hk_ep_dispatch / hk_ep_return over symmetric buffers), so a step needs no
+    host synchronisation and no NCCL call: the counts, the routed rows and the expert outputs
+    travel as NVLink stores from our kernels, and every rank waits on epoch flags with a bound.
+
+    The receive buffer comes out expert-major, so the grouped FFN runs over it with the
+    identity permutation.  Buffers are sized for `tokens` tokens per rank routed top_k ways."""
+
+    FLAGS_COUNTS, FLAGS_DISPATCH, FLAGS_RETURN = 0, 1, 2
+
+    def __init__(self, num_experts, tokens, top_k, hidden, group=None, timeout_us=2_000_000):
+        import torch.distributed._symmetric_memory as symm
+
+        self.group = group or dist.group.WORLD
+        self.world = dist.get_world_size(self.group)
+        self.rank = dist.get_rank(self.group)
+        self.E, self.H = num_experts, hidden
+        self.El = num_experts // self.world
+        self.back_cap = tokens * top_k
+        self.rows_cap = tokens * top_k * self.world
+        self.timeout_us = timeout_us
+        dev = torch.device("cuda", torch.cuda.current_device())
+
+        def sym(shape, dtype):
+            t = symm.empty(shape, dtype=dtype, device=dev)
+            h = symm.rendezvous(t, self.group)
+            ptrs = (ctypes.c_uint64 * self.world)(*[int(x) for x in h.buffer_ptrs])  # host array
+            return t, h, ptrs
+
+        self.counts, self._hc, self.counts_ptrs = sym((self.world * num_experts,), torch.int32)
+        self.flags, self._hf, self.flags_ptrs = sym((3 * 8,), torch.int32)
+        self.recv_x, self._hx, self.recv_x_ptrs = sym((self.rows_cap, hidden), torch.uint8)
+        self.recv_s, self._hs, self.recv_s_ptrs = sym((self.rows_cap, hidden // 128), torch.float32)
+        self.back_y, self._hb, self.back_y_ptrs = sym((self.back_cap, hidden), torch.bfloat16)
+        self.flags.zero_()
+        self.counts.zero_()
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        self.send_base = torch.zeros(num_experts, dtype=torch.int32, device=dev)
+        self.local_off = torch.zeros(self.El + 1, dtype=torch.int32, device=dev)
+        self.ret_base = torch.zeros(self.world * self.El, dtype=torch.int32, device=dev)
+        self.done = torch.zeros(2, dtype=torch.int32, device=dev)
+        self.identity = torch.arange(self.rows_cap, dtype=torch.int32, device=dev)
+        self.epoch = 0
+
+    def _wait(self, which, stream):
+        _lib.call("hk_ep_wait", _lib.ptr(self.flags), which, self.world, self.epoch, self.timeout_us,
+                  _lib.stream_ptr(stream))
+
+    def dispatch(self, xq, sx, offsets, perm_token, stream=None):
+        """Sends this rank's routed rows; returns (recv_x, recv_s, local_offsets, identity) for
+        the grouped FFN over this rank's experts, ready once the call's stream gets there."""
+        self.epoch = (self.epoch + 1) & 0x7FFFFFFF or 1
+        s = _lib.stream_ptr(stream)
+        _lib.call("hk_ep_counts", _lib.ptr(offsets), self.E, self.world, self.rank, ctypes.addressof(self.counts_ptrs),
+                  ctypes.addressof(self.flags_ptrs), self.epoch, self.timeout_us, _lib.ptr(self.send_base),
+                  _lib.ptr(self.local_off), _lib.ptr(self.ret_base), s)
+        rows = perm_token.shape[0]
+        _lib.call("hk_ep_dispatch", _lib.ptr(xq), _lib.ptr(sx), xq.shape[0], _lib.ptr(perm_token), _lib.ptr(offsets),
+                  rows, self.E, self.world, self.rank, self.H, self.rows_cap, _lib.ptr(self.send_base),
+                  ctypes.addressof(self.recv_x_ptrs), ctypes.addressof(self.recv_s_ptrs), ctypes.addressof(self.flags_ptrs),
+                  _lib.ptr(self.done[0:1]), self.epoch, s)
+        self._wait(self.FLAGS_DISPATCH, stream)
+        return self.recv_x, self.recv_s, self.local_off, self.identity
+
+    def give_back(self, y_local, stream=None):
+        """Returns the expert outputs (rows in the receive buffer's order) to their sources;
+        the result is this rank's routed rows in its permuted order (back_y)."""
+        s = _lib.stream_ptr(stream)
+        _lib.call("hk_ep_return", _lib.ptr(y_local), self.E, self.world, self.rank, self.H, _lib.ptr(self.local_off),
+                  _lib.ptr(self.counts), _lib.ptr(self.ret_base), self.back_cap, self.rows_cap,
+                  ctypes.addressof(self.back_y_ptrs), ctypes.addressof(self.flags_ptrs), _lib.ptr(self.done[1:2]), self.epoch, s)
+        self._wait(self.FLAGS_RETURN, stream)
+        return self.back_y

@@ -245,6 +245,40 @@ int hk_gather_rows(const void* src, int64_t src_rows, const int32_t* idx, int64_
 int hk_scatter_rows(const void* src, int64_t rows, const int32_t* idx, int64_t dst_rows,
                     int32_t row_bytes, void* dst, void* stream);
 
+/* Expert-parallel exchange over NVLink peer memory (no NCCL on the data path).  Rank r of
+ * `world` (<= 8) owns experts [r E/world, (r+1) E/world).  Buffer arguments named by rank are
+ * host arrays of `world` device addresses, element i = rank i's copy of a symmetric buffer
+ * mapped into this process: counts [world][E] int32, flags [3][8] uint32 (zero before the first step),
+ * recv_x [rows_cap][hidden] e4m3, recv_s [rows_cap][hidden/128] fp32, back_y [back_cap][hidden]
+ * bf16.  `epoch` is a nonzero step counter the caller increments every step; every wait is
+ * bounded by timeout_us and a timeout sets the device error word.
+ *   hk_ep_counts: exchanges per-expert row counts and computes send_base[E] (where this rank's
+ *     rows of expert e start in the owner's receive buffer, expert-major, sources in rank
+ *     order), local_off[E/world + 1] (the receive buffer's expert offsets) and
+ *     ret_base[world][E/world] (where source s's rows of a local expert sit in s's order).
+ *   hk_ep_dispatch: copies routed row p (xq[perm_token[p]] and its scales) straight into its
+ *     owner's receive buffer; raises the dispatch flag on every rank when done.
+ *   hk_ep_return: copies received row j of y (expert-major, local_off order) back into its
+ *     source's back_y at its permuted position; raises the return flag on every rank.
+ *   hk_ep_wait: waits until every rank raised flag set `which` (0 counts, 1 dispatch, 2 return)
+ *     in this rank's flags with the epoch.
+ * done_ctr: one zeroed device word per launch kind, private to this rank. */
+int hk_ep_counts(const int32_t* offsets, int32_t num_experts, int32_t world, int32_t rank,
+                 const uint64_t* counts, const uint64_t* flags, uint32_t epoch, int32_t timeout_us,
+                 int32_t* send_base, int32_t* local_off, int32_t* ret_base, void* stream);
+int hk_ep_dispatch(const uint8_t* xq, const float* sx, int32_t tokens, const int32_t* perm_token,
+                   const int32_t* offsets, int32_t rows, int32_t num_experts, int32_t world,
+                   int32_t rank, int32_t hidden, int32_t rows_cap, const int32_t* send_base,
+                   const uint64_t* recv_x, const uint64_t* recv_s, const uint64_t* flags,
+                   uint32_t* done_ctr, uint32_t epoch, void* stream);
+int hk_ep_return(const uint16_t* y, int32_t num_experts, int32_t world, int32_t rank,
+                 int32_t hidden, const int32_t* local_off, const int32_t* counts,
+                 const int32_t* ret_base, int32_t back_cap, int32_t rows_bound,
+                 const uint64_t* back_y, const uint64_t* flags, uint32_t* done_ctr,
+                 uint32_t epoch, void* stream);
+int hk_ep_wait(const uint32_t* flags, int32_t which, int32_t world, uint32_t epoch,
+               int32_t timeout_us, void* stream);
+
 /* out[t][hidden] bf16 = sum_k perm_weight[inv[t,k]] * y[inv[t,k]] (+ shared[t] when not
  * NULL), fp32 accumulation in k order; y has `rows` rows. */
 int hk_combine(const uint16_t* y, int64_t rows, const float* perm_weight, const int32_t* inv,

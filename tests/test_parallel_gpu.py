@@ -59,6 +59,8 @@ def _rank_main(rank, port, what):
     try:
         if what == "ep":
             _ep(rank, dev)
+        elif what == "ep_peer":
+            _ep_peer(rank, dev)
         else:
             _cp(rank, dev)
     finally:
@@ -88,6 +90,35 @@ def _ep(rank, dev):
     torch.cuda.synchronize()
     hk.check_errors()
     assert torch.equal(y_back.view(torch.int16), want.view(torch.int16)), f"rank {rank}: EP rows differ"
+
+
+def _ep_peer(rank, dev):
+    """The same expert-parallel step with dispatch and return as NVLink stores from libhk's
+    kernels (EpPeer): every routed row must come back bit-identical to the one-GPU result,
+    over several steps (the epoch flags advance)."""
+    from hyperkernel_b200 import _lib as hk
+    from hyperkernel_b200 import parallel as P
+
+    T, E, H, I, K = 64, 8, 512, 256, 4
+    inp = W.moe_inputs(T * 2, E, H, I, top_k=K, seed=93)
+    d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    w13, s13, w2, s2 = d(inp["w13"]), d(inp["s13"]), d(inp["w2"]), d(inp["s2"])
+    e0, e1 = P.expert_range(E, 2, rank)
+    lw = [t[e0:e1].contiguous() for t in (w13, s13, w2, s2)]
+    ep = P.EpPeer(E, T, K, H)
+    for step in range(3):
+        x = torch.from_numpy(inp["x"][rank * T:(rank + 1) * T].view(np.int16)).to(dev).view(torch.bfloat16)
+        logits = d(inp["logits"][rank * T:(rank + 1) * T]) * (1.0 + 0.1 * step)
+        ids, w = hk.route(logits, None, K, 1.0)
+        off, tok, pw, inv = hk.permute(ids, w, E)
+        xq, sx = hk.quant_fp8(x)
+        want = hk.moe_grouped(xq, sx, off, tok, T * K, H, I, w13, s13, w2, s2)[:T * K]
+        rx, rs, loff, ident = ep.dispatch(xq, sx, off, tok)
+        y_local = hk.moe_grouped(rx, rs, loff, ident, ep.rows_cap, H, I, *lw)
+        back = ep.give_back(y_local)
+        torch.cuda.synchronize()
+        hk.check_errors()
+        assert torch.equal(back[:T * K].view(torch.int16), want.view(torch.int16)), f"rank {rank} step {step}"
 
 
 def _cp(rank, dev):
@@ -128,3 +159,8 @@ def test_expert_parallel_on_two_gpus():
 @pytest.mark.skipif(not _two_gpus(), reason="needs two GPUs")
 def test_context_parallel_on_two_gpus():
     mp.spawn(_rank_main, args=(_port(), "cp"), nprocs=2, join=True)
+
+
+@pytest.mark.skipif(not _two_gpus(), reason="needs two GPUs")
+def test_expert_parallel_over_peer_memory_on_two_gpus():
+    mp.spawn(_rank_main, args=(_port(), "ep_peer"), nprocs=2, join=True)
