@@ -177,6 +177,8 @@ def main(argv=None):
     ap.add_argument("--no-e2e", action="store_true", help="skip the host round trip leg")
     ap.add_argument("--workload", default="decode", choices=["decode", "moe", "linear", "longctx"])
     ap.add_argument("--experts", type=int, default=None, help="profiling override of config 4's 256 experts")
+    ap.add_argument("--ep", default="peer", choices=["peer", "nccl"],
+                    help="expert-parallel exchange: NVLink stores from libhk kernels, or NCCL all-to-allv")
     args = ap.parse_args(argv)
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -438,38 +440,42 @@ def _run_moe(args, torch, dist, hk, par, ClockSampler, world, rank, local, devic
     y_sh = torch.empty((T, H), dtype=torch.bfloat16, device=device)
     sh_off = torch.tensor([0, T], dtype=torch.int32, device=device)
     sh_tok = torch.arange(T, dtype=torch.int32, device=device)
+    peer = par.EpPeer(E, T, K, H) if world > 1 and args.ep == "peer" else None
     info = {}
 
     def step(x_in, logits_in, ev=None):
         xq, sx = hk.quant_fp8(x_in)
         ids, w = hk.route(logits_in, None, K, 1.0)
         off, tok, pw, inv = hk.permute(ids, w, E)
-        if world > 1:
+        if peer is not None:
+            xr, sr, loff, lperm = peer.dispatch(xq, sx, off, tok)
+            n_in = peer.rows_cap
+        elif world > 1:
             xr, sr, loff, lperm, plan = par.ep_dispatch(xq, sx, off, tok, E)
             n_in = xr.shape[0]
-            info["rows_in"] = n_in
-            info["hit"] = int((plan.recv_expert_counts.sum(0) > 0).sum())
         if ev is not None:
             ev[0].record(stream)
         if world > 1:
             y_local = hk.moe_grouped(xr, sr, loff, lperm, n_in, H, I, w13, s13, w2, s2, out=y_buf, workspace=ws)
         else:
             y_local = hk.moe_grouped(xq, sx, off, tok, rows, H, I, w13, s13, w2, s2, out=y_buf, workspace=ws)
-            info["rows_in"] = rows
         hk.moe_grouped(xq, sx, sh_off, sh_tok, T, H, I, sh13, shs13, sh2, shs2, out=y_sh, workspace=ws_sh)
         if ev is not None:
             ev[1].record(stream)
-        y = par.ep_return(y_local, plan, lperm) if world > 1 else y_local
-        return hk.combine(y, pw, inv, y_sh, T, K), off
+        if peer is not None:
+            y = peer.give_back(y_local)
+        elif world > 1:
+            y = par.ep_return(y_local, plan, lperm)
+        else:
+            y = y_local
+        return hk.combine(y, pw, inv, y_sh, T, K), (loff if world > 1 else off)
 
     for _ in range(args.warmup):
         _, off = step(x, logits)
     torch.cuda.synchronize()
     hk.check_errors()
-    if world == 1:
-        counts = (off[1:] - off[:-1]).cpu().numpy()
-        info["hit"] = int((counts > 0).sum())
-    hit, rows_in = info["hit"], info["rows_in"]
+    counts = (off[1:] - off[:-1]).cpu().numpy()  # rows per expert this rank ran (local experts when N > 1)
+    hit, rows_in = int((counts > 0).sum()), int(counts.sum())
     wbytes = (hit + 1) * 3 * H * I + (hit + 1) * (2 * I // 128 * H // 128 + H // 128 * I // 128) * 4
     abytes = wbytes + (rows_in + T) * (H + 2 * 2 * I + 2 * H)
     flops = 2 * (rows_in + T) * 3 * H * I
@@ -511,7 +517,7 @@ def _run_moe(args, torch, dist, hk, par, ClockSampler, world, rank, local, devic
         "data": "synthetic (seeded): e4m3 weights, N(0,1) activations and router logits",
         "config": {"workload": "config4: 512 tokens per GPU, 256 routed experts top-8 + 1 shared, hidden 7168, "
                                "inter 2048, FP8 128x128 block scales; quant+route+permute+grouped FFN+combine",
-                   "parallelism": f"ep{world}" if world > 1 else "single",
+                   "parallelism": (f"ep{world} ({args.ep})" if world > 1 else "single"),
                    "experts_per_gpu": El, "experts_hit_rank0": hit, "rows_in_rank0": rows_in,
                    "l2": "11.4 GB / N of expert weights per GPU per step, no flush"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
