@@ -21,6 +21,9 @@ lanes per step scaled to the whole batch.
 JSON line: config 4 (MoE layer: quantise, route, permute, grouped FP8 expert FFN over 256
 routed experts + the shared expert, combine; 512 tokens, hidden 7168, inter 2048) and config 3
 (the MLA FP8 projections q_a, q_b, kv_a, o over the 4144-token mixed prefill + decode batch).
+--workload longctx measures config 5 (one lane at 1M cached rows plus 7 shorter ones, 1 + 4
+spec-verify rows each, FP8 latent cache); on N GPUs the long lane's KV is split by position
+(context parallel) and the partials merged by LSE.
 """
 from __future__ import annotations
 
@@ -537,9 +540,10 @@ def _run_longctx(args, torch, dist, hk, par, ClockSampler, world, rank, local, d
                  peak_src, barrier):
     """Config 5: one lane at 1M cached tokens and 7 at U[4K, 64K], each verifying 1 + 4 rows,
     FP8 latent cache.  N > 1: the long lane's KV is split into page-aligned position ranges, one
-    per rank (context parallel), the short lanes go round-robin; every rank runs one partial
-    attention launch over its ranges, then the long lane's partials are all-gathered and merged
-    by LSE (strong scaling: the total work is fixed)."""
+    per rank (context parallel), the short lanes go round-robin; every rank converts the pages
+    of its ranges to the blocked bf16 layout and runs one tcgen05 partial attention launch over
+    them (--attn-impl 1: the CUDA-core FP8 partial kernel instead), then the long lane's
+    partials are all-gathered and merged by LSE (strong scaling: the total work is fixed)."""
     from hyperkernel_b200 import workload as W
 
     lay = W.config5_layout(seed=0)
@@ -566,7 +570,12 @@ def _run_longctx(args, torch, dist, hk, par, ClockSampler, world, rank, local, d
     scale = 1.0 / math.sqrt(DK)
     long_rows = int(lay.new_rows[0]) * H
 
-    kv_bf16 = torch.empty((lay.num_slots, DK), dtype=torch.bfloat16, device=device) if world == 1 else None
+    portable = world > 1 and args.attn_impl == 1
+    kv_bf16 = None if portable else torch.empty((lay.num_slots, DK), dtype=torch.bfloat16, device=device)
+    # pages of this rank's ranges (the long lane's shard and its short lanes)
+    my_pages = torch.from_numpy(np.concatenate(
+        [lay.block_table[i, int(begin[i]) // PAGE:(int(end[i]) + PAGE - 1) // PAGE] for i in range(L)]
+    ).astype(np.int32)).to(device)
 
     def step(ev=None):
         pk = hk.pack(lane_tokens, lane_pos, bt, PAGE, lay.num_pages, T)
@@ -577,9 +586,12 @@ def _run_longctx(args, torch, dist, hk, par, ClockSampler, world, rank, local, d
             # one GPU: the FP8 pool as page-blocked bf16, then the tcgen05 kernel
             hk.kv_dequant_fp8(cache, scales, PAGE, out=kv_bf16)
             o, lse = hk.mla_decode(q, kv_bf16, bt, pk["cu_seqlens"], pk["positions"], PAGE, max_kv, scale)
-        else:
+        elif portable:
             o, lse = hk.mla_partial_fp8(q, cache, scales, bt, pk["cu_seqlens"], pk["positions"], kb, ke, PAGE,
                                         max_kv, scale)
+        else:
+            hk.kv_dequant_fp8(cache, scales, PAGE, out=kv_bf16, pages=my_pages)
+            o, lse = hk.mla_partial(q, kv_bf16, bt, pk["cu_seqlens"], pk["positions"], kb, ke, PAGE, max_kv, scale)
         if ev is not None:
             ev[1].record(stream)
         if world > 1:
@@ -620,7 +632,10 @@ def _run_longctx(args, torch, dist, hk, par, ClockSampler, world, rank, local, d
         "roofline": {"bound": "tensor", "achieved": tflops, "peak": bf16_peak, "unit": "TFLOP/s",
                      "frac": tflops / bf16_peak, "traffic": None,
                      "kernel": ("FP8 pool -> blocked bf16 (hk_kv_dequant_fp8) + tcgen05 attention (hk_mla_decode)"
-                                if world == 1 else "CUDA-core FP8 partial attention on rank 0 (hk_mla_partial_fp8)"),
+                                if world == 1 else
+                                "CUDA-core FP8 partial attention on rank 0 (hk_mla_partial_fp8)" if portable else
+                                "rank 0's FP8 pages -> blocked bf16 (hk_kv_dequant_fp8, page list) + tcgen05 "
+                                "partial attention (hk_mla_partial)"),
                      "kernel_ms": attn_ms, "algorithmic_flops": flops, "peak_source": f"{peak_src} bf16 burst",
                      "fp8_kv_gbs": abytes / (attn_ms / 1e3) / 1e9, "fp8_kv_frac_of_hbm": abytes / (attn_ms / 1e3) / 1e9 / hbm_peak},
         "cpu_baseline": None,

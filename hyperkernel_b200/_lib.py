@@ -33,13 +33,14 @@ SIGNATURES = {
     "hk_pack": (C.c_int, [P, P, P, I32, I32, I32, I32, I32, P, P, P, P, P, P, P]),
     "hk_kv_append_bf16": (C.c_int, [P, P, I32, I32, I32, P, I64, P]),
     "hk_kv_append_fp8": (C.c_int, [P, P, I32, I32, P, P, I64, P]),
-    "hk_kv_dequant_fp8": (C.c_int, [P, P, I64, I32, I32, P, P]),
+    "hk_kv_dequant_fp8": (C.c_int, [P, P, I64, I32, I32, P, I64, P, P]),
     "hk_kv_append_f32": (C.c_int, [P, P, P, I32, I32, P, P, I64, P]),
     "hk_gqa_decode_f32": (C.c_int, [P, P, P, P, I32, P, P, I32, I32, I32, I32, I32, I32, I64, F32, P, P, P]),
     "hk_mla_workspace_size": (SZ, [I32, I32, I32, I32]),
     "hk_mla_decode": (C.c_int, [P, P, P, I32, P, P, I32, I32, I32, I32, I64, I32, F32, P, P, P, SZ, I32, P]),
     "hk_mla_decode_fp8": (C.c_int, [P, P, P, P, I32, P, P, I32, I32, I32, I32, I64, I32, F32, P, P, P, SZ, P]),
     "hk_mla_partial_fp8": (C.c_int, [P, P, P, P, I32, P, P, P, P, I32, I32, I32, I32, I64, I32, F32, P, P, P, SZ, P]),
+    "hk_mla_partial": (C.c_int, [P, P, P, I32, P, P, P, P, I32, I32, I32, I32, I64, I32, F32, P, P, P, SZ, P]),
     "hk_lse_merge": (C.c_int, [P, P, I32, I64, I32, P, P, P]),
     "hk_quant_fp8": (C.c_int, [P, I64, I32, P, P, P]),
     "hk_gemm_fp8": (C.c_int, [P, P, P, P, I64, I32, I32, P, P]),
@@ -195,13 +196,15 @@ def kv_append_fp8(kv_new, slot_mapping, kv_cache, kv_scale, num_tokens=None, str
          ptr(kv_scale), kv_cache.shape[0], stream_ptr(stream))
 
 
-def kv_dequant_fp8(kv_cache, kv_scale, page_rows=64, out=None, stream=None):
-    """The FP8 cache [slots][576] as the page-blocked bf16 cache of hk_mla_decode."""
+def kv_dequant_fp8(kv_cache, kv_scale, page_rows=64, out=None, pages=None, stream=None):
+    """The FP8 cache [slots][576] as the page-blocked bf16 cache of hk_mla_decode (only the
+    pages listed in `pages`, an int32 device tensor, when given)."""
     slots, row = kv_cache.shape
     if out is None:
         out = torch.empty((slots, row), dtype=torch.bfloat16, device=kv_cache.device)
-    call("hk_kv_dequant_fp8", ptr(kv_cache), ptr(kv_scale), slots, row, page_rows, ptr(_u16(out)),
-         stream_ptr(stream))
+    n = 0 if pages is None else pages.shape[0]
+    call("hk_kv_dequant_fp8", ptr(kv_cache), ptr(kv_scale), slots, row, page_rows, ptr(pages), n,
+         ptr(_u16(out)), stream_ptr(stream))
     return out
 
 
@@ -273,6 +276,24 @@ def mla_partial_fp8(q, kv_cache, kv_scale, block_table, cu_seqlens, positions, k
          block_table.shape[1], ptr(cu_seqlens), ptr(positions), ptr(kv_begin), ptr(kv_end), L, T,
          H, page_size, kv_cache.shape[0], max_kv_len, scale, ptr(o), ptr(lse), ptr(workspace),
          workspace.numel(), stream_ptr(stream))
+    return o, lse
+
+
+def mla_partial(q, kv_cache, block_table, cu_seqlens, positions, kv_begin, kv_end, page_size, max_kv_len,
+                scale, stream=None):
+    """Partial attention of KV ranges on the tcgen05 kernel over the page-blocked bf16 cache:
+    fp32 o [T, H, 512] normalised within the range, lse [T, H] (-inf where it is empty)."""
+    T, H, _ = q.shape
+    dev = q.device
+    o = torch.empty((T, H, 512), dtype=torch.float32, device=dev)
+    lse = torch.empty((T, H), dtype=torch.float32, device=dev)
+    L = cu_seqlens.shape[0] - 1
+    ws = mla_workspace_size(L, T, H, max_kv_len)
+    workspace = torch.empty(max(ws, 16), dtype=torch.uint8, device=dev)
+    call("hk_mla_partial", ptr(q), ptr(_u16(kv_cache)), ptr(block_table), block_table.shape[1],
+         ptr(cu_seqlens), ptr(positions), ptr(kv_begin), ptr(kv_end), L, T, H, page_size,
+         kv_cache.shape[0], max_kv_len, scale, ptr(o), ptr(lse), ptr(workspace), workspace.numel(),
+         stream_ptr(stream))
     return o, lse
 
 

@@ -274,10 +274,13 @@ struct Params {
   int32_t bt_stride;
   const int32_t* cu;
   const int32_t* positions;
+  const int32_t* kv_begin;  // optional KV range per lane (context-parallel partials)
+  const int32_t* kv_end;
   int32_t num_lanes, num_tokens;
   int32_t num_pages;
   float scale_log2;
-  uint16_t* out;
+  uint16_t* out;            // bf16 output, or
+  float* out_f32;           // fp32 output (partials), when not null
   float* lse;
   float* part_o;
   float* part_lse;
@@ -285,8 +288,23 @@ struct Params {
   unsigned long long* err;
 };
 
+// KV rows [lo, hi) that row t of lane b attends: its causal prefix [0, pos], cut to the
+// lane's [kv_begin, kv_end) when a range is given.  hi <= lo: the row attends nothing.
+__device__ __forceinline__ void row_span(const int32_t* __restrict__ positions,
+                                         const int32_t* __restrict__ kv_begin,
+                                         const int32_t* __restrict__ kv_end, int t, int b,
+                                         int& lo, int& hi) {
+  lo = 0;
+  hi = positions[t] + 1;
+  if (kv_begin != nullptr) {
+    lo = max(0, kv_begin[b]);
+    hi = min(hi, kv_end[b]);
+  }
+}
+
 // ---------------------------------------------------------------------------------------
-// plan: tiles per row, their prefix, the cluster cut, and which rows need partials
+// plan: tiles per row, their prefix, the cluster cut, and which rows need partials.
+// A row's tiles start at the page holding its first KV row.
 // ---------------------------------------------------------------------------------------
 __device__ __forceinline__ int block_scan_excl(int v, int* sums, int* total) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
@@ -315,6 +333,10 @@ __device__ __forceinline__ int block_scan_excl(int v, int* sums, int* total) {
 }
 
 __global__ void __launch_bounds__(1024) mla_plan_kernel(const int32_t* __restrict__ positions,
+                                                        const int32_t* __restrict__ cu,
+                                                        int32_t num_lanes,
+                                                        const int32_t* __restrict__ kv_begin,
+                                                        const int32_t* __restrict__ kv_end,
                                                         int32_t T, int32_t clusters, Plan plan,
                                                         unsigned long long* err) {
   __shared__ int sums[32];
@@ -326,7 +348,10 @@ __global__ void __launch_bounds__(1024) mla_plan_kernel(const int32_t* __restric
     if (t < T) {
       const int pos = positions[t];
       if (pos < 0) hk_flag(err, hk::kErrAttnPage, (unsigned)t);
-      tiles = pos >= 0 ? (pos + kTileTok) / kTileTok : 0;
+      int lo, hi;
+      row_span(positions, kv_begin, kv_end, t, lane_of_row(cu, num_lanes, t), lo, hi);
+      const int base = lo - lo % kPage;
+      tiles = (pos >= 0 && hi > lo) ? (hi - base + kTileTok - 1) / kTileTok : 0;
     }
     int total;
     const int ex = block_scan_excl(tiles, sums, &total);
@@ -478,7 +503,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int a = max(c0, rts[t]) - rts[t], z = min(c1, rts[t + 1]) - rts[t];
         if (a >= z) continue;
         const int b = lane_of_row(prm.cu, prm.num_lanes, t);
-        const int row_pages = (prm.positions[t] + kPage) / kPage;
+        int lo, hi;
+        row_span(prm.positions, prm.kv_begin, prm.kv_end, t, b, lo, hi);
+        const int pg0 = lo / kPage;                        // page of the row's first KV row
+        const int row_pages = (hi + kPage - 1) / kPage;    // pages up to its last
         if (seg > 0 && !mbar_wait(bar(kBarQEmpty), (seg - 1) & 1, abort, prm.err, 1)) break;
         if (rank == 0) mbar_expect_tx(bar(kBarQFull), 2 * 9 * kBox);
         const uint32_t qbar = mapa_rank(bar(kBarQFull), 0);
@@ -487,7 +515,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         int prev[4] = {0, 0, 0, 0};
         for (int i = a; ok && i < z; ++i) {
           int cur[4];
-          for (int p = 0; p < 4; ++p) cur[p] = page_of(prm, b, 4 * i + p, row_pages);
+          for (int p = 0; p < 4; ++p) cur[p] = page_of(prm, b, pg0 + 4 * i + p, row_pages);
           for (int d = 0; d < 9 && ok; ++d) {
             uint32_t dst, fbar;
             if (!next_entry(dst, fbar)) { ok = false; break; }
@@ -595,7 +623,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = t_first; t < prm.num_tokens && rts[t] < c1; ++t) {
       const int a = max(c0, rts[t]) - rts[t], z = min(c1, rts[t + 1]) - rts[t];
       if (a >= z) continue;
-      const int kv_len = prm.positions[t] + 1;
+      int kv_lo, kv_len;
+      row_span(prm.positions, prm.kv_begin, prm.kv_end, t, lane_of_row(prm.cu, prm.num_lanes, t),
+               kv_lo, kv_len);
+      kv_len -= kv_lo - kv_lo % kPage;  // tile coordinates start at the first page
+      kv_lo %= kPage;                   // rows of the first page before the range
       float m_run = -INFINITY, l_part = 0.f;
       const int g_first = g;
       for (int i = a; i < z; ++i, ++g) {
@@ -613,10 +645,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lane == 0) mbar_arrive_leader(bar(kBarSFree + 8 * s), rank);
           const int tok0 = i * kTileTok + th * 128;
           const int valid = kv_len - tok0;  // tokens of this thread's 128 that exist
+          const int skip = tok0 == 0 ? kv_lo : 0;  // leading rows outside the range
+          if (skip == 0) {
 #pragma unroll
-          for (int k = 0; k < 128; ++k) {
-            v[k] = (k < valid) ? v[k] * prm.scale_log2 : -INFINITY;
-            mt = fmaxf(mt, v[k]);
+            for (int k = 0; k < 128; ++k) {
+              v[k] = (k < valid) ? v[k] * prm.scale_log2 : -INFINITY;
+              mt = fmaxf(mt, v[k]);
+            }
+          } else {
+#pragma unroll
+            for (int k = 0; k < 128; ++k) {
+              v[k] = (k >= skip && k < valid) ? v[k] * prm.scale_log2 : -INFINITY;
+              mt = fmaxf(mt, v[k]);
+            }
           }
         }
         float* xm = xmax + (g & 1) * 128;
@@ -701,8 +742,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         float o[32];
         tmem_ld32(tmem + lane_addr + kTmemO + 32 * c, o);
         const int dim0 = 256 * (c >> 2) + 128 * th + 32 * (c & 3);
-        if (split) {
-          float4* dst = reinterpret_cast<float4*>(prm.part_o + orow * kDV + dim0);
+        if (split || prm.out_f32 != nullptr) {
+          float4* dst = reinterpret_cast<float4*>((split ? prm.part_o : prm.out_f32) + orow * kDV + dim0);
 #pragma unroll
           for (int k = 0; k < 8; ++k)
             dst[k] = make_float4(o[4 * k] * inv, o[4 * k + 1] * inv, o[4 * k + 2] * inv,
@@ -749,12 +790,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // Merge of split rows: one CTA of 128 threads (4 dims each) per (row, head).
+// A row with no tile (its range is empty) gets o = 0 and lse = -inf here.
 __global__ void mla_merge_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse,
                                  Plan plan, int32_t T, uint16_t* __restrict__ out,
-                                 float* __restrict__ lse) {
+                                 float* __restrict__ out_f32, float* __restrict__ lse) {
   const int t = blockIdx.x / kHeads, h = blockIdx.x % kHeads;
   const int n = plan.n_split[t];
-  if (n <= 1) return;
+  if (n == 1) return;
   const int base = plan.split_base[t];
   float m = -INFINITY;
   for (int i = 0; i < n; ++i) m = fmaxf(m, part_lse[(int64_t)(base + i) * kHeads + h]);
@@ -771,13 +813,19 @@ __global__ void mla_merge_kernel(const float* __restrict__ part_o, const float* 
     acc.w = fmaf(w, o.w, acc.w);
   }
   const float inv = sum > 0.f ? 1.f / sum : 0.f;
-  uint2 pk;
-  __nv_bfloat162 a = __floats2bfloat162_rn(acc.x * inv, acc.y * inv);
-  __nv_bfloat162 b = __floats2bfloat162_rn(acc.z * inv, acc.w * inv);
-  pk.x = *reinterpret_cast<uint32_t*>(&a);
-  pk.y = *reinterpret_cast<uint32_t*>(&b);
-  reinterpret_cast<uint2*>(out + ((int64_t)t * kHeads + h) * kDV)[threadIdx.x] = pk;
-  if (threadIdx.x == 0) lse[(int64_t)t * kHeads + h] = sum > 0.f ? m + logf(sum) : -INFINITY;
+  const int64_t row = (int64_t)t * kHeads + h;
+  if (out_f32 != nullptr) {
+    reinterpret_cast<float4*>(out_f32 + row * kDV)[threadIdx.x] =
+        make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+  } else {
+    uint2 pk;
+    __nv_bfloat162 a = __floats2bfloat162_rn(acc.x * inv, acc.y * inv);
+    __nv_bfloat162 b = __floats2bfloat162_rn(acc.z * inv, acc.w * inv);
+    pk.x = *reinterpret_cast<uint32_t*>(&a);
+    pk.y = *reinterpret_cast<uint32_t*>(&b);
+    reinterpret_cast<uint2*>(out + row * kDV)[threadIdx.x] = pk;
+  }
+  if (threadIdx.x == 0) lse[row] = sum > 0.f ? m + logf(sum) : -INFINITY;
 }
 
 // ---------------------------------------------------------------------------------------
@@ -839,8 +887,9 @@ size_t mla_sm100_workspace(int32_t, int32_t num_tokens, int32_t heads, int32_t) 
 
 int mla_sm100(const uint16_t* q, const uint16_t* kv_cache, const int32_t* block_table,
               int32_t bt_stride, const int32_t* cu_seqlens, const int32_t* positions,
-              int32_t num_lanes, int32_t num_tokens, int32_t heads, int32_t page_size,
-              int64_t num_slots, int32_t max_kv_len, float scale, uint16_t* out, float* lse,
+              const int32_t* kv_begin, const int32_t* kv_end, int32_t num_lanes,
+              int32_t num_tokens, int32_t heads, int32_t page_size, int64_t num_slots,
+              int32_t max_kv_len, float scale, uint16_t* out, float* out_f32, float* lse,
               void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   (void)max_kv_len;
   const size_t need = mla_sm100_workspace(num_lanes, num_tokens, heads, max_kv_len);
@@ -871,7 +920,8 @@ int mla_sm100(const uint16_t* q, const uint16_t* kv_cache, const int32_t* block_
   HK_TRY(make_map_bf16(&q_map, q, (uint64_t)num_tokens * kHeads, kDK, 64));
   HK_TRY(make_map_bf16(&kv_map, kv_cache, (uint64_t)num_slots * 9, 64, 64));
 
-  mla_plan_kernel<<<1, 1024, 0, stream>>>(positions, num_tokens, clusters, plan, err_word());
+  mla_plan_kernel<<<1, 1024, 0, stream>>>(positions, cu_seqlens, num_lanes, kv_begin, kv_end,
+                                          num_tokens, clusters, plan, err_word());
   HK_TRY_LAUNCH("mla_plan_kernel");
 
   Params prm;
@@ -879,11 +929,14 @@ int mla_sm100(const uint16_t* q, const uint16_t* kv_cache, const int32_t* block_
   prm.bt_stride = bt_stride;
   prm.cu = cu_seqlens;
   prm.positions = positions;
+  prm.kv_begin = kv_begin;
+  prm.kv_end = kv_end;
   prm.num_lanes = num_lanes;
   prm.num_tokens = num_tokens;
   prm.num_pages = (int32_t)(num_slots / kPage);
   prm.scale_log2 = scale * 1.4426950408889634f;
   prm.out = out;
+  prm.out_f32 = out_f32;
   prm.lse = lse;
   prm.part_o = part_o;
   prm.part_lse = part_lse;
@@ -908,7 +961,7 @@ int mla_sm100(const uint16_t* q, const uint16_t* kv_cache, const int32_t* block_
   note_launch();
 
   mla_merge_kernel<<<(unsigned)(T * kHeads), kDV / 4, 0, stream>>>(part_o, part_lse, plan,
-                                                                   num_tokens, out, lse);
+                                                                   num_tokens, out, out_f32, lse);
   HK_TRY_LAUNCH("mla_merge_kernel");
   return HK_OK;
 }

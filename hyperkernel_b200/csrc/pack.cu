@@ -163,10 +163,20 @@ __global__ void append_kv_kernel(const uint4* __restrict__ k_src, const uint4* _
 // FP8 rows -> the page-blocked bf16 layout: one warp per cache row, bf16(e4m3 * scale).
 __global__ void dequant_fp8_blocked_kernel(const uint2* __restrict__ src, const float* __restrict__ scales,
                                            int64_t num_slots, int32_t row_vec, int32_t page_rows,
-                                           uint4* __restrict__ dst) {
-  const int64_t s = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+                                           const int32_t* __restrict__ pages, int64_t num_pages,
+                                           int64_t rows, uint4* __restrict__ dst, unsigned long long* err) {
+  const int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (s >= num_slots) return;
+  if (i >= rows) return;
+  int64_t s = i;  // cache row; with a page list, row i % page_rows of listed page i / page_rows
+  if (pages != nullptr) {
+    const int32_t pg = pages[i / page_rows];
+    if (pg < 0 || (int64_t)pg * page_rows >= num_slots || pg >= num_pages) {
+      if (lane == 0) hk_flag(err, hk::kErrAttnPage, (unsigned)(i / page_rows));
+      return;
+    }
+    s = (int64_t)pg * page_rows + i % page_rows;
+  }
   const float sc = scales[s];
   const uint2* in = src + s * row_vec;
   uint4* page = dst + (s / page_rows) * page_rows * row_vec;
@@ -278,17 +288,21 @@ int hk_kv_append_bf16(const uint16_t* kv_new, const int32_t* slot_mapping, int32
 }
 
 int hk_kv_dequant_fp8(const uint8_t* kv_fp8, const float* kv_scale, int64_t num_slots, int32_t row_elems,
-                      int32_t page_rows, uint16_t* kv_bf16, void* stream) {
+                      int32_t page_rows, const int32_t* pages, int64_t n_pages, uint16_t* kv_bf16,
+                      void* stream) {
   HK_TRY(hk::ensure_device());
   HK_REQUIRE(kv_fp8 && kv_scale && kv_bf16, "hk_kv_dequant_fp8: null pointer");
   HK_REQUIRE(num_slots >= 0 && page_rows > 0 && num_slots % page_rows == 0 && row_elems > 0 && row_elems % 64 == 0,
              "hk_kv_dequant_fp8: num_slots %lld (a multiple of page_rows %d), row_elems %d (a multiple of 64)",
              (long long)num_slots, page_rows, row_elems);
   HK_REQUIRE(((uintptr_t)kv_fp8 % 8 == 0) && ((uintptr_t)kv_bf16 % 16 == 0), "hk_kv_dequant_fp8: misaligned buffers");
-  if (num_slots == 0) return HK_OK;
-  const int64_t threads = num_slots * 32;
+  HK_REQUIRE(pages == nullptr || n_pages >= 0, "hk_kv_dequant_fp8: negative page count");
+  const int64_t rows = pages == nullptr ? num_slots : n_pages * page_rows;
+  if (rows == 0) return HK_OK;
+  const int64_t threads = rows * 32;
   dequant_fp8_blocked_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
-      (const uint2*)kv_fp8, kv_scale, num_slots, row_elems / 8, page_rows, (uint4*)kv_bf16);
+      (const uint2*)kv_fp8, kv_scale, num_slots, row_elems / 8, page_rows, pages, num_slots / page_rows, rows,
+      (uint4*)kv_bf16, hk::err_word());
   HK_TRY_LAUNCH("dequant_fp8_blocked_kernel");
   return HK_OK;
 }

@@ -101,9 +101,12 @@ int hk_kv_append_fp8(const uint16_t* kv_new, const int32_t* slot_mapping, int32_
 /* The FP8 latent cache (row-major [num_slots][row_elems] e4m3 with one scale per row) as the
  * page-blocked bf16 cache hk_mla_decode reads: element (slot, e) = bf16(e4m3(q) * scale[slot])
  * at the blocked position of hk_kv_append_bf16.  num_slots a multiple of page_rows, row_elems a
- * multiple of 64.  Lets FP8-stored KV use the tcgen05 bf16 attention kernel. */
+ * multiple of 64.  `pages` (device, n_pages ids; NULL = every page) restricts the conversion to
+ * the listed pages, written at their own positions.  Lets FP8-stored KV use the tcgen05 bf16
+ * attention kernel. */
 int hk_kv_dequant_fp8(const uint8_t* kv_fp8, const float* kv_scale, int64_t num_slots,
-                      int32_t row_elems, int32_t page_rows, uint16_t* kv_bf16, void* stream);
+                      int32_t row_elems, int32_t page_rows, const int32_t* pages, int64_t n_pages,
+                      uint16_t* kv_bf16, void* stream);
 
 /* GQA rows (config 1): k_new/v_new[T][kv_heads*head_dim] fp32 -> k_cache/v_cache[slot][..]. */
 int hk_kv_append_f32(const float* k_new, const float* v_new, const int32_t* slot_mapping,
@@ -160,6 +163,17 @@ int hk_mla_partial_fp8(const uint16_t* q, const uint8_t* kv_cache, const float* 
                        int32_t num_lanes, int32_t num_tokens, int32_t heads, int32_t page_size,
                        int64_t num_slots, int32_t max_kv_len, float scale, float* o_part,
                        float* lse_part, void* workspace, size_t workspace_bytes, void* stream);
+
+/* The same partial on the tcgen05 kernel, over the page-blocked bf16 cache of hk_mla_decode
+ * (128 heads, pages of 64 rows; an FP8 pool goes through hk_kv_dequant_fp8 first, restricted
+ * to the shard's pages).  kv_begin need not be page-aligned.  Workspace:
+ * hk_mla_workspace_size. */
+int hk_mla_partial(const uint16_t* q, const uint16_t* kv_cache, const int32_t* block_table,
+                   int32_t bt_stride, const int32_t* cu_seqlens, const int32_t* positions,
+                   const int32_t* kv_begin, const int32_t* kv_end, int32_t num_lanes,
+                   int32_t num_tokens, int32_t heads, int32_t page_size, int64_t num_slots,
+                   int32_t max_kv_len, float scale, float* o_part, float* lse_part,
+                   void* workspace, size_t workspace_bytes, void* stream);
 
 /* a10  LSE merge of n_parts partials: o_parts[n][rows][dv] fp32, lse_parts[n][rows]
  * -> out[rows][dv] bf16 and lse_out[rows]:  m = max lse_i,

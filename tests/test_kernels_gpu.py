@@ -438,3 +438,108 @@ def test_fp8_cache_through_the_tcgen05_kernel_matches_oracle(hk, orc, cuda):
     hk.check_errors()
     assert rel_err(to_np_bf16(out), want) <= TOL
     assert np.abs(lse.cpu().numpy() - want_lse).max() <= 1e-2
+
+
+def test_kv_dequant_fp8_page_list_converts_only_listed_pages(hk, cuda):
+    """With a page list the conversion writes exactly those pages, bit-identical to the full
+    conversion, and leaves every other page of the bf16 pool as it was."""
+    rng = W.Rng(97)
+    pages = 12
+    q = rng.integers(0, 256, pages * 64 * 576).astype(np.uint8).reshape(pages * 64, 576)
+    q[(q & 0x7F) == 0x7F] ^= 1
+    sc = (rng.uniform(pages * 64) * 0.01 + 1e-4).astype(np.float32)
+    full = hk.kv_dequant_fp8(dev(q, cuda), dev(sc, cuda))
+    mine = np.array([3, 7, 1, 11], np.int32)
+    out = torch.full((pages * 64, 576), 1.5, dtype=torch.bfloat16, device=cuda)
+    hk.kv_dequant_fp8(dev(q, cuda), dev(sc, cuda), out=out, pages=dev(mine, cuda))
+    hk.check_errors()
+    f = full.view(torch.int16).cpu().numpy().reshape(pages, -1)
+    o = out.view(torch.int16).cpu().numpy().reshape(pages, -1)
+    untouched = torch.full((1,), 1.5, dtype=torch.bfloat16).view(torch.int16).item()
+    for pg in range(pages):
+        if pg in mine:
+            assert np.array_equal(o[pg], f[pg]), pg
+        else:
+            assert (o[pg] == untouched).all(), pg
+
+
+def _range_case(kv_len, new_rows, seed):
+    """Per-lane KV ranges that exercise every edge of the range logic: the whole lane, an
+    unaligned start, an empty range, a range that starts inside the step's new rows (earlier
+    rows see nothing), and a page-aligned middle third."""
+    r = W.Rng(seed)
+    L = kv_len.shape[0]
+    b = np.zeros(L, np.int32)
+    e = np.zeros(L, np.int32)
+    for ln in range(L):
+        kv = int(kv_len[ln])
+        kind = ln % 5
+        if kind == 0:
+            b[ln], e[ln] = 0, kv
+        elif kind == 1:
+            b[ln] = 1 + int(r.integers(0, max(1, kv // 2), 1)[0])
+            e[ln] = kv - 1
+        elif kind == 2:
+            b[ln] = e[ln] = 0
+        elif kind == 3:
+            b[ln], e[ln] = kv - int(new_rows[ln]) // 2, kv
+        else:
+            b[ln], e[ln] = (kv // 3) // 64 * 64, 2 * kv // 3
+    return b, e
+
+
+def test_mla_tcgen05_partials_match_oracle(hk, orc, cuda):
+    """hk_mla_partial (tcgen05) restricted to per-lane KV ranges against the oracle's partial
+    attention: fp32 o normalised within the range, lse, and o = 0 / lse = -inf for rows whose
+    range holds nothing.  The long lane is split across several SM pairs."""
+    lay, inp = _mla_case(seed=98, lanes=10, lo=300, hi=3000, heads=128, rows=5, long_ctx=30000)
+    T = lay.num_tokens
+    p = orc.pack(lay.new_rows, lay.context, lay.block_table, 64, lay.num_pages, T)
+    b, e = _range_case(lay.kv_len, lay.new_rows, 99)
+    want, want_lse = orc.mla_decode(inp["q"], lay.block_table, p["cu_seqlens"], p["positions"][:T], 64,
+                                    inp["scale"], kv_bf16=inp["kv_cache"], kv_begin=b, kv_end=e)
+    o, lse = hk.mla_partial(bf16_dev(inp["q"], cuda), bf16_dev(inp["kv_cache"], cuda), dev(lay.block_table, cuda),
+                            dev(p["cu_seqlens"], cuda), dev(p["positions"][:T].copy(), cuda), dev(b, cuda),
+                            dev(e, cuda), 64, int(lay.kv_len.max()), inp["scale"])
+    hk.check_errors()
+    o, lse = o.cpu().numpy(), lse.cpu().numpy()
+    empty = np.isneginf(want_lse)
+    assert empty.any() and (~empty).any()
+    assert np.array_equal(np.isneginf(lse), empty)
+    assert (o[empty] == 0).all()
+    assert rel_err(o[~empty], want[~empty]) <= TOL
+    assert np.abs(lse[~empty] - want_lse[~empty]).max() <= 1e-3
+
+
+def test_tcgen05_context_parallel_shards_merge_to_whole(hk, orc, cuda):
+    """The context-parallel step on one GPU: 3 page-aligned shards per lane, each converted
+    from the FP8 pool by page list and attended by the tcgen05 kernel, merged by LSE, against
+    the oracle's whole-lane FP8 attention."""
+    lay, inp = _mla_case(seed=100, lanes=4, lo=500, hi=3000, heads=128, rows=5, long_ctx=20000)
+    T = lay.num_tokens
+    p = orc.pack(lay.new_rows, lay.context, lay.block_table, 64, lay.num_pages, T)
+    c8 = np.zeros((lay.num_slots, 576), np.uint8)
+    s8 = np.zeros(lay.num_slots, np.float32)
+    orc.kv_append_fp8(inp["kv_cache"], np.arange(lay.num_slots, dtype=np.int32), c8, s8)
+    want, want_lse = orc.mla_decode(inp["q"], lay.block_table, p["cu_seqlens"], p["positions"][:T],
+                                    64, inp["scale"], kv_fp8=c8, kv_scale=s8)
+    kv = lay.kv_len
+    cuts = [np.zeros_like(kv), (kv // 3) // 64 * 64, (2 * kv // 3) // 64 * 64, kv]
+    q = bf16_dev(inp["q"], cuda)
+    c8d, s8d = dev(c8, cuda), dev(s8, cuda)
+    bt = dev(lay.block_table, cuda)
+    parts, lses = [], []
+    for i in range(3):
+        mine = np.concatenate([lay.block_table[ln, cuts[i][ln] // 64:(cuts[i + 1][ln] + 63) // 64]
+                               for ln in range(lay.lanes)]).astype(np.int32)
+        kv_bf16 = torch.zeros((lay.num_slots, 576), dtype=torch.bfloat16, device=cuda)
+        hk.kv_dequant_fp8(c8d, s8d, out=kv_bf16, pages=dev(mine, cuda))
+        o, l = hk.mla_partial(q, kv_bf16, bt, dev(p["cu_seqlens"], cuda), dev(p["positions"][:T].copy(), cuda),
+                              dev(cuts[i].astype(np.int32), cuda), dev(cuts[i + 1].astype(np.int32), cuda), 64,
+                              int(kv.max()), inp["scale"])
+        parts.append(o.reshape(T * 128, 512))
+        lses.append(l.reshape(T * 128))
+    out, lse = hk.lse_merge(torch.stack(parts).contiguous(), torch.stack(lses).contiguous())
+    hk.check_errors()
+    assert rel_err(to_np_bf16(out), want.reshape(-1, 512)) <= TOL
+    assert np.abs(lse.cpu().numpy() - want_lse.ravel()).max() <= 1e-2
