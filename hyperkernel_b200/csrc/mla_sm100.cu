@@ -407,7 +407,8 @@ __device__ __forceinline__ int page_of(const Params& prm, int b, int pg, int row
 // ---------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(kThreads, 1)
     mla_decode_sm100_kernel(const __grid_constant__ CUtensorMap q_map,
-                            const __grid_constant__ CUtensorMap kv_map, Params prm) {
+                            const __grid_constant__ CUtensorMap kv_map,
+                            const __grid_constant__ CUtensorMap kv_map2, Params prm) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t rank = cluster_rank();
   const int cid = blockIdx.x / kClusterCTAs;
@@ -493,9 +494,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int p = 0; p < 4; ++p) {
             uint32_t dst, fbar;
             if (!next_entry(dst, fbar)) return false;
-            for (int aa = 0; aa < 2; ++aa)
-              tma_load_2d_pair(dst + aa * kBox, &kv_map, fbar, 0,
-                               (pages[p] * 9 + 4 * j + 2 * (int)rank + aa) * kPage);
+            // this SM's two V chunks of the page are adjacent blocks: one 16 KB box
+            tma_load_2d_pair(dst, &kv_map2, fbar, 0, (pages[p] * 9 + 4 * j + 2 * (int)rank) * kPage);
           }
         return true;
       };
@@ -533,21 +533,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ----------------------------------------------------------------- MMA issuer
     if (rank == 0 && lane == 0) {
-      const uint32_t q_s = smem_u32(smem + kOffQ);
-      const uint32_t p_s = smem_u32(smem + kOffP);
-      const uint32_t ring = smem_u32(smem + kOffRing);
-      int e = 0, g = 0, seg = 0;
+      // Operand descriptors are built once; per MMA only the start-address field (bits 0-13,
+      // address / 16) moves, and every shared address here stays below 2^18 bytes, so adding
+      // the offset / 16 to the whole descriptor never carries out of the field.
+      const uint64_t q_desc = sdesc_sw128(smem_u32(smem + kOffQ), 16, 1024);
+      const uint64_t p_desc = sdesc_sw128(smem_u32(smem + kOffP), 16, 1024);
+      const uint64_t k_desc = sdesc_sw128(smem_u32(smem + kOffRing), 16, 1024);
+      const uint64_t v_desc = sdesc_sw128(smem_u32(smem + kOffRing), kBox, 1024);
+      const uint32_t full0 = bar(kBarFull), empty0 = bar(kBarEmpty);
+      uint32_t slot = 0, phase = 0;  // ring position and parity of the next entry
+      int g = 0, seg = 0;
       bool ok = true;
       auto take_entry = [&](uint32_t& src) -> bool {
-        const int slot = e % kRing;
-        if (!mbar_wait(bar(kBarFull + 8 * slot), (e / kRing) & 1, abort, prm.err, 6)) return false;
+        if (!mbar_wait(full0 + 8 * slot, phase, abort, prm.err, 6)) return false;
         tc_fence_after();
-        src = ring + slot * kEntry;
+        src = slot * (kEntry >> 4);
         return true;
       };
       auto release_entry = [&]() {
-        umma_commit_pair(bar(kBarEmpty + 8 * (e % kRing)));
-        ++e;
+        umma_commit_pair(empty0 + 8 * slot);
+        if (++slot == kRing) {
+          slot = 0;
+          phase ^= 1;
+        }
       };
       auto issue_pv = [&](int gg, bool first, int seg_of) -> bool {
         const int s = gg & 1;
@@ -555,18 +563,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (first && seg_of > 0 && !mbar_wait(bar(kBarOFree), (seg_of - 1) & 1, abort, prm.err, 4))
           return false;
         tc_fence_after();
-        const uint32_t pb = p_s;
+#pragma unroll
         for (int j = 0; j < 2; ++j) {
+#pragma unroll
           for (int p = 0; p < 4; ++p) {
             uint32_t src;
             if (!take_entry(src)) return false;
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-              const uint64_t adesc = sdesc_sw128(pb + p * kPAtom + 32 * kk, 16, 1024);
-              const uint64_t bdesc = sdesc_sw128(src + kk * 2048, kBox, 1024);
-              umma_pair(tmem + kTmemO + 128 * j, adesc, bdesc, kIdescPV,
+            for (int kk = 0; kk < 4; ++kk)
+              umma_pair(tmem + kTmemO + 128 * j, p_desc + ((p * kPAtom + 32 * kk) >> 4),
+                        v_desc + src + ((kk * 2048) >> 4), kIdescPV,
                         (first && p == 0 && kk == 0) ? 0u : 1u);
-            }
             release_entry();
           }
         }
@@ -588,11 +595,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t src;
             if (!take_entry(src)) { ok = false; break; }
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const uint64_t adesc = sdesc_sw128(q_s + d * kBox + 32 * k, 16, 1024);
-              const uint64_t bdesc = sdesc_sw128(src + 32 * k, 16, 1024);
-              umma_pair(tmem + kTmemS + 128 * s, adesc, bdesc, kIdescQK, (d | k) ? 1u : 0u);
-            }
+            for (int k = 0; k < 4; ++k)
+              umma_pair(tmem + kTmemS + 128 * s, q_desc + ((d * kBox + 32 * k) >> 4),
+                        k_desc + src + ((32 * k) >> 4), kIdescQK, (d | k) ? 1u : 0u);
             release_entry();
           }
           if (!ok) break;
@@ -913,12 +918,13 @@ int mla_sm100(const uint16_t* q, const uint16_t* kv_cache, const int32_t* block_
   int clusters = sms / kClusterCTAs;
   if (clusters > kMaxClusters) clusters = kMaxClusters;
 
-  CUtensorMap q_map, kv_map;
+  CUtensorMap q_map, kv_map, kv_map2;
   // q: rows of 576 dims.  The page-blocked cache: every page is 9 blocks of 64 rows x 64 dims,
   // so as a 2-D array it is (num_slots * 9) rows of 64 dims; block d of page p starts at row
-  // (p * 9 + d) * 64 and one box is a contiguous 8 KB.
+  // (p * 9 + d) * 64 and one box is a contiguous 8 KB (kv_map2: two adjacent blocks, 16 KB).
   HK_TRY(make_map_bf16(&q_map, q, (uint64_t)num_tokens * kHeads, kDK, 64));
   HK_TRY(make_map_bf16(&kv_map, kv_cache, (uint64_t)num_slots * 9, 64, 64));
+  HK_TRY(make_map_bf16(&kv_map2, kv_cache, (uint64_t)num_slots * 9, 64, 128));
 
   mla_plan_kernel<<<1, 1024, 0, stream>>>(positions, cu_seqlens, num_lanes, kv_begin, kv_end,
                                           num_tokens, clusters, plan, err_word());
@@ -957,7 +963,7 @@ int mla_sm100(const uint16_t* q, const uint16_t* kv_cache, const int32_t* block_
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  HK_TRY_CUDA(cudaLaunchKernelEx(&cfg, mla_decode_sm100_kernel, q_map, kv_map, prm));
+  HK_TRY_CUDA(cudaLaunchKernelEx(&cfg, mla_decode_sm100_kernel, q_map, kv_map, kv_map2, prm));
   note_launch();
 
   mla_merge_kernel<<<(unsigned)(T * kHeads), kDV / 4, 0, stream>>>(part_o, part_lse, plan,
