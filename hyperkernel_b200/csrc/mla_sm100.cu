@@ -107,18 +107,21 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
                "r"(bytes)
                : "memory");
 }
-// Arrive on the barrier at the same offset in CTA 0 of the pair (local when rank 0).
+// Arrive on the barrier at the same offset in CTA 0 of the pair (local when rank 0).  The
+// arrive keeps the default CTA-scope release: a cluster-scope release measured ≈1,300-1,900
+// cycles per arrive here (it drains far more than the few shared-memory stores it orders),
+// against ≈30-100 for this form.  What it orders for the MMA is covered by the proxy and
+// tcgen05 fences the callers issue before it.
 __device__ __forceinline__ void mbar_arrive_leader(uint32_t bar, uint32_t rank) {
   const uint32_t remote = mapa_rank(bar, 0);
   (void)rank;
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote)
-               : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(remote) : "memory");
 }
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n.reg .pred p;\n"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
       "selp.u32 %0, 1, 0, p;\n}"
       : "=r"(ok)
       : "r"(bar), "r"(parity)
