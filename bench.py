@@ -138,25 +138,31 @@ def run_reference(args):
 
 
 def run_e2e(args, step, q, kv_new, lane_tokens, lane_pos, T, stream, barrier, world, device):
-    """Same step through MlaDecodeStep.step_host: pinned host inputs copied in and the output
-    copied out inside the timed region, every step."""
+    """Same steps through the public host-buffer API (hyperkernel_b200.step.HostPipeline):
+    every step copies its pinned host inputs in and its output out inside the timed region,
+    the copies overlapped with the neighbouring steps' kernels.  Timed from an event on the
+    input-copy stream before the first step to one on the output-copy stream after the last."""
     import torch
     import torch.distributed as dist
+    from hyperkernel_b200.step import HostPipeline
 
     q_h = q.cpu().pin_memory()
     kv_h = kv_new.cpu().pin_memory()
     lt_h = lane_tokens.cpu().pin_memory()
     lp_h = lane_pos.cpu().pin_memory()
-    out_h = torch.empty((T, HEADS, DV), dtype=torch.bfloat16).pin_memory()
-    for _ in range(args.warmup):
-        step.step_host(lt_h, lp_h, q_h, kv_h, out_h, T, stream)
+    out_h = [torch.empty((T, HEADS, DV), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    pipe = HostPipeline(step, stream)
+    for i in range(args.warmup):
+        pipe.submit(lt_h, lp_h, q_h, kv_h, out_h[i % 2], T)
+    pipe.finish()
     torch.cuda.synchronize()
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        step.step_host(lt_h, lp_h, q_h, kv_h, out_h, T, stream)
-    e1.record(stream)
+    e0.record(pipe.h2d)
+    for i in range(args.steps):
+        pipe.submit(lt_h, lp_h, q_h, kv_h, out_h[i % 2], T)
+    e1.record(pipe.d2h)
+    pipe.finish()
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)
     if world > 1:

@@ -543,3 +543,39 @@ def test_tcgen05_context_parallel_shards_merge_to_whole(hk, orc, cuda):
     hk.check_errors()
     assert rel_err(to_np_bf16(out), want.reshape(-1, 512)) <= TOL
     assert np.abs(lse.cpu().numpy() - want_lse.ravel()).max() <= 1e-2
+
+
+def test_host_pipeline_matches_serial_host_steps(hk, cuda):
+    """HostPipeline (copies overlapped with neighbouring steps) returns, step by step, the
+    same bits as MlaDecodeStep.step_host run one step at a time on one stream."""
+    from hyperkernel_b200.step import HostPipeline, MlaDecodeStep
+
+    lay = W.config2_layout(seed=7, lanes=12, lo=200, hi=3000)
+    T = lay.num_tokens
+    g = torch.Generator().manual_seed(3)
+    qs = [torch.randn((T, 128, 576), generator=g).to(torch.bfloat16).pin_memory() for _ in range(3)]
+    kvs = [torch.randn((T, 576), generator=g).to(torch.bfloat16).pin_memory() for _ in range(3)]
+    lt = torch.from_numpy(lay.new_rows.astype(np.int32)).pin_memory()
+    lp = torch.from_numpy(lay.context.astype(np.int32)).pin_memory()
+    cache0 = torch.randn((lay.num_slots, 576), generator=g).to(torch.bfloat16)
+    n = 7
+
+    def make():
+        return MlaDecodeStep(lay.block_table, lay.num_pages, 64, 128, 1 / 24.0, T, int(lay.kv_len.max()),
+                             cuda, cache=cache0.to(cuda))
+
+    serial = make()
+    want = []
+    for i in range(n):
+        o = torch.empty((T, 128, 512), dtype=torch.bfloat16).pin_memory()
+        serial.step_host(lt, lp, qs[i % 3], kvs[i % 3], o, T)
+        torch.cuda.synchronize()
+        want.append(o.clone())
+    pipe = HostPipeline(make())
+    got = [torch.empty((T, 128, 512), dtype=torch.bfloat16).pin_memory() for _ in range(n)]
+    for i in range(n):
+        pipe.submit(lt, lp, qs[i % 3], kvs[i % 3], got[i], T)
+    pipe.finish()
+    hk.check_errors()
+    for i in range(n):
+        assert torch.equal(got[i].view(torch.int16), want[i].view(torch.int16)), f"step {i}"
