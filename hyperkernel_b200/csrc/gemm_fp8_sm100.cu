@@ -73,17 +73,18 @@ constexpr int kStageBytes = kABytes + kBBytes;
 constexpr int kStages = 196608 / kStageBytes < 8 ? 196608 / kStageBytes : 8;
 constexpr int kOffCtl = kStages * kStageBytes;
 constexpr int kSmemBytes = kOffCtl + 1024;
-constexpr uint32_t kTmemCols = 2 * kBN;
+constexpr int kTBufs = 512 / kBN;                    // TMEM accumulators (all 512 columns)
+constexpr uint32_t kTmemCols = kTBufs * kBN;
 static_assert(kBN == 128 || kBN == 256, "tile width");
 static_assert(kLdCols == 16 || kLdCols == 32 || kLdCols == 64, "TMEM load width");
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 constexpr int kBarFull = 0;     // [kStages] TMA bytes of a stage landed
 constexpr int kBarEmpty = 64;   // [kStages] the stage's MMAs completed
-constexpr int kBarTFull = 128;  // [2] a TMEM accumulator holds a finished K block
-constexpr int kBarTEmpty = 144; // [2] every promotion warp has read it
-constexpr int kTmemSlot = 160;
-constexpr int kAbort = 164;
+constexpr int kBarTFull = 128;  // [kTBufs] a TMEM accumulator holds a finished K block
+constexpr int kBarTEmpty = 160; // [kTBufs] every promotion warp has read it
+constexpr int kTmemSlot = 192;
+constexpr int kAbort = 196;
 constexpr uint32_t kIdesc = idesc_e4m3(kBM, kBN);
 constexpr unsigned long long kDrainNs = 1000000000ull;
 
@@ -114,7 +115,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(ctl_u + kBarFull + 8 * s, 1);
       mbar_init(ctl_u + kBarEmpty + 8 * s, 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kTBufs; ++b) {
       mbar_init(ctl_u + kBarTFull + 8 * b, 1);
       mbar_init(ctl_u + kBarTEmpty + 8 * b, kEpiWarps);
     }
@@ -162,7 +163,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
         for (int kb = 0; kb < kblocks; ++kb) {
-          const int s = g % kStages, fill = g / kStages, buf = g & 1, use = g >> 1;
+          const int s = g % kStages, fill = g / kStages, buf = g % kTBufs, use = g / kTBufs;
           if (!mbar_wait(ctl_u + kBarFull + 8 * s, fill & 1, abort, p.err, 952) ||
               (use > 0 && !mbar_wait(ctl_u + kBarTEmpty + 8 * buf, (use - 1) & 1, abort, p.err, 953))) {
             ok = false;
@@ -184,7 +185,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (g > 0) {
         const int last = g - 1;
         const unsigned long long t0 = globaltimer();
-        while (!mbar_try_wait(ctl_u + kBarTFull + 8 * (last & 1), (last >> 1) & 1) &&
+        while (!mbar_try_wait(ctl_u + kBarTFull + 8 * (last % kTBufs), (last / kTBufs) & 1) &&
                globaltimer() - t0 < kDrainNs) {
         }
       }
@@ -208,7 +209,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int i = 0; i < 128; ++i) acc[i] = 0.f;
       float sc_next = use ? sxr[0] * swr[0] : 0.f;
       for (int kb = 0; kb < kblocks; ++kb) {
-        const int buf = g & 1, u = g >> 1;
+        const int buf = g % kTBufs, u = g / kTBufs;
         const float sc = sc_next;
         if (use && kb + 1 < kblocks) sc_next = sxr[kb + 1] * swr[kb + 1];
         bool ok = true;
