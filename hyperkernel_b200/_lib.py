@@ -7,12 +7,12 @@ sm_100 part, calls raise HKError.  torch is used only for device memory and stre
 from __future__ import annotations
 
 import ctypes as C
+import os
 import re
 from pathlib import Path
 
+import numpy as np
 import torch
-
-import os
 
 PKG = Path(__file__).resolve().parent
 # HK_LIB_PATH selects another build of the same library (A/B timing of kernel variants).
@@ -42,6 +42,8 @@ SIGNATURES = {
     "hk_mla_partial_fp8": (C.c_int, [P, P, P, P, I32, P, P, P, P, I32, I32, I32, I32, I64, I32, F32, P, P, P, SZ, P]),
     "hk_mla_partial": (C.c_int, [P, P, P, I32, P, P, P, P, I32, I32, I32, I32, I64, I32, F32, P, P, P, SZ, P]),
     "hk_lse_merge": (C.c_int, [P, P, I32, I64, I32, P, P, P]),
+    "hk_sample_workspace_size": (SZ, [I32, I32]),
+    "hk_sample_verify": (C.c_int, [P, I32, P, I32, I32, I32, P, P, P, I32, P, P, P, SZ, P]),
     "hk_quant_fp8": (C.c_int, [P, I64, I32, P, P, P]),
     "hk_gemm_fp8": (C.c_int, [P, P, P, P, I64, I32, I32, P, P]),
     "hk_route": (C.c_int, [P, P, I32, I32, I32, F32, P, P, P]),
@@ -295,6 +297,34 @@ def mla_partial(q, kv_cache, block_table, cu_seqlens, positions, kv_begin, kv_en
          kv_cache.shape[0], max_kv_len, scale, ptr(o), ptr(lse), ptr(workspace), workspace.numel(),
          stream_ptr(stream))
     return o, lse
+
+
+SAMPLING_DTYPE = np.dtype([("temperature", "<f4"), ("top_p", "<f4"), ("top_k", "<u4"),
+                           ("logprobs", "<u4"), ("seed", "<u8")])
+
+
+def sampling_array(samplings, device):
+    """hk_sampling[] on the device from dicts with temperature, top_p, top_k (logprobs, seed)."""
+    a = np.zeros(len(samplings), SAMPLING_DTYPE)
+    for i, sm in enumerate(samplings):
+        a[i] = (sm["temperature"], sm["top_p"], sm["top_k"], sm.get("logprobs", 0), sm.get("seed", 0))
+    return torch.from_numpy(a.view(np.uint8).copy()).to(device)
+
+
+def sample_verify(logits, cu_rows, sampling, state, drafts, block, n_logprobs, stream=None):
+    """Draws and verifies every lane's rows: returns (ids [lanes, block], lp [lanes, block,
+    2n+1]); `state` (uint64 stored as int64, one per lane) advances in place."""
+    rows, vocab = logits.shape
+    lanes = cu_rows.shape[0] - 1
+    dev = logits.device
+    ids = torch.empty((lanes, block), dtype=torch.int32, device=dev)
+    lp = torch.empty((lanes, block, 2 * n_logprobs + 1), dtype=torch.float32, device=dev)
+    ws = lib().hk_sample_workspace_size(rows, vocab)
+    workspace = torch.empty(ws, dtype=torch.uint8, device=dev)
+    call("hk_sample_verify", ptr(logits), vocab, ptr(cu_rows), lanes, rows, block, ptr(sampling), ptr(state),
+         ptr(drafts), n_logprobs, ptr(ids), ptr(lp) if n_logprobs > 0 else None, ptr(workspace),
+         workspace.numel(), stream_ptr(stream))
+    return ids, lp
 
 
 def lse_merge(o_parts, lse_parts, stream=None):

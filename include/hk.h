@@ -299,15 +299,8 @@ int hk_combine(const uint16_t* y, int64_t rows, const float* perm_weight, const 
                const uint16_t* shared, int32_t tokens, int32_t top_k, int32_t hidden,
                uint16_t* out, void* stream);
 
-/* ------------------------------------------------------------------------------------ */
-/* Kernel boundary: the reference's `Kernel` trait (src/gpu/mod.rs:42-46)                */
-/*   pools() -> hk_pools, push(&Share) -> hk_push, drain() -> hk_drain                   */
-/* Types mirror Share / Command / Event / Sampled (src/gpu/mod.rs:13-40) as flat arrays.  */
-/* ------------------------------------------------------------------------------------ */
-
-typedef struct hk_handle hk_handle;
-
-/* Sampling, src/engine/request.rs:142-149. */
+/* Sampling, src/engine/request.rs:31-37 (declared here for hk_sample_verify; the kernel
+ * boundary below carries it in hk_command). */
 typedef struct {
     float temperature;
     float top_p;
@@ -315,6 +308,33 @@ typedef struct {
     uint32_t logprobs;
     uint64_t seed;
 } hk_sampling;
+
+/* Spec-decode verification with on-device sampling (the reply side of the step,
+ * src/gpu/feed.rs:163-208).  Lane b's logits rows are cu_rows[b] .. cu_rows[b+1]-1 of
+ * logits[num_rows][vocab] (fp32; 1 + drafts rows, at most `block`).  Row j is drawn with
+ * sampling[b] (device array) and the lane's generator state[b] (device, advanced once per
+ * sampled draw; start it at the request's seed), and the chain continues to row j + 1 only
+ * while the token equals drafts[b][j] (drafts [num_lanes][block - 1]).  The draw restates the
+ * reference's source sampler (src/evo2/draw.rs:14-58): greedy (first greatest logit) when
+ * temperature <= 0 or top_k == 1, else top-k, softmax at the temperature in f64, top-p tail
+ * cut, u = splitmix64(state) / 2^53 * kept.  ids [num_lanes][block]: the accepted tokens then
+ * -2; a row with a non-finite logit gives -1 and ends the lane.  lp [num_lanes][block]
+ * [2 n_logprobs + 1] (may be NULL when n_logprobs = 0): per token, the n_logprobs best
+ * (id, logprob) pairs of the row's log-softmax (id -1 past the vocabulary), then the token's
+ * own logprob.  vocab <= 4,194,304; workspace 256-byte aligned, hk_sample_workspace_size. */
+size_t hk_sample_workspace_size(int32_t num_rows, int32_t vocab);
+int hk_sample_verify(const float* logits, int32_t vocab, const int32_t* cu_rows, int32_t num_lanes,
+                     int32_t num_rows, int32_t block, const hk_sampling* sampling, uint64_t* state,
+                     const int32_t* drafts, int32_t n_logprobs, int32_t* ids, float* lp,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------------------ */
+/* Kernel boundary: the reference's `Kernel` trait (src/gpu/mod.rs:42-46)                */
+/*   pools() -> hk_pools, push(&Share) -> hk_push, drain() -> hk_drain                   */
+/* Types mirror Share / Command / Event / Sampled (src/gpu/mod.rs:13-40) as flat arrays.  */
+/* ------------------------------------------------------------------------------------ */
+
+typedef struct hk_handle hk_handle;
 
 #define HK_CMD_END 0    /* End { lane } */
 #define HK_CMD_PAGES 1  /* Pages { lane, from, upto, row } */

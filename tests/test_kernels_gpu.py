@@ -579,3 +579,53 @@ def test_host_pipeline_matches_serial_host_steps(hk, cuda):
     hk.check_errors()
     for i in range(n):
         assert torch.equal(got[i].view(torch.int16), want[i].view(torch.int16)), f"step {i}"
+
+
+# ------------------------------------------------------------------------------------------
+# spec-decode verification with on-device sampling
+# ------------------------------------------------------------------------------------------
+
+def _sample_case(vocab, seed):
+    from oracle import sample as S
+
+    rng = np.random.default_rng(seed)
+    block = 5
+    rows_per_lane = [5, 3, 1, 5, 2, 5, 4]
+    samplings = [dict(temperature=0.0, top_k=0, top_p=1.0), dict(temperature=0.7, top_k=50, top_p=1.0),
+                 dict(temperature=1.0, top_k=0, top_p=0.9), dict(temperature=1.3, top_k=0, top_p=1.0),
+                 dict(temperature=0.8, top_k=20, top_p=0.5), dict(temperature=1.0, top_k=1, top_p=1.0),
+                 dict(temperature=0.9, top_k=0, top_p=0.6)]
+    cu = np.concatenate([[0], np.cumsum(rows_per_lane)]).astype(np.int32)
+    logits = (rng.standard_normal((cu[-1], vocab)) * 2.0).astype(np.float32)
+    logits[cu[6] + 2, vocab // 3] = np.inf               # lane 6 meets a non-finite row
+    states = [int(v) for v in rng.integers(0, 2**63, len(rows_per_lane))]
+    states[3] |= 1 << 63
+    # drafts that the oracle's own draws accept up to a per-lane depth
+    depth = [4, 1, 0, 2, 4, 3, 3]
+    drafts = np.full((len(rows_per_lane), block - 1), -7, np.int32)
+    for j in range(block - 1):
+        ids, _, _ = S.sample_verify(logits, cu, samplings, states, drafts, block, 0)
+        for b in range(len(rows_per_lane)):
+            if j < depth[b] and ids[b, j] >= 0:
+                drafts[b, j] = ids[b, j]
+    return logits, cu, samplings, states, drafts, block
+
+
+@pytest.mark.parametrize("vocab,seed,n", [(5000, 1, 4), (129280, 2, 8), (37, 3, 40)])
+def test_sample_verify_matches_oracle(hk, cuda, vocab, seed, n):
+    """Accepted ids and generator states bit-exact, logprob rows within 1e-5, for greedy,
+    top-k, top-p and plain temperature lanes, partial chains, a non-finite row and more
+    logprob pairs than the vocabulary."""
+    from oracle import sample as S
+
+    logits, cu, samplings, states, drafts, block = _sample_case(vocab, seed)
+    want_ids, want_lp, want_states = S.sample_verify(logits, cu, samplings, states, drafts, block, n)
+    st = torch.tensor(np.array(states, dtype=np.uint64).view(np.int64), device=cuda)
+    ids, lp = hk.sample_verify(dev(logits, cuda), dev(cu, cuda), hk.sampling_array(samplings, cuda), st,
+                               dev(drafts, cuda), block, n)
+    hk.check_errors()
+    assert np.array_equal(ids.cpu().numpy(), want_ids)
+    assert st.cpu().numpy().view(np.uint64).tolist() == [s & ((1 << 64) - 1) for s in want_states]
+    got = lp.cpu().numpy()
+    assert np.array_equal(got[..., 0:-1:2], want_lp[..., 0:-1:2])      # the ids of the pairs
+    assert np.abs(got - want_lp).max() <= 1e-5
