@@ -184,7 +184,7 @@ def main(argv=None):
     ap.add_argument("--ctx-min", type=int, default=1024, help="profiling override of config 2")
     ap.add_argument("--ctx-max", type=int, default=131072, help="profiling override of config 2")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host round trip leg")
-    ap.add_argument("--workload", default="decode", choices=["decode", "moe", "linear", "longctx"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "moe", "linear", "longctx", "sample"])
     ap.add_argument("--experts", type=int, default=None, help="profiling override of config 4's 256 experts")
     ap.add_argument("--ep", default="peer", choices=["peer", "nccl"],
                     help="expert-parallel exchange: NVLink stores from libhk kernels, or NCCL all-to-allv")
@@ -412,6 +412,9 @@ def run_layer(args):
     elif args.workload == "longctx":
         line = _run_longctx(args, torch, dist, hk, par, ClockSampler, world, rank, local, device, stream, gen,
                             hbm_peak, peak_src, barrier)
+    elif args.workload == "sample":
+        line = _run_sample(args, torch, dist, hk, ClockSampler, world, rank, local, device, stream, gen,
+                           hbm_peak, peak_src, barrier)
     else:
         line = _run_linear(args, torch, dist, hk, ClockSampler, world, rank, local, device, stream, gen,
                            fp8_peak, peak_src, barrier)
@@ -732,6 +735,107 @@ def _run_linear(args, torch, dist, hk, ClockSampler, world, rank, local, device,
                 "d2h_bytes_per_step": T * sum(n for nm, n, _ in LINEAR_PROJ if nm != "q_a") * 2},
         "gpu_launches": int(launches), "clocks": clocks,
     }
+
+
+SAMPLE_VOCAB = 129280
+SAMPLE_LANES, SAMPLE_BLOCK, SAMPLE_LOGPROBS = 8, 5, 20
+SAMPLE_MIX = [dict(temperature=0.0, top_k=0, top_p=1.0), dict(temperature=0.7, top_k=50, top_p=1.0),
+              dict(temperature=1.0, top_k=0, top_p=0.9), dict(temperature=0.8, top_k=0, top_p=1.0)]
+
+
+def _run_sample(args, torch, dist, hk, ClockSampler, world, rank, local, device, stream, gen, hbm_peak,
+                peak_src, barrier):
+    """Spec-decode verification with on-device sampling at config 5's shape: 8 lanes x (1 + 4)
+    rows of fp32 logits over a 129,280-token vocabulary, 20 logprob pairs per token, lanes
+    cycling greedy / top-k 50 / top-p 0.9 / plain temperature.  Drafts are each row's greedy
+    token, so greedy lanes accept every draft.  N > 1: independent replicas."""
+    V, L, B, n = SAMPLE_VOCAB, SAMPLE_LANES, SAMPLE_BLOCK, SAMPLE_LOGPROBS
+    rows = L * B
+    logits = torch.randn((rows, V), generator=gen, device=device) * 2.0
+    cu = torch.arange(0, rows + 1, B, dtype=torch.int32, device=device)
+    samplings = [SAMPLE_MIX[i % len(SAMPLE_MIX)] for i in range(L)]
+    smp = hk.sampling_array(samplings, device)
+    seeds = torch.arange(1, L + 1, dtype=torch.int64, device=device) * 7919
+    state = seeds.clone()
+    drafts = logits.view(L, B, V).argmax(dim=2)[:, :B - 1].to(torch.int32).contiguous()
+
+    def step(ev=None, lg=None):
+        if ev is not None:
+            ev[0].record(stream)
+        out = hk.sample_verify(logits if lg is None else lg, cu, smp, state, drafts, B, n, stream)
+        if ev is not None:
+            ev[1].record(stream)
+        return out
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    hk.check_errors()
+    sampler = ClockSampler(local).start()
+    launches0 = hk.kernel_launches()
+    barrier()
+    t0 = time.perf_counter()
+    ms, k_ms = _timed(torch, step, args.steps, stream)
+    t1 = time.perf_counter()
+    barrier()
+    launches = hk.kernel_launches() - launches0
+    sampler.stop()
+    clocks = sampler.summary(t0, t1)
+    hk.check_errors()
+    ms, k_ms = _reduce_max(torch, dist, world, device, ms, k_ms)
+    h_logits = torch.empty((rows, V), dtype=torch.float32).pin_memory().copy_(logits.cpu())
+    d_logits = torch.empty_like(logits)
+    h_ids = torch.empty((L, B), dtype=torch.int32).pin_memory()
+    h_lp = torch.empty((L, B, 2 * n + 1), dtype=torch.float32).pin_memory()
+
+    def e2e(ev):
+        d_logits.copy_(h_logits, non_blocking=True)
+        ids, lp = step(None, d_logits)
+        h_ids.copy_(ids, non_blocking=True)
+        h_lp.copy_(lp, non_blocking=True)
+
+    barrier()
+    e2e_ms, _ = _timed(torch, e2e, args.steps, stream, inner=False)
+    (e2e_ms,) = _reduce_max(torch, dist, world, device, e2e_ms)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = _sample_cpu_baseline(logits, cu, samplings, seeds, drafts)
+    abytes = rows * V * 4 + L * B * (4 + (2 * n + 1) * 4)
+    gbs = abytes / (k_ms / 1e3) / 1e9
+    return {
+        "metric": "spec-verify rows/s with on-device sampling (config 5 shape)",
+        "value": rows * world * args.steps / (ms / 1e3), "unit": "verify rows/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32 logits, f64 probabilities", "data": "synthetic (seeded)",
+        "config": {"workload": f"{L} lanes x {B} rows, vocab {V}, {n} logprobs; greedy / top-k 50 / top-p 0.9 / "
+                               "temperature lanes; per-row bucket selection (no full sort)",
+                   "parallelism": f"replicas{world}" if world > 1 else "single",
+                   "l2": f"{rows * V * 4 / 1e6:.0f} MB of logits, L2-resident between steps (no flush)"},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
+                     "traffic": None, "kernel": "hk_sample_verify (row selection + chain)", "kernel_ms": k_ms,
+                     "algorithmic_bytes": abytes, "peak_source": peak_src},
+        "cpu_baseline": cpu,
+        "e2e": {"value": rows * world * args.steps / (e2e_ms / 1e3), "unit": "verify rows/s",
+                "h2d_bytes_per_step": rows * V * 4, "d2h_bytes_per_step": L * B * (4 + (2 * n + 1) * 4)},
+        "gpu_launches": int(launches), "clocks": clocks,
+    }
+
+
+def _sample_cpu_baseline(logits, cu, samplings, seeds, drafts, sample_lanes=4):
+    """The oracle's verify step for the first `sample_lanes` lanes (one per sampling kind),
+    scaled to all lanes."""
+    from oracle import sample as S
+
+    lg = logits.cpu().numpy()
+    cun = cu.cpu().numpy()[:sample_lanes + 1]
+    st = seeds.cpu().numpy().view(np.uint64).tolist()[:sample_lanes]
+    dr = drafts.cpu().numpy()[:sample_lanes]
+    t0 = time.perf_counter()
+    S.sample_verify(lg[:cun[-1]], cun, samplings[:sample_lanes], st, dr, SAMPLE_BLOCK, SAMPLE_LOGPROBS)
+    dt = time.perf_counter() - t0
+    rows = int(cun[-1])
+    return {"value": rows / dt, "unit": "verify rows/s", "cores": 1, "kind": "port",
+            "sample": f"{sample_lanes} of {SAMPLE_LANES} lanes ({rows} rows), numpy restatement, one step"}
 
 
 def _moe_cpu_baseline(x, logits, w13, s13, w2, s2, sh13, shs13, sh2, shs2, sample_experts=6):

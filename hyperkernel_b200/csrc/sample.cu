@@ -6,7 +6,7 @@
 //     generator state, and the chain goes on to row j + 1 only while the token drawn equals
 //     draft j;
 //   * greedy (temperature <= 0 or top_k == 1): the first index of the greatest logit, no draw;
-//   * otherwise the row is sorted by value, descending in the IEEE total order, ties in index
+//   * otherwise the row is ordered by value, descending in the IEEE total order, ties in index
 //     order; the first top_k are kept (all when top_k == 0); p = softmax(value / temperature)
 //     in f64; when 0 < top_p < 1 the tail whose inclusive sum from the bottom is <= 1 - top_p
 //     is zeroed; u = splitmix(state) / 2^53 * kept picks the first index whose running sum
@@ -14,55 +14,76 @@
 //   * a row with a non-finite logit gives id -1 and ends the lane;
 //   * every accepted token gets a logprob row: n (id, logprob) pairs of log-softmax(row) at
 //     temperature 1, best first, id -1 past the vocabulary, then the token's own logprob.
-// Sums run in parallel here (the reference sums left to right): probabilities agree to the
-// last few bits, so a draw differs only if u falls that close to a boundary.
 //
-// Kernels: one CTA per row sorts the row (stable LSD radix sort of total-order keys with the
-// indices as payload, 4 passes of 8 bits, in global scratch) and prepares the row's running
-// probabilities; then one thread per lane walks the chain.
+// A row is drawn before it is known whether the chain reaches it: the state a row j draws
+// with is the lane's state advanced j times (splitmix steps by a constant), so every row is
+// independent and the chain kernel only compares tokens with drafts and counts the draws.
+//
+// Per row (one CTA) nothing is sorted in full.  The row's values go into 4096 buckets of
+// equal width between its minimum and maximum (a monotone map, so the buckets are in value
+// order); a bucket histogram of counts, or of probabilities, finds the bucket where a count
+// or a running sum crosses its target, and only the elements up to (or of) that bucket are
+// gathered into shared memory and sorted there (bitonic, by total-order key then index):
+//   * top-n logprob pairs and the top-k set: the first n / k of the buckets up to the one
+//     where the count reaches n / k; with top_k > 0 the whole reference computation then
+//     runs on those k entries in shared memory, sums left to right as in the reference;
+//   * top_k == 0: the top-p cut and the draw are running-sum crossings over the whole row:
+//     bucket sums (f64) up to the crossing bucket, then that bucket's elements in order.
+//     Those sums are not left to right, so a draw could differ from the reference only where
+//     u lies within a few ulps of a boundary.
+// A crossing bucket with more than kCap elements (near-constant rows) falls back to a full
+// stable radix sort of the row in global scratch.
 #include "common.cuh"
 
 namespace {
 
-constexpr int kThreads = 512;
+constexpr int kThreads = 1024;
 constexpr int kWarps = kThreads / 32;
 constexpr int kMaxVocab = 1 << 22;
+constexpr int kBuckets = 4096;
+constexpr int kCap = 8192;            // elements a gather may hold
+constexpr int kMaxLogprobs = 64;
+constexpr uint64_t kGamma = 0x9E3779B97F4A7C15ull;
+constexpr int kDynSmem = kBuckets * (4 + 8) + kCap * 8;
 
 struct RowStat {
   double lse;      // log-sum-exp of the row (temperature 1)
-  double kept;     // probability mass left after top-k / top-p (sampled rows)
   int32_t argmax;  // first index of the greatest logit
-  int32_t m;       // entries kept by top-k
-  int32_t flags;   // 1: a non-finite logit; 2: the row was sorted
-  int32_t pad;
+  int32_t token;   // the drawn token (sampled rows)
+  int32_t flags;   // 1: a non-finite logit
+  int32_t ntop;    // pairs in the row's top list
 };
 
 struct Scratch {
-  uint32_t* keys;  // [rows][2][vocab]
+  uint32_t* keys;  // [rows][2][vocab]  (full-sort fallback)
   int32_t* idx;    // [rows][2][vocab]
-  double* cum;     // [rows][vocab]
+  int32_t* top;    // [rows][kMaxLogprobs] indices, best first
+  float* topv;     // [rows][kMaxLogprobs] their logits
   RowStat* stats;  // [rows]
 };
 
 size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
-Scratch carve(void* ws, int32_t rows, int32_t vocab) {
-  uint8_t* p = reinterpret_cast<uint8_t*>(ws);
-  Scratch s;
-  const size_t nv = (size_t)rows * vocab;
-  s.keys = reinterpret_cast<uint32_t*>(p);
-  p += align256(nv * 2 * sizeof(uint32_t));
-  s.idx = reinterpret_cast<int32_t*>(p);
-  p += align256(nv * 2 * sizeof(int32_t));
-  s.cum = reinterpret_cast<double*>(p);
-  p += align256(nv * sizeof(double));
-  s.stats = reinterpret_cast<RowStat*>(p);
-  return s;
-}
-
 size_t scratch_bytes(int32_t rows, int32_t vocab) {
   const size_t nv = (size_t)rows * vocab;
-  return align256(nv * 8) + align256(nv * 8) + align256(nv * 8) + align256((size_t)rows * sizeof(RowStat));
+  return align256(nv * 8) + align256(nv * 8) + 2 * align256((size_t)rows * kMaxLogprobs * 4) +
+         align256((size_t)rows * sizeof(RowStat));
+}
+
+Scratch carve(void* ws, int32_t rows, int32_t vocab) {
+  uint8_t* p = reinterpret_cast<uint8_t*>(ws);
+  const size_t nv = (size_t)rows * vocab;
+  Scratch s;
+  s.keys = reinterpret_cast<uint32_t*>(p);
+  p += align256(nv * 8);
+  s.idx = reinterpret_cast<int32_t*>(p);
+  p += align256(nv * 8);
+  s.top = reinterpret_cast<int32_t*>(p);
+  p += align256((size_t)rows * kMaxLogprobs * 4);
+  s.topv = reinterpret_cast<float*>(p);
+  p += align256((size_t)rows * kMaxLogprobs * 4);
+  s.stats = reinterpret_cast<RowStat*>(p);
+  return s;
 }
 
 // Descending IEEE total order as an ascending unsigned key, and back.
@@ -89,6 +110,14 @@ __device__ __forceinline__ int lane_of(const int32_t* cu, int lanes, int r) {
   return lo;
 }
 
+// The draw of the state advanced `steps` + 1 times (src/evo2/draw.rs:52-58).
+__device__ __forceinline__ uint64_t splitmix_at(uint64_t state, uint64_t steps) {
+  uint64_t z = state + (steps + 1) * kGamma;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return (z ^ (z >> 31)) >> 11;
+}
+
 // Block-wide sum of a double (every thread gets it); `red` holds kWarps doubles.
 __device__ double block_sum(double v, double* red) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -103,19 +132,20 @@ __device__ double block_sum(double v, double* red) {
   return t;
 }
 
-// Block-wide exclusive prefix of a double in thread order (and the total).
-__device__ double block_excl(double v, double* red, double* total) {
+// Block-wide exclusive prefix in thread order (and the total), for doubles and counts.
+template <typename T>
+__device__ T block_excl(T v, T* red, T* total) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  double x = v;
+  T x = v;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
-    const double y = __shfl_up_sync(0xffffffffu, x, o);
+    const T y = __shfl_up_sync(0xffffffffu, x, o);
     if (lane >= o) x += y;
   }
   __syncthreads();
   if (lane == 31) red[warp] = x;
   __syncthreads();
-  double before = 0.0, t = 0.0;
+  T before = 0, t = 0;
 #pragma unroll
   for (int w = 0; w < kWarps; ++w) {
     if (w < warp) before += red[w];
@@ -125,62 +155,114 @@ __device__ double block_excl(double v, double* red, double* total) {
   return before + x - v;
 }
 
-__global__ void __launch_bounds__(kThreads) sample_rows_kernel(
-    const float* __restrict__ logits, int32_t vocab, const int32_t* __restrict__ cu, int32_t lanes,
-    int32_t rows, const hk_sampling* __restrict__ sampling, int32_t n_logprobs, Scratch s,
-    unsigned long long* err) {
-  __shared__ uint32_t hist[256], base[256], run[256];
-  __shared__ uint32_t wcnt[kWarps][256];  // (tag << 16) | count of a digit in a warp's slice
-  __shared__ double red[kWarps];
-  __shared__ float smax[kWarps];
-  __shared__ int sarg[kWarps], sbad[kWarps];
-  const int r = blockIdx.x;
-  if (r >= rows) return;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const hk_sampling smp = sampling[lane_of(cu, lanes, r)];
-  const float* x = logits + (int64_t)r * vocab;
-  RowStat* st = s.stats + r;
-
-  // ---- the row's maximum (first index), finiteness and log-sum-exp
-  float mx = -INFINITY;
-  int arg = 0x7fffffff, bad = 0;
-  for (int i = tid; i < vocab; i += kThreads) {
-    const float v = x[i];
-    if (!isfinite(v)) bad = 1;
-    else if (v > mx || (v == mx && i < arg)) { mx = v; arg = i; }
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float m2 = __shfl_xor_sync(0xffffffffu, mx, o);
-    const int a2 = __shfl_xor_sync(0xffffffffu, arg, o);
-    if (m2 > mx || (m2 == mx && a2 < arg)) { mx = m2; arg = a2; }
-    bad |= __shfl_xor_sync(0xffffffffu, bad, o);
-  }
-  if (lane == 0) { smax[warp] = mx; sarg[warp] = arg; sbad[warp] = bad; }
+// Sorts list[0..n) ascending (n <= kCap), padding to a power of two with ~0.
+__device__ void bitonic(uint64_t* list, int n) {
+  int N = 1;
+  while (N < n) N <<= 1;
+  for (int i = n + (int)threadIdx.x; i < N; i += kThreads) list[i] = ~0ull;
   __syncthreads();
-  mx = smax[0]; arg = sarg[0]; bad = sbad[0];
-  for (int w = 1; w < kWarps; ++w) {
-    if (smax[w] > mx || (smax[w] == mx && sarg[w] < arg)) { mx = smax[w]; arg = sarg[w]; }
-    bad |= sbad[w];
-  }
-  if (bad) {
-    if (tid == 0) { st->flags = 1; st->argmax = 0; st->m = 0; st->kept = 0.0; st->lse = 0.0; }
-    return;
-  }
-  double e = 0.0;
-  for (int i = tid; i < vocab; i += kThreads) e += exp((double)x[i] - (double)mx);
-  const double lse = (double)mx + log(block_sum(e, red));
-  const bool sampled = !greedy(smp);
-  if (!sampled && n_logprobs == 0) {
-    if (tid == 0) { st->flags = 0; st->argmax = arg; st->m = 0; st->kept = 0.0; st->lse = lse; }
-    return;
-  }
+  for (int k = 2; k <= N; k <<= 1)
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = threadIdx.x; i < N; i += kThreads) {
+        const int l = i ^ j;
+        if (l > i) {
+          const uint64_t a = list[i], b = list[l];
+          if ((a > b) == ((i & k) == 0)) {
+            list[i] = b;
+            list[l] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+}
 
-  // ---- stable LSD radix sort of (key, index), 4 passes of 8 bits, buffers 0 -> 1 -> 0 ...
-  uint32_t* k0 = s.keys + (int64_t)r * 2 * vocab;
-  uint32_t* k1 = k0 + vocab;
-  int32_t* i0 = s.idx + (int64_t)r * 2 * vocab;
-  int32_t* i1 = i0 + vocab;
+__device__ __forceinline__ uint64_t composite(float v, int i) {
+  return ((uint64_t)desc_key(v) << 32) | (uint32_t)i;
+}
+
+struct Row {
+  const float* x;
+  int vocab;
+  float xmax, inv_w;
+  __device__ __forceinline__ int bucket(float v) const {
+    const int b = (int)((xmax - v) * inv_w);
+    return b < kBuckets - 1 ? b : kBuckets - 1;
+  }
+};
+
+// The bucket where the inclusive count prefix reaches `target` (>= 1), and the count before it.
+__device__ int count_cross(const uint32_t* hist_c, uint32_t target, uint32_t* before_out, uint32_t* red) {
+  constexpr int kPer = kBuckets / kThreads;
+  __shared__ int found;
+  __shared__ uint32_t found_before;
+  const int b0 = threadIdx.x * kPer;
+  uint32_t loc = 0;
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) loc += hist_c[b0 + j];
+  uint32_t total;
+  uint32_t acc = block_excl<uint32_t>(loc, red, &total);
+  if (threadIdx.x == 0) { found = kBuckets - 1; found_before = 0; }
+  __syncthreads();
+  if (acc < target && acc + loc >= target) {
+    for (int j = 0; j < kPer; ++j) {
+      const uint32_t c = hist_c[b0 + j];
+      if (acc + c >= target) { found = b0 + j; found_before = acc; break; }
+      acc += c;
+    }
+  }
+  __syncthreads();
+  *before_out = found_before;
+  return found;
+}
+
+// Bucket weights are fixed point: w * 2^40 rounded (w <= 1, so a row of 4M entries stays
+// below 2^62), summed with integer atomics; prefix sums over buckets are then exact.
+constexpr double kFix = 1099511627776.0;
+
+// The first bucket whose inclusive weight prefix exceeds `target`, and the weight before it.
+__device__ int weight_cross(const unsigned long long* hist_w, double target, double* before_out,
+                            unsigned long long* red) {
+  constexpr int kPer = kBuckets / kThreads;
+  __shared__ int found;
+  __shared__ unsigned long long found_before;
+  const int b0 = threadIdx.x * kPer;
+  unsigned long long loc = 0;
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) loc += hist_w[b0 + j];
+  unsigned long long total;
+  unsigned long long acc = block_excl<unsigned long long>(loc, red, &total);
+  const double tfix = target * kFix;
+  if (threadIdx.x == 0) { found = -1; found_before = 0; }
+  __syncthreads();
+  if ((double)acc <= tfix && (double)(acc + loc) > tfix) {
+    for (int j = 0; j < kPer; ++j) {
+      const unsigned long long w = hist_w[b0 + j];
+      if ((double)(acc + w) > tfix) { found = b0 + j; found_before = acc; break; }
+      acc += w;
+    }
+  }
+  __syncthreads();
+  if (found < 0) {  // the target at the very end: the last non-empty bucket
+    if (threadIdx.x == 0) {
+      unsigned long long a = 0;
+      for (int b = 0; b < kBuckets; ++b) {
+        if (hist_w[b] > 0) { found = b; found_before = a; }
+        a += hist_w[b];
+      }
+      if (found < 0) found = 0;
+    }
+    __syncthreads();
+  }
+  *before_out = (double)found_before / kFix;
+  return found;
+}
+
+// Stable LSD radix sort of the row's (total-order key, index) pairs in global scratch, 4
+// passes of 8 bits; the result is in k0 / i0.  The fallback for near-constant rows.
+__device__ void full_sort(const float* x, int vocab, uint32_t* k0, uint32_t* k1, int32_t* i0, int32_t* i1,
+                          uint32_t* hist, uint32_t* base, uint32_t* run, uint32_t (*wcnt)[256]) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   for (int i = tid; i < vocab; i += kThreads) { k0[i] = desc_key(x[i]); i0[i] = i; }
   for (int i = tid; i < kWarps * 256; i += kThreads) (&wcnt[0][0])[i] = 0u;
   const int tiles = (vocab + kThreads - 1) / kThreads;
@@ -195,7 +277,7 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(
     __syncthreads();
     for (int i = tid; i < vocab; i += kThreads) atomicAdd(&hist[(ks[i] >> shift) & 255u], 1u);
     __syncthreads();
-    if (warp == 0) {  // exclusive scan of the 256 digit counts, 8 per lane
+    if (warp == 0) {
       uint32_t loc[8], sum = 0;
 #pragma unroll
       for (int j = 0; j < 8; ++j) { loc[j] = hist[lane * 8 + j]; sum += loc[j]; }
@@ -212,10 +294,10 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(
     __syncthreads();
     for (int t = 0; t < tiles; ++t) {
       const uint32_t tag = (uint32_t)(pass * tiles + t + 1);
-      const int e_ = t * kThreads + tid;
-      const bool valid = e_ < vocab;
-      const uint32_t key = valid ? ks[e_] : 0u;
-      const int32_t ix = valid ? is[e_] : 0;
+      const int e = t * kThreads + tid;
+      const bool valid = e < vocab;
+      const uint32_t key = valid ? ks[e] : 0u;
+      const int32_t ix = valid ? is[e] : 0;
       const uint32_t d = valid ? ((key >> shift) & 255u) : 256u;
       const uint32_t peers = __match_any_sync(0xffffffffu, d);
       const uint32_t wrank = __popc(peers & lt_mask);
@@ -243,59 +325,241 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(
       __syncthreads();
     }
   }
-  // sorted keys and indices are in k0 / i0
-
-  int m = 0;
-  double kept = 0.0;
-  if (sampled) {
-    m = smp.top_k > 0 ? (int)min((uint32_t)vocab, smp.top_k) : vocab;
-    double* p = s.cum + (int64_t)r * vocab;
-    const double temp = (double)smp.temperature;
-    const double s0 = (double)key_value(k0[0]) / temp;
-    const int chunk = (m + kThreads - 1) / kThreads;
-    const int a = min(m, tid * chunk), z = min(m, a + chunk);
-    double loc = 0.0;
-    for (int i = a; i < z; ++i) {
-      const double v = exp((double)key_value(k0[i]) / temp - s0);
-      p[i] = v;
-      loc += v;
-    }
-    const double total = block_sum(loc, red);
-    for (int i = a; i < z; ++i) p[i] = p[i] / total;
-    const double top_p = (double)smp.top_p;
-    if (top_p > 0.0 && top_p < 1.0) {
-      // zero the tail whose inclusive sum from the bottom is <= 1 - top_p
-      loc = 0.0;
-      for (int i = a; i < z; ++i) loc += p[i];
-      double all;
-      const double before = block_excl(loc, red, &all);
-      double below = all - before - loc;  // mass of the chunks after this one
-      for (int i = z - 1; i >= a; --i) {
-        below += p[i];
-        if (below <= 1.0 - top_p) p[i] = 0.0;
-      }
-      __syncthreads();
-    }
-    // running sums of what is left
-    loc = 0.0;
-    for (int i = a; i < z; ++i) loc += p[i];
-    double all;
-    double acc = block_excl(loc, red, &all);
-    for (int i = a; i < z; ++i) {
-      acc += p[i];
-      p[i] = acc;
-    }
-    kept = all;
-  }
-  if (tid == 0) { st->flags = 2; st->argmax = arg; st->m = m; st->kept = kept; st->lse = lse; }
 }
 
-__device__ __forceinline__ uint64_t splitmix(uint64_t& state) {
-  state += 0x9E3779B97F4A7C15ull;
-  uint64_t z = state;
-  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
-  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
-  return (z ^ (z >> 31)) >> 11;
+// The reference draw over m sorted entries (values v(i), indices id(i)), run by one thread
+// with every sum left to right (src/evo2/draw.rs:24-48).
+template <typename V, typename I>
+__device__ int draw_sorted(int m, V v, I id, const hk_sampling& smp, uint64_t bits) {
+  const double temp = (double)smp.temperature;
+  const double most = (double)v(0) / temp;
+  double total = 0.0;
+  for (int i = 0; i < m; ++i) total += exp((double)v(i) / temp - most);
+  const double top_p = (double)smp.top_p;
+  const bool cut = top_p > 0.0 && top_p < 1.0;
+  // the zeroed tail is a suffix: find where it starts, summing from the bottom
+  int keep = m;
+  if (cut) {
+    double below = 0.0;
+    for (int i = m - 1; i >= 0; --i) {
+      below += exp((double)v(i) / temp - most) / total;
+      if (below <= 1.0 - top_p) keep = i; else break;
+    }
+  }
+  double kept = 0.0;
+  for (int i = 0; i < keep; ++i) kept += exp((double)v(i) / temp - most) / total;
+  const double u = (double)bits / 9007199254740992.0 * kept;
+  double seen = 0.0;
+  for (int i = 0; i < keep; ++i) {
+    seen += exp((double)v(i) / temp - most) / total;
+    if (u < seen) return id(i);
+  }
+  // the last index with a non-zero probability
+  for (int i = keep - 1; i >= 0; --i)
+    if (exp((double)v(i) / temp - most) / total > 0.0) return id(i);
+  return id(0);
+}
+
+__global__ void __launch_bounds__(kThreads) sample_rows_kernel(
+    const float* __restrict__ logits, int32_t vocab, const int32_t* __restrict__ cu, int32_t lanes,
+    int32_t rows, const hk_sampling* __restrict__ sampling, const uint64_t* __restrict__ state,
+    int32_t n_logprobs, Scratch s, unsigned long long* err) {
+  extern __shared__ __align__(16) uint8_t dyn[];
+  uint32_t* hist_c = reinterpret_cast<uint32_t*>(dyn);
+  unsigned long long* hist_w = reinterpret_cast<unsigned long long*>(dyn + kBuckets * 4);
+  uint64_t* list = reinterpret_cast<uint64_t*>(dyn + kBuckets * 12);
+  __shared__ uint32_t shist[256], sbase[256], srun[256];
+  __shared__ uint32_t wcnt[kWarps][256];
+  __shared__ double red[kWarps];
+  __shared__ uint32_t redu[kWarps];
+  __shared__ unsigned long long redl[kWarps];
+  __shared__ float smax[kWarps], smin[kWarps];
+  __shared__ int sarg[kWarps], sbad[kWarps];
+  __shared__ int list_n, result;
+  const int r = blockIdx.x;
+  if (r >= rows) return;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int b = lane_of(cu, lanes, r);
+  const hk_sampling smp = sampling[b];
+  const int j = r - cu[b];  // the row's position in its lane: draws before it
+  const float* x = logits + (int64_t)r * vocab;
+  RowStat* st = s.stats + r;
+
+  // ---- maximum (first index), minimum, finiteness, log-sum-exp
+  float mx = -INFINITY, mn = INFINITY;
+  int arg = 0x7fffffff, bad = 0;
+  for (int i = tid; i < vocab; i += kThreads) {
+    const float v = x[i];
+    if (!isfinite(v)) { bad = 1; continue; }
+    if (v > mx || (v == mx && i < arg)) { mx = v; arg = i; }
+    mn = fminf(mn, v);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, mx, o);
+    const int a2 = __shfl_xor_sync(0xffffffffu, arg, o);
+    if (m2 > mx || (m2 == mx && a2 < arg)) { mx = m2; arg = a2; }
+    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+    bad |= __shfl_xor_sync(0xffffffffu, bad, o);
+  }
+  if (lane == 0) { smax[warp] = mx; smin[warp] = mn; sarg[warp] = arg; sbad[warp] = bad; }
+  __syncthreads();
+  mx = smax[0]; mn = smin[0]; arg = sarg[0]; bad = sbad[0];
+  for (int w = 1; w < kWarps; ++w) {
+    if (smax[w] > mx || (smax[w] == mx && sarg[w] < arg)) { mx = smax[w]; arg = sarg[w]; }
+    mn = fminf(mn, smin[w]);
+    bad |= sbad[w];
+  }
+  if (bad) {
+    if (tid == 0) { st->flags = 1; st->argmax = 0; st->token = -1; st->ntop = 0; st->lse = 0.0; }
+    return;
+  }
+  double lse = 0.0;  // log-sum-exp for the logprob rows (computed with the top-n pass)
+  const bool sampled = !greedy(smp);
+  const Row row{x, vocab, mx, mx > mn ? (float)kBuckets / (mx - mn) : 0.f};
+  const int n = min(n_logprobs, vocab);
+  const int k = sampled && smp.top_k > 0 ? (int)min((uint32_t)vocab, smp.top_k) : 0;
+  const uint64_t bits = sampled ? splitmix_at(state[b], (uint64_t)j) : 0ull;
+  int token = arg;
+  bool sorted_full = false;
+  uint32_t* k0 = s.keys + (int64_t)r * 2 * vocab;
+  int32_t* i0 = s.idx + (int64_t)r * 2 * vocab;
+
+  // ---- the top max(n, k) in order: buckets up to the count crossing, gathered and sorted
+  const int c = max(n, k);
+  if (c > 0) {
+    for (int i = tid; i < kBuckets; i += kThreads) hist_c[i] = 0u;
+    __syncthreads();
+    // single-precision exponentials (one rounding each) summed in f64 for the log-sum-exp
+    double e = 0.0;
+    for (int i = tid; i < vocab; i += kThreads) {
+      const float v = x[i];
+      atomicAdd(&hist_c[row.bucket(v)], 1u);
+      if (n > 0) e += (double)expf(v - mx);
+    }
+    lse = (double)mx + log(block_sum(e, red));  // block_sum's barriers close the histogram
+    uint32_t before;
+    const int bc = count_cross(hist_c, (uint32_t)c, &before, redu);
+    const uint32_t upto = before + hist_c[bc];  // elements in buckets 0..bc
+    if (tid == 0) list_n = 0;
+    __syncthreads();
+    if (upto <= (uint32_t)kCap) {
+      for (int i = tid; i < vocab; i += kThreads) {
+        const float v = x[i];
+        if (row.bucket(v) <= bc) list[atomicAdd(&list_n, 1)] = composite(v, i);
+      }
+      __syncthreads();
+      bitonic(list, (int)upto);
+      for (int q = tid; q < n; q += kThreads) {
+        const uint64_t L = list[q];
+        s.top[(int64_t)r * kMaxLogprobs + q] = (int32_t)(uint32_t)L;
+        s.topv[(int64_t)r * kMaxLogprobs + q] = key_value((uint32_t)(L >> 32));
+      }
+      if (k > 0 && tid == 0)
+        token = draw_sorted(
+            k, [&](int i) { return key_value((uint32_t)(list[i] >> 32)); },
+            [&](int i) { return (int)(uint32_t)list[i]; }, smp, bits);
+    } else {
+      full_sort(x, vocab, k0, k0 + vocab, i0, i0 + vocab, shist, sbase, srun, wcnt);
+      sorted_full = true;
+      for (int q = tid; q < n; q += kThreads) {
+        s.top[(int64_t)r * kMaxLogprobs + q] = i0[q];
+        s.topv[(int64_t)r * kMaxLogprobs + q] = key_value(k0[q]);
+      }
+      if (k > 0 && tid == 0)
+        token = draw_sorted(
+            k, [&](int i) { return key_value(k0[i]); }, [&](int i) { return i0[i]; }, smp, bits);
+    }
+    __syncthreads();
+  }
+
+  // ---- top_k == 0: the top-p cut and the draw as running-sum crossings over the whole row
+  if (sampled && k == 0) {
+    const double temp = (double)smp.temperature;
+    const double most = (double)mx / temp;
+    if (sorted_full) {
+      if (tid == 0)
+        token = draw_sorted(
+            vocab, [&](int i) { return key_value(k0[i]); }, [&](int i) { return i0[i]; }, smp, bits);
+    } else {
+      for (int i = tid; i < kBuckets; i += kThreads) { hist_c[i] = 0u; hist_w[i] = 0ull; }
+      __syncthreads();
+      // Bucket sums only place a crossing to within ~1e-12 of the mass; the crossing bucket's
+      // own entries are then summed exactly.  So single-precision exponentials suffice here.
+      unsigned long long loc = 0;
+      for (int i = tid; i < vocab; i += kThreads) {
+        const float v = x[i];
+        const int bk = row.bucket(v);
+        const unsigned long long w =
+            __double2ull_rn((double)expf((float)((double)v / temp - most)) * kFix);
+        atomicAdd(&hist_c[bk], 1u);
+        atomicAdd(&hist_w[bk], w);
+        loc += w;
+      }
+      unsigned long long tot_fix;
+      block_excl<unsigned long long>(loc, redl, &tot_fix);  // includes the barrier the histograms need
+      const double total = (double)tot_fix / kFix;
+      // Running-sum crossing of `target` (unnormalised): the element, and the sum through it.
+      auto cross = [&](double target, double* incl) -> int {
+        double before;
+        const int bk = weight_cross(hist_w, target, &before, redl);
+        const uint32_t cnt = hist_c[bk];
+        __syncthreads();
+        if (cnt > (uint32_t)kCap) return -1;
+        if (tid == 0) list_n = 0;
+        __syncthreads();
+        for (int i = tid; i < vocab; i += kThreads) {
+          const float v = x[i];
+          if (row.bucket(v) == bk) list[atomicAdd(&list_n, 1)] = composite(v, i);
+        }
+        __syncthreads();
+        bitonic(list, (int)cnt);
+        if (tid == 0) {
+          double acc = before;
+          int pick = -1;
+          for (uint32_t q = 0; q < cnt; ++q) {
+            acc += exp((double)key_value((uint32_t)(list[q] >> 32)) / temp - most);
+            if (acc > target) { pick = (int)(uint32_t)list[q]; break; }
+          }
+          if (pick < 0 && cnt > 0) pick = (int)(uint32_t)list[cnt - 1];
+          result = pick;
+          red[0] = acc;
+        }
+        __syncthreads();
+        *incl = red[0];
+        const int out = result;
+        __syncthreads();
+        return out;
+      };
+      double kept = total;
+      bool ok = true;
+      const double top_p = (double)smp.top_p;
+      if (top_p > 0.0 && top_p < 1.0) {
+        double incl;
+        ok = cross(top_p * total, &incl) >= 0;
+        kept = incl;
+      }
+      if (ok) {
+        double incl;
+        const int t = cross((double)bits / 9007199254740992.0 * kept, &incl);
+        ok = t >= 0;
+        token = t;
+      }
+      if (!ok) {  // a crossing bucket too full to gather: sort the row
+        full_sort(x, vocab, k0, k0 + vocab, i0, i0 + vocab, shist, sbase, srun, wcnt);
+        if (tid == 0)
+          token = draw_sorted(
+              vocab, [&](int i) { return key_value(k0[i]); }, [&](int i) { return i0[i]; }, smp, bits);
+      }
+    }
+  }
+  if (tid == 0) {
+    st->flags = 0;
+    st->argmax = arg;
+    st->token = sampled ? token : arg;
+    st->ntop = n;
+    st->lse = lse;
+  }
 }
 
 __global__ void sample_chain_kernel(const float* __restrict__ logits, int32_t vocab,
@@ -317,8 +581,8 @@ __global__ void sample_chain_kernel(const float* __restrict__ logits, int32_t vo
     hk_flag(err, hk::kErrMoeRow, (unsigned)b);
     return;
   }
-  const hk_sampling smp = sampling[b];
-  uint64_t st = state[b];
+  const bool sampled = !greedy(sampling[b]);
+  uint64_t draws = 0;
   for (int j = 0; j < rows; ++j) {
     const int r = r0 + j;
     const RowStat rs = s.stats[r];
@@ -327,37 +591,15 @@ __global__ void sample_chain_kernel(const float* __restrict__ logits, int32_t vo
       *out = -1;
       break;
     }
-    const int32_t* sorted = s.idx + (int64_t)r * 2 * vocab;
-    const uint32_t* keys = s.keys + (int64_t)r * 2 * vocab;
-    int t;
-    if (greedy(smp)) {
-      t = rs.argmax;
-    } else {
-      const double* cum = s.cum + (int64_t)r * vocab;
-      const double u = (double)splitmix(st) / 9007199254740992.0 * rs.kept;
-      int lo = 0, hi = rs.m;  // first index whose running sum exceeds u
-      while (lo < hi) {
-        const int mid = (lo + hi) >> 1;
-        if (cum[mid] > u) hi = mid; else lo = mid + 1;
-      }
-      if (lo >= rs.m) {  // none: the last index with a non-zero probability
-        const double last = cum[rs.m - 1];
-        lo = 0;
-        hi = rs.m - 1;
-        while (lo < hi) {
-          const int mid = (lo + hi) >> 1;
-          if (cum[mid] >= last) hi = mid; else lo = mid + 1;
-        }
-      }
-      t = sorted[lo];
-    }
+    const int t = rs.token;
+    draws += sampled ? 1 : 0;
     *out = t;
     if (n_logprobs > 0) {
       float* row = lp + ((int64_t)b * block + j) * width;
       for (int q = 0; q < n_logprobs; ++q) {
-        if (q < vocab) {
-          row[2 * q] = (float)sorted[q];
-          row[2 * q + 1] = (float)((double)key_value(keys[q]) - rs.lse);
+        if (q < rs.ntop) {
+          row[2 * q] = (float)s.top[(int64_t)r * kMaxLogprobs + q];
+          row[2 * q + 1] = (float)((double)s.topv[(int64_t)r * kMaxLogprobs + q] - rs.lse);
         } else {
           row[2 * q] = -1.f;
         }
@@ -366,7 +608,7 @@ __global__ void sample_chain_kernel(const float* __restrict__ logits, int32_t vo
     }
     if (j + 1 < rows && t != drafts[(int64_t)b * (block - 1) + j]) break;
   }
-  state[b] = st;
+  state[b] += draws * kGamma;
 }
 
 }  // namespace
@@ -385,7 +627,7 @@ int hk_sample_verify(const float* logits, int32_t vocab, const int32_t* cu_rows,
   HK_TRY(hk::ensure_device());
   HK_REQUIRE(logits && cu_rows && sampling && state && ids && workspace, "hk_sample_verify: null pointer");
   HK_REQUIRE(vocab > 0 && vocab <= kMaxVocab, "hk_sample_verify: vocab %d not in 1..%d", vocab, kMaxVocab);
-  HK_REQUIRE(num_lanes > 0 && num_rows >= 0 && block >= 1 && n_logprobs >= 0 && n_logprobs <= 64,
+  HK_REQUIRE(num_lanes > 0 && num_rows >= 0 && block >= 1 && n_logprobs >= 0 && n_logprobs <= kMaxLogprobs,
              "hk_sample_verify: bad sizes");
   HK_REQUIRE(block == 1 || drafts != nullptr, "hk_sample_verify: drafts needed for block %d", block);
   HK_REQUIRE(n_logprobs == 0 || lp != nullptr, "hk_sample_verify: lp needed for %d logprobs", n_logprobs);
@@ -395,9 +637,14 @@ int hk_sample_verify(const float* logits, int32_t vocab, const int32_t* cu_rows,
     return hk::fail(HK_ESPACE, "hk_sample_verify: workspace of %zu bytes, %zu needed", workspace_bytes, need);
   Scratch s = carve(workspace, num_rows, vocab);
   cudaStream_t st = (cudaStream_t)stream;
+  static bool attr = false;
+  if (!attr) {
+    HK_TRY_CUDA(cudaFuncSetAttribute(sample_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmem));
+    attr = true;
+  }
   if (num_rows > 0) {
-    sample_rows_kernel<<<num_rows, kThreads, 0, st>>>(logits, vocab, cu_rows, num_lanes, num_rows, sampling,
-                                                      n_logprobs, s, hk::err_word());
+    sample_rows_kernel<<<num_rows, kThreads, kDynSmem, st>>>(logits, vocab, cu_rows, num_lanes, num_rows,
+                                                             sampling, state, n_logprobs, s, hk::err_word());
     HK_TRY_LAUNCH("sample_rows_kernel");
   }
   sample_chain_kernel<<<(num_lanes + 63) / 64, 64, 0, st>>>(logits, vocab, cu_rows, num_lanes, block, sampling,
