@@ -23,7 +23,9 @@ routed experts + the shared expert, combine; 512 tokens, hidden 7168, inter 2048
 (the MLA FP8 projections q_a, q_b, kv_a, o over the 4144-token mixed prefill + decode batch).
 --workload longctx measures config 5 (one lane at 1M cached rows plus 7 shorter ones, 1 + 4
 spec-verify rows each, FP8 latent cache); on N GPUs the long lane's KV is split by position
-(context parallel) and the partials merged by LSE.
+(context parallel) and the partials merged by LSE.  --workload sample measures spec-decode
+verification with on-device sampling at config 5's shape (8 lanes x 5 rows of logits over a
+129,280-token vocabulary).
 """
 from __future__ import annotations
 
