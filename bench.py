@@ -43,7 +43,7 @@ sys.path.insert(0, ROOT)
 
 HEADS = 128
 PAGE = 64
-TRAFFIC_PER_ALGORITHMIC_BYTE = 1.046
+TRAFFIC_PER_ALGORITHMIC_BYTE = 1.044
 DK, DV = 576, 512
 
 
@@ -313,11 +313,11 @@ def main(argv=None):
                        "attn_impl": args.attn_impl},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak,
-                         # DRAM read+write bytes per launch: 1.046 x algorithmic in an ncu
+                         # DRAM read+write bytes per launch: 1.044 x algorithmic in an ncu
                          # capture of 64 lanes, ctx <= 16K, scaled here by the KV rows.
                          "traffic": TRAFFIC_PER_ALGORITHMIC_BYTE * abytes,
                          "traffic_source": "ncu dram__bytes_read+write of a 64-lane ctx<=16K "
-                                           "launch (1.046 x algorithmic), scaled by KV rows",
+                                           "launch (1.044 x algorithmic), scaled by KV rows",
                          "kernel": "attention (hk_mla_decode)", "kernel_ms": attn_ms,
                          "algorithmic_bytes": abytes, "peak_source": peak_src,
                          "tflops": attn_flops(lay.kv_len) / (attn_ms / 1e3) / 1e12},
