@@ -83,6 +83,7 @@ def cpu_step_seconds(lay, target_rows: int, reps: int = 1):
     (seconds per full step extrapolated by KV rows, sample rows, sample lanes, threads)."""
     import oracle
 
+    oracle.use_all_cores()
     sub, rows = cpu_sample_layout(lay, target_rows)
     g = np.random.default_rng(7)
     T = sub.num_tokens
@@ -846,6 +847,8 @@ def _moe_cpu_baseline(x, logits, w13, s13, w2, s2, sh13, shs13, sh2, shs2, sampl
     linear in rows) plus the shared expert scaled likewise."""
     import oracle
 
+    oracle.use_all_cores()
+
     xb = x.view(torch_int16()).cpu().numpy().view(np.uint16)
     lg = logits.cpu().numpy()
     t0 = time.perf_counter()
@@ -876,6 +879,8 @@ def _moe_cpu_baseline(x, logits, w13, s13, w2, s2, sh13, shs13, sh2, shs2, sampl
 def _linear_cpu_baseline(x, attn, ws, sample_tokens=8):
     """The oracle's FP8 projections on the host cores for `sample_tokens` tokens, scaled."""
     import oracle
+
+    oracle.use_all_cores()
 
     xb = x[:sample_tokens].view(torch_int16()).cpu().numpy().view(np.uint16)
     ab = attn[:sample_tokens].view(torch_int16()).cpu().numpy().view(np.uint16)

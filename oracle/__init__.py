@@ -33,6 +33,8 @@ def lib():
         _lib.orc_sigmoid.restype = C.c_float
         _lib.orc_sigmoid.argtypes = [C.c_float]
         _lib.orc_threads.restype = C.c_int
+        _lib.orc_set_threads.restype = C.c_int
+        _lib.orc_set_threads.argtypes = [C.c_int]
     return _lib
 
 
@@ -46,6 +48,14 @@ def _c(a, dtype):
 
 def threads() -> int:
     return lib().orc_threads()
+
+
+def use_all_cores() -> int:
+    """OpenMP threads = the CPUs this process may run on (torchrun sets OMP_NUM_THREADS=1)."""
+    import os
+
+    n = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    return lib().orc_set_threads(n)
 
 
 def pack(lane_tokens, lane_pos, block_table, page_size, num_pages, max_tokens):

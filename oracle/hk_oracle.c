@@ -550,6 +550,17 @@ void orc_rope_table(int64_t rows, int dim, float base, int original_seq_len, flo
   }
 }
 
+/* Sets the OpenMP thread count of later calls (a launcher may have set OMP_NUM_THREADS=1). */
+int orc_set_threads(int n) {
+#ifdef _OPENMP
+  if (n > 0) omp_set_num_threads(n);
+  return omp_get_max_threads();
+#else
+  (void)n;
+  return 1;
+#endif
+}
+
 int orc_threads(void) {
 #ifdef _OPENMP
   return omp_get_max_threads();
