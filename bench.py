@@ -187,7 +187,7 @@ def main(argv=None):
     ap.add_argument("--ctx-min", type=int, default=1024, help="profiling override of config 2")
     ap.add_argument("--ctx-max", type=int, default=131072, help="profiling override of config 2")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host round trip leg")
-    ap.add_argument("--workload", default="decode", choices=["decode", "moe", "linear", "longctx", "sample"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "moe", "linear", "longctx", "sample", "mixed"])
     ap.add_argument("--experts", type=int, default=None, help="profiling override of config 4's 256 experts")
     ap.add_argument("--ep", default="peer", choices=["peer", "nccl"],
                     help="expert-parallel exchange: NVLink stores from libhk kernels, or NCCL all-to-allv")
@@ -415,6 +415,9 @@ def run_layer(args):
     elif args.workload == "longctx":
         line = _run_longctx(args, torch, dist, hk, par, ClockSampler, world, rank, local, device, stream, gen,
                             hbm_peak, peak_src, barrier)
+    elif args.workload == "mixed":
+        line = _run_mixed(args, torch, dist, hk, ClockSampler, world, rank, local, device, stream, gen,
+                          hbm_peak, peak_src, barrier)
     elif args.workload == "sample":
         line = _run_sample(args, torch, dist, hk, ClockSampler, world, rank, local, device, stream, gen,
                            hbm_peak, peak_src, barrier)
@@ -737,6 +740,77 @@ def _run_linear(args, torch, dist, hk, ClockSampler, world, rank, local, device,
                 "h2d_bytes_per_step": x.numel() * 2 + attn.numel() * 2,
                 "d2h_bytes_per_step": T * sum(n for nm, n, _ in LINEAR_PROJ if nm != "q_a") * 2},
         "gpu_launches": int(launches), "clocks": clocks,
+    }
+
+
+def _run_mixed(args, torch, dist, hk, ClockSampler, world, rank, local, device, stream, gen, hbm_peak,
+               peak_src, barrier):
+    """Configuration 3's attention: 48 decode lanes (contexts U[2K, 32K], one new row each)
+    and two chunked-prefill segments of 2048 rows (a prompt's first chunk and its second,
+    after 2048 cached rows) in one token stream: pack, append every new latent row, then the
+    tcgen05 MLA kernel with causal rows.  N > 1: independent replicas."""
+    from hyperkernel_b200 import workload as W
+
+    lay = W.config3_attn_layout(seed=0)
+    T, H = lay.num_tokens, HEADS
+    cache = torch.randn((lay.num_slots, DK), generator=gen, device=device).to(torch.bfloat16)
+    q = torch.randn((T, H, DK), generator=gen, device=device).to(torch.bfloat16)
+    kv_new = torch.randn((T, DK), generator=gen, device=device).to(torch.bfloat16)
+    lane_tokens = torch.from_numpy(lay.new_rows.astype(np.int32)).to(device)
+    lane_pos = torch.from_numpy(lay.context.astype(np.int32)).to(device)
+    bt = torch.from_numpy(lay.block_table).to(device)
+    max_kv = int(lay.kv_len.max())
+    scale = 1.0 / math.sqrt(DK)
+    ws = torch.empty(max(hk.mla_workspace_size(lay.lanes, T, H, max_kv), 16), dtype=torch.uint8, device=device)
+    out = torch.empty((T, H, DV), dtype=torch.bfloat16, device=device)
+    lse = torch.empty((T, H), dtype=torch.float32, device=device)
+
+    def step(ev=None):
+        pk = hk.pack(lane_tokens, lane_pos, bt, PAGE, lay.num_pages, T)
+        hk.kv_append_bf16(kv_new, pk["slot_mapping"], cache)
+        if ev is not None:
+            ev[0].record(stream)
+        hk.mla_decode(q, cache, bt, pk["cu_seqlens"], pk["positions"], PAGE, max_kv, scale, out=out, lse=lse,
+                      workspace=ws)
+        if ev is not None:
+            ev[1].record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    hk.check_errors()
+    sampler = ClockSampler(local).start()
+    launches0 = hk.kernel_launches()
+    barrier()
+    t0 = time.perf_counter()
+    ms, attn_ms = _timed(torch, step, args.steps, stream)
+    t1 = time.perf_counter()
+    barrier()
+    launches = hk.kernel_launches() - launches0
+    sampler.stop()
+    clocks = sampler.summary(t0, t1)
+    hk.check_errors()
+    ms, attn_ms = _reduce_max(torch, dist, world, device, ms, attn_ms)
+    rows_kv = int(sum(int(c) * int(r) + int(r) * (int(r) + 1) // 2 for c, r in zip(lay.context, lay.new_rows)))
+    flops = 2 * H * (DK + DV) * rows_kv
+    abytes = int(lay.kv_len.sum()) * DK * 2 + T * H * (DK * 2 + DV * 2 + 4)
+    bf16_peak = _peaks()[1] / 2.0
+    tflops = flops / (attn_ms / 1e3) / 1e12
+    return {
+        "metric": "mixed prefill + decode attention tokens/s (config 3)", "value": T * world * args.steps / (ms / 1e3),
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (seeded)",
+        "config": {"workload": "config3 attention: 48 decode lanes U[2K,32K] + 2 chunked-prefill segments of 2048 "
+                               "rows (after 0 and 2048 cached rows), 4144 rows, 128 heads, MLA 512+64, causal",
+                   "parallelism": f"replicas{world}" if world > 1 else "single",
+                   "kv_rows": int(lay.kv_len.sum()), "query_kv_pairs": rows_kv,
+                   "l2": "the prefill rows re-read their prefixes from L2; no flush (tensor-bound)"},
+        "roofline": {"bound": "tensor", "achieved": tflops, "peak": bf16_peak, "unit": "TFLOP/s",
+                     "frac": tflops / bf16_peak, "traffic": None, "kernel": "tcgen05 attention (hk_mla_decode)",
+                     "kernel_ms": attn_ms, "algorithmic_flops": flops, "algorithmic_bytes": abytes,
+                     "peak_source": f"{peak_src} bf16 burst"},
+        "cpu_baseline": None, "e2e": None, "gpu_launches": int(launches), "clocks": clocks,
     }
 
 

@@ -186,6 +186,17 @@ def config5_layout(seed: int = 0, long_ctx: int = 1 << 20, short_lanes: int = 7,
     return paged_layout(rng, ctx, np.full(len(ctx), rows, np.int64), 64)
 
 
+def config3_attn_layout(seed: int = 0, decode_lanes: int = 48, lo: int = 2048, hi: int = 32768,
+                       chunk: int = 2048, chunk_ctx=(0, 2048)) -> Paged:
+    """Configuration 3's attention batch: decode lanes with contexts U[lo, hi] and one new row,
+    then one lane per chunked-prefill segment of `chunk` rows after chunk_ctx cached rows
+    (the first chunk of a prompt and its second), page 64, scattered pages."""
+    rng = Rng(seed)
+    ctx = np.concatenate([rng.integers(lo, hi, decode_lanes), np.asarray(chunk_ctx)]).astype(np.int64)
+    rows = np.concatenate([np.ones(decode_lanes, np.int64), np.full(len(chunk_ctx), chunk, np.int64)])
+    return paged_layout(rng, ctx, rows, 64)
+
+
 def mla_inputs(lay: Paged, heads: int, seed: int = 1) -> dict:
     """bf16 bit patterns of N(0,1) queries, new latent rows and the cached rows."""
     rng = Rng(seed)

@@ -629,3 +629,13 @@ def test_sample_verify_matches_oracle(hk, cuda, vocab, seed, n):
     got = lp.cpu().numpy()
     assert np.array_equal(got[..., 0:-1:2], want_lp[..., 0:-1:2])      # the ids of the pairs
     assert np.abs(got - want_lp).max() <= 1e-5
+
+
+def test_mla_tcgen05_prefill_chunk_with_decode_lanes(hk, orc, cuda):
+    """Configuration 3's shape in small: decode lanes beside a chunked-prefill segment of 160
+    causal rows after 100 cached rows, through the tcgen05 kernel."""
+    lay = W.config3_attn_layout(seed=41, decode_lanes=3, lo=200, hi=2000, chunk=160, chunk_ctx=(100,))
+    inp = W.mla_inputs(lay, 128, seed=42)
+    out, lse, want, want_lse = _run_mla(hk, orc, cuda, lay, inp, impl=2)
+    assert rel_err(out, want) <= TOL
+    assert np.abs(lse - want_lse).max() <= 1e-3
