@@ -44,7 +44,7 @@ constexpr int kBuckets = 4096;
 constexpr int kCap = 8192;            // elements a gather may hold
 constexpr int kMaxLogprobs = 64;
 constexpr uint64_t kGamma = 0x9E3779B97F4A7C15ull;
-constexpr int kDynSmem = kBuckets * (4 + 8) + kCap * 8;
+constexpr int kDynSmem = kBuckets * (4 + 8) + kCap * 8 + kCap * 8;  // histograms, list, weights
 
 struct RowStat {
   double lse;      // log-sum-exp of the row (temperature 1)
@@ -327,14 +327,13 @@ __device__ void full_sort(const float* x, int vocab, uint32_t* k0, uint32_t* k1,
   }
 }
 
-// The reference draw over m sorted entries (values v(i), indices id(i)), run by one thread
-// with every sum left to right (src/evo2/draw.rs:24-48).
-template <typename V, typename I>
-__device__ int draw_sorted(int m, V v, I id, const hk_sampling& smp, uint64_t bits) {
-  const double temp = (double)smp.temperature;
-  const double most = (double)v(0) / temp;
+// The reference draw over m sorted entries, run by one thread with every sum left to right
+// (src/evo2/draw.rs:24-48): w(i) = exp(value_i / temperature - value_0 / temperature), id(i)
+// the entry's index.
+template <typename W, typename I>
+__device__ int draw_sorted(int m, W w, I id, const hk_sampling& smp, uint64_t bits) {
   double total = 0.0;
-  for (int i = 0; i < m; ++i) total += exp((double)v(i) / temp - most);
+  for (int i = 0; i < m; ++i) total += w(i);
   const double top_p = (double)smp.top_p;
   const bool cut = top_p > 0.0 && top_p < 1.0;
   // the zeroed tail is a suffix: find where it starts, summing from the bottom
@@ -342,21 +341,21 @@ __device__ int draw_sorted(int m, V v, I id, const hk_sampling& smp, uint64_t bi
   if (cut) {
     double below = 0.0;
     for (int i = m - 1; i >= 0; --i) {
-      below += exp((double)v(i) / temp - most) / total;
+      below += w(i) / total;
       if (below <= 1.0 - top_p) keep = i; else break;
     }
   }
   double kept = 0.0;
-  for (int i = 0; i < keep; ++i) kept += exp((double)v(i) / temp - most) / total;
+  for (int i = 0; i < keep; ++i) kept += w(i) / total;
   const double u = (double)bits / 9007199254740992.0 * kept;
   double seen = 0.0;
   for (int i = 0; i < keep; ++i) {
-    seen += exp((double)v(i) / temp - most) / total;
+    seen += w(i) / total;
     if (u < seen) return id(i);
   }
   // the last index with a non-zero probability
   for (int i = keep - 1; i >= 0; --i)
-    if (exp((double)v(i) / temp - most) / total > 0.0) return id(i);
+    if (w(i) / total > 0.0) return id(i);
   return id(0);
 }
 
@@ -368,6 +367,7 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(
   uint32_t* hist_c = reinterpret_cast<uint32_t*>(dyn);
   unsigned long long* hist_w = reinterpret_cast<unsigned long long*>(dyn + kBuckets * 4);
   uint64_t* list = reinterpret_cast<uint64_t*>(dyn + kBuckets * 12);
+  double* wbuf = reinterpret_cast<double*>(dyn + kBuckets * 12 + kCap * 8);
   __shared__ uint32_t shist[256], sbase[256], srun[256];
   __shared__ uint32_t wcnt[kWarps][256];
   __shared__ double red[kWarps];
@@ -455,10 +455,16 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(
         s.top[(int64_t)r * kMaxLogprobs + q] = (int32_t)(uint32_t)L;
         s.topv[(int64_t)r * kMaxLogprobs + q] = key_value((uint32_t)(L >> 32));
       }
-      if (k > 0 && tid == 0)
-        token = draw_sorted(
-            k, [&](int i) { return key_value((uint32_t)(list[i] >> 32)); },
-            [&](int i) { return (int)(uint32_t)list[i]; }, smp, bits);
+      if (k > 0) {  // the exponentials in parallel, the sums by one thread in order
+        const double temp = (double)smp.temperature;
+        const double most = (double)key_value((uint32_t)(list[0] >> 32)) / temp;
+        for (int q = tid; q < k; q += kThreads)
+          wbuf[q] = exp((double)key_value((uint32_t)(list[q] >> 32)) / temp - most);
+        __syncthreads();
+        if (tid == 0)
+          token = draw_sorted(
+              k, [&](int i) { return wbuf[i]; }, [&](int i) { return (int)(uint32_t)list[i]; }, smp, bits);
+      }
     } else {
       full_sort(x, vocab, k0, k0 + vocab, i0, i0 + vocab, shist, sbase, srun, wcnt);
       sorted_full = true;
@@ -468,7 +474,9 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(
       }
       if (k > 0 && tid == 0)
         token = draw_sorted(
-            k, [&](int i) { return key_value(k0[i]); }, [&](int i) { return i0[i]; }, smp, bits);
+            k, [&](int i) { return exp((double)key_value(k0[i]) / (double)smp.temperature -
+                                  (double)key_value(k0[0]) / (double)smp.temperature); },
+            [&](int i) { return i0[i]; }, smp, bits);
     }
     __syncthreads();
   }
@@ -480,7 +488,9 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(
     if (sorted_full) {
       if (tid == 0)
         token = draw_sorted(
-            vocab, [&](int i) { return key_value(k0[i]); }, [&](int i) { return i0[i]; }, smp, bits);
+            vocab, [&](int i) { return exp((double)key_value(k0[i]) / (double)smp.temperature -
+                                  (double)key_value(k0[0]) / (double)smp.temperature); },
+            [&](int i) { return i0[i]; }, smp, bits);
     } else {
       for (int i = tid; i < kBuckets; i += kThreads) { hist_c[i] = 0u; hist_w[i] = 0ull; }
       __syncthreads();
@@ -514,11 +524,14 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(
         }
         __syncthreads();
         bitonic(list, (int)cnt);
+        for (uint32_t q = tid; q < cnt; q += kThreads)
+          wbuf[q] = exp((double)key_value((uint32_t)(list[q] >> 32)) / temp - most);
+        __syncthreads();
         if (tid == 0) {
           double acc = before;
           int pick = -1;
           for (uint32_t q = 0; q < cnt; ++q) {
-            acc += exp((double)key_value((uint32_t)(list[q] >> 32)) / temp - most);
+            acc += wbuf[q];
             if (acc > target) { pick = (int)(uint32_t)list[q]; break; }
           }
           if (pick < 0 && cnt > 0) pick = (int)(uint32_t)list[cnt - 1];
@@ -549,7 +562,9 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(
         full_sort(x, vocab, k0, k0 + vocab, i0, i0 + vocab, shist, sbase, srun, wcnt);
         if (tid == 0)
           token = draw_sorted(
-              vocab, [&](int i) { return key_value(k0[i]); }, [&](int i) { return i0[i]; }, smp, bits);
+              vocab, [&](int i) { return exp((double)key_value(k0[i]) / (double)smp.temperature -
+                                  (double)key_value(k0[0]) / (double)smp.temperature); },
+            [&](int i) { return i0[i]; }, smp, bits);
       }
     }
   }
