@@ -181,6 +181,26 @@ __device__ __forceinline__ uint64_t composite(float v, int i) {
   return ((uint64_t)desc_key(v) << 32) | (uint32_t)i;
 }
 
+// Calls f(i, x[i]) for this thread's share of the row: 16-byte loads, two in flight, when
+// the row allows them.
+template <typename F>
+__device__ __forceinline__ void for_row(const float* __restrict__ x, int vocab, F f) {
+  if ((vocab & 3) == 0 && ((uintptr_t)x & 15) == 0) {
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    const int n4 = vocab >> 2;
+#pragma unroll 2
+    for (int i = threadIdx.x; i < n4; i += kThreads) {
+      const float4 v = x4[i];
+      f(4 * i, v.x);
+      f(4 * i + 1, v.y);
+      f(4 * i + 2, v.z);
+      f(4 * i + 3, v.w);
+    }
+  } else {
+    for (int i = threadIdx.x; i < vocab; i += kThreads) f(i, x[i]);
+  }
+}
+
 struct Row {
   const float* x;
   int vocab;
@@ -388,12 +408,11 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(
   // ---- maximum (first index), minimum, finiteness, log-sum-exp
   float mx = -INFINITY, mn = INFINITY;
   int arg = 0x7fffffff, bad = 0;
-  for (int i = tid; i < vocab; i += kThreads) {
-    const float v = x[i];
-    if (!isfinite(v)) { bad = 1; continue; }
+  for_row(x, vocab, [&](int i, float v) {
+    if (!isfinite(v)) { bad = 1; return; }
     if (v > mx || (v == mx && i < arg)) { mx = v; arg = i; }
     mn = fminf(mn, v);
-  }
+  });
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float m2 = __shfl_xor_sync(0xffffffffu, mx, o);
@@ -432,11 +451,10 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(
     __syncthreads();
     // single-precision exponentials (one rounding each) summed in f64 for the log-sum-exp
     double e = 0.0;
-    for (int i = tid; i < vocab; i += kThreads) {
-      const float v = x[i];
+    for_row(x, vocab, [&](int, float v) {
       atomicAdd(&hist_c[row.bucket(v)], 1u);
       if (n > 0) e += (double)expf(v - mx);
-    }
+    });
     lse = (double)mx + log(block_sum(e, red));  // block_sum's barriers close the histogram
     uint32_t before;
     const int bc = count_cross(hist_c, (uint32_t)c, &before, redu);
@@ -444,10 +462,9 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(
     if (tid == 0) list_n = 0;
     __syncthreads();
     if (upto <= (uint32_t)kCap) {
-      for (int i = tid; i < vocab; i += kThreads) {
-        const float v = x[i];
+      for_row(x, vocab, [&](int i, float v) {
         if (row.bucket(v) <= bc) list[atomicAdd(&list_n, 1)] = composite(v, i);
-      }
+      });
       __syncthreads();
       bitonic(list, (int)upto);
       for (int q = tid; q < n; q += kThreads) {
@@ -497,15 +514,14 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(
       // Bucket sums only place a crossing to within ~1e-12 of the mass; the crossing bucket's
       // own entries are then summed exactly.  So single-precision exponentials suffice here.
       unsigned long long loc = 0;
-      for (int i = tid; i < vocab; i += kThreads) {
-        const float v = x[i];
+      for_row(x, vocab, [&](int, float v) {
         const int bk = row.bucket(v);
         const unsigned long long w =
             __double2ull_rn((double)expf((float)((double)v / temp - most)) * kFix);
         atomicAdd(&hist_c[bk], 1u);
         atomicAdd(&hist_w[bk], w);
         loc += w;
-      }
+      });
       unsigned long long tot_fix;
       block_excl<unsigned long long>(loc, redl, &tot_fix);  // includes the barrier the histograms need
       const double total = (double)tot_fix / kFix;
@@ -518,10 +534,9 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(
         if (cnt > (uint32_t)kCap) return -1;
         if (tid == 0) list_n = 0;
         __syncthreads();
-        for (int i = tid; i < vocab; i += kThreads) {
-          const float v = x[i];
+        for_row(x, vocab, [&](int i, float v) {
           if (row.bucket(v) == bk) list[atomicAdd(&list_n, 1)] = composite(v, i);
-        }
+        });
         __syncthreads();
         bitonic(list, (int)cnt);
         for (uint32_t q = tid; q < cnt; q += kThreads)
