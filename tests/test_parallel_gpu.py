@@ -141,14 +141,21 @@ def _cp(rank, dev):
     kv = int(lay.kv_len[0])
     full, full_lse = hk.mla_decode_fp8(*args, 64, kv, inp["scale"])
     b, e = P.cp_ranges(kv, 2)[rank]
-    o, l = hk.mla_partial_fp8(*args, d(np.array([b], np.int32)), d(np.array([e], np.int32)), 64, kv, inp["scale"])
-    out, lse = P.cp_merge(o.reshape(T * heads, 512), l.reshape(T * heads))
-    torch.cuda.synchronize()
-    hk.check_errors()
-    a = out.float().cpu().numpy()
+    kb, ke = d(np.array([b], np.int32)), d(np.array([e], np.int32))
     f = full.reshape(-1, 512).float().cpu().numpy()
-    assert np.abs(a - f).max() / np.abs(f).max() <= TOL
-    assert (lse.cpu() - full_lse.reshape(-1).cpu()).abs().max().item() <= 1e-3
+    # the CUDA-core FP8 partial, and the tcgen05 partial over this rank's pages converted to bf16
+    o, l = hk.mla_partial_fp8(*args, kb, ke, 64, kv, inp["scale"])
+    mine = d(lay.block_table[0, b // 64:(e + 63) // 64].astype(np.int32))
+    kv_bf16 = torch.zeros((lay.num_slots, 576), dtype=torch.bfloat16, device=dev)
+    hk.kv_dequant_fp8(args[1], args[2], 64, out=kv_bf16, pages=mine)
+    o2, l2 = hk.mla_partial(q, kv_bf16, args[3], args[4], args[5], kb, ke, 64, kv, inp["scale"])
+    for oo, ll in ((o, l), (o2, l2)):
+        out, lse = P.cp_merge(oo.reshape(T * heads, 512), ll.reshape(T * heads))
+        torch.cuda.synchronize()
+        hk.check_errors()
+        a = out.float().cpu().numpy()
+        assert np.abs(a - f).max() / np.abs(f).max() <= TOL
+        assert (lse.cpu() - full_lse.reshape(-1).cpu()).abs().max().item() <= 1e-3
 
 
 @pytest.mark.skipif(not _two_gpus(), reason="needs two GPUs")
