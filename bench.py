@@ -189,6 +189,8 @@ def main(argv=None):
     ap.add_argument("--no-e2e", action="store_true", help="skip the host round trip leg")
     ap.add_argument("--workload", default="decode", choices=["decode", "moe", "linear", "longctx", "sample", "mixed"])
     ap.add_argument("--experts", type=int, default=None, help="profiling override of config 4's 256 experts")
+    ap.add_argument("--full-dequant", action="store_true",
+                    help="longctx: convert the whole FP8 pool to bf16 every step (no mirror)")
     ap.add_argument("--ep", default="peer", choices=["peer", "nccl"],
                     help="expert-parallel exchange: NVLink stores from libhk kernels, or NCCL all-to-allv")
     args = ap.parse_args(argv)
@@ -592,20 +594,28 @@ def _run_longctx(args, torch, dist, hk, par, ClockSampler, world, rank, local, d
         [lay.block_table[i, int(begin[i]) // PAGE:(int(end[i]) + PAGE - 1) // PAGE] for i in range(L)]
     ).astype(np.int32)).to(device)
 
+    # The tcgen05 kernel reads a page-blocked bf16 mirror of the FP8 pool (of this rank's pages
+    # on N > 1): converted once here, then kept current by converting each step's appended rows
+    # (--full-dequant converts the whole pool, or the rank's pages, every step instead).
+    if kv_bf16 is not None:
+        hk.kv_dequant_fp8(cache, scales, PAGE, out=kv_bf16, pages=None if world == 1 else my_pages)
+
     def step(ev=None):
         pk = hk.pack(lane_tokens, lane_pos, bt, PAGE, lay.num_pages, T)
         hk.kv_append_fp8(kv_new, pk["slot_mapping"], cache, scales)
         if ev is not None:
             ev[0].record(stream)
+        if kv_bf16 is not None:
+            if args.full_dequant:
+                hk.kv_dequant_fp8(cache, scales, PAGE, out=kv_bf16, pages=None if world == 1 else my_pages)
+            else:
+                hk.kv_dequant_fp8_rows(cache, scales, pk["slot_mapping"], kv_bf16, PAGE)
         if world == 1:
-            # one GPU: the FP8 pool as page-blocked bf16, then the tcgen05 kernel
-            hk.kv_dequant_fp8(cache, scales, PAGE, out=kv_bf16)
             o, lse = hk.mla_decode(q, kv_bf16, bt, pk["cu_seqlens"], pk["positions"], PAGE, max_kv, scale)
         elif portable:
             o, lse = hk.mla_partial_fp8(q, cache, scales, bt, pk["cu_seqlens"], pk["positions"], kb, ke, PAGE,
                                         max_kv, scale)
         else:
-            hk.kv_dequant_fp8(cache, scales, PAGE, out=kv_bf16, pages=my_pages)
             o, lse = hk.mla_partial(q, kv_bf16, bt, pk["cu_seqlens"], pk["positions"], kb, ke, PAGE, max_kv, scale)
         if ev is not None:
             ev[1].record(stream)
@@ -646,11 +656,11 @@ def _run_longctx(args, torch, dist, hk, par, ClockSampler, world, rank, local, d
                    "l2": "0.75 GB of FP8 KV, no flush"},
         "roofline": {"bound": "tensor", "achieved": tflops, "peak": bf16_peak, "unit": "TFLOP/s",
                      "frac": tflops / bf16_peak, "traffic": None,
-                     "kernel": ("FP8 pool -> blocked bf16 (hk_kv_dequant_fp8) + tcgen05 attention (hk_mla_decode)"
-                                if world == 1 else
-                                "CUDA-core FP8 partial attention on rank 0 (hk_mla_partial_fp8)" if portable else
-                                "rank 0's FP8 pages -> blocked bf16 (hk_kv_dequant_fp8, page list) + tcgen05 "
-                                "partial attention (hk_mla_partial)"),
+                     "kernel": ("CUDA-core FP8 partial attention on rank 0 (hk_mla_partial_fp8)" if portable else
+                                ("FP8 pool -> blocked bf16 every step (hk_kv_dequant_fp8" if args.full_dequant else
+                                 "bf16 mirror of the FP8 pool, the step's appended rows converted "
+                                 "(hk_kv_dequant_fp8_rows") + ") + tcgen05 attention ("
+                                + ("hk_mla_decode)" if world == 1 else "hk_mla_partial over rank 0's ranges)")),
                      "kernel_ms": attn_ms, "algorithmic_flops": flops, "peak_source": f"{peak_src} bf16 burst",
                      "fp8_kv_gbs": abytes / (attn_ms / 1e3) / 1e9, "fp8_kv_frac_of_hbm": abytes / (attn_ms / 1e3) / 1e9 / hbm_peak},
         "cpu_baseline": None,

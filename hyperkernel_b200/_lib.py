@@ -34,6 +34,7 @@ SIGNATURES = {
     "hk_kv_append_bf16": (C.c_int, [P, P, I32, I32, I32, P, I64, P]),
     "hk_kv_append_fp8": (C.c_int, [P, P, I32, I32, P, P, I64, P]),
     "hk_kv_dequant_fp8": (C.c_int, [P, P, I64, I32, I32, P, I64, P, P]),
+    "hk_kv_dequant_fp8_rows": (C.c_int, [P, P, I64, I32, I32, P, I64, P, P]),
     "hk_kv_append_f32": (C.c_int, [P, P, P, I32, I32, P, P, I64, P]),
     "hk_gqa_decode_f32": (C.c_int, [P, P, P, P, I32, P, P, I32, I32, I32, I32, I32, I32, I64, F32, P, P, P]),
     "hk_mla_workspace_size": (SZ, [I32, I32, I32, I32]),
@@ -196,6 +197,14 @@ def kv_append_fp8(kv_new, slot_mapping, kv_cache, kv_scale, num_tokens=None, str
     n = kv_new.shape[0] if num_tokens is None else num_tokens
     call("hk_kv_append_fp8", ptr(kv_new), ptr(slot_mapping), n, kv_new.shape[-1], ptr(kv_cache),
          ptr(kv_scale), kv_cache.shape[0], stream_ptr(stream))
+
+
+def kv_dequant_fp8_rows(kv_cache, kv_scale, slots, out, page_rows=64, stream=None):
+    """Refreshes the rows `slots` (int32 device tensor) of the bf16 mirror `out`."""
+    slots_n, row = kv_cache.shape
+    call("hk_kv_dequant_fp8_rows", ptr(kv_cache), ptr(kv_scale), slots_n, row, page_rows, ptr(slots),
+         slots.shape[0], ptr(_u16(out)), stream_ptr(stream))
+    return out
 
 
 def kv_dequant_fp8(kv_cache, kv_scale, page_rows=64, out=None, pages=None, stream=None):

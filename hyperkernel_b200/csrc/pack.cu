@@ -164,12 +164,22 @@ __global__ void append_kv_kernel(const uint4* __restrict__ k_src, const uint4* _
 __global__ void dequant_fp8_blocked_kernel(const uint2* __restrict__ src, const float* __restrict__ scales,
                                            int64_t num_slots, int32_t row_vec, int32_t page_rows,
                                            const int32_t* __restrict__ pages, int64_t num_pages,
-                                           int64_t rows, uint4* __restrict__ dst, unsigned long long* err) {
+                                           const int32_t* __restrict__ slots, int64_t rows,
+                                           uint4* __restrict__ dst, unsigned long long* err) {
   const int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (i >= rows) return;
-  int64_t s = i;  // cache row; with a page list, row i % page_rows of listed page i / page_rows
-  if (pages != nullptr) {
+  // cache row: i itself; with a page list, row i % page_rows of listed page i / page_rows;
+  // with a slot list, slots[i]
+  int64_t s = i;
+  if (slots != nullptr) {
+    const int32_t sl = slots[i];
+    if (sl < 0 || sl >= num_slots) {
+      if (lane == 0) hk_flag(err, hk::kErrAttnPage, (unsigned)i);
+      return;
+    }
+    s = sl;
+  } else if (pages != nullptr) {
     const int32_t pg = pages[i / page_rows];
     if (pg < 0 || (int64_t)pg * page_rows >= num_slots || pg >= num_pages) {
       if (lane == 0) hk_flag(err, hk::kErrAttnPage, (unsigned)(i / page_rows));
@@ -301,8 +311,28 @@ int hk_kv_dequant_fp8(const uint8_t* kv_fp8, const float* kv_scale, int64_t num_
   if (rows == 0) return HK_OK;
   const int64_t threads = rows * 32;
   dequant_fp8_blocked_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
-      (const uint2*)kv_fp8, kv_scale, num_slots, row_elems / 8, page_rows, pages, num_slots / page_rows, rows,
-      (uint4*)kv_bf16, hk::err_word());
+      (const uint2*)kv_fp8, kv_scale, num_slots, row_elems / 8, page_rows, pages, num_slots / page_rows, nullptr,
+      rows, (uint4*)kv_bf16, hk::err_word());
+  HK_TRY_LAUNCH("dequant_fp8_blocked_kernel");
+  return HK_OK;
+}
+
+int hk_kv_dequant_fp8_rows(const uint8_t* kv_fp8, const float* kv_scale, int64_t num_slots, int32_t row_elems,
+                           int32_t page_rows, const int32_t* slots, int64_t n_rows, uint16_t* kv_bf16,
+                           void* stream) {
+  HK_TRY(hk::ensure_device());
+  HK_REQUIRE(kv_fp8 && kv_scale && kv_bf16 && slots, "hk_kv_dequant_fp8_rows: null pointer");
+  HK_REQUIRE(num_slots >= 0 && page_rows > 0 && num_slots % page_rows == 0 && row_elems > 0 && row_elems % 64 == 0,
+             "hk_kv_dequant_fp8_rows: num_slots %lld (a multiple of page_rows %d), row_elems %d (a multiple of 64)",
+             (long long)num_slots, page_rows, row_elems);
+  HK_REQUIRE(((uintptr_t)kv_fp8 % 8 == 0) && ((uintptr_t)kv_bf16 % 16 == 0),
+             "hk_kv_dequant_fp8_rows: misaligned buffers");
+  HK_REQUIRE(n_rows >= 0, "hk_kv_dequant_fp8_rows: negative row count");
+  if (n_rows == 0) return HK_OK;
+  const int64_t threads = n_rows * 32;
+  dequant_fp8_blocked_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+      (const uint2*)kv_fp8, kv_scale, num_slots, row_elems / 8, page_rows, nullptr, num_slots / page_rows, slots,
+      n_rows, (uint4*)kv_bf16, hk::err_word());
   HK_TRY_LAUNCH("dequant_fp8_blocked_kernel");
   return HK_OK;
 }

@@ -107,6 +107,12 @@ int hk_kv_append_fp8(const uint16_t* kv_new, const int32_t* slot_mapping, int32_
 int hk_kv_dequant_fp8(const uint8_t* kv_fp8, const float* kv_scale, int64_t num_slots,
                       int32_t row_elems, int32_t page_rows, const int32_t* pages, int64_t n_pages,
                       uint16_t* kv_bf16, void* stream);
+/* The same conversion for the listed cache rows only (device slots[n_rows], e.g. a step's
+ * slot_mapping after hk_kv_append_fp8): keeps a bf16 mirror of an FP8 pool current at the
+ * cost of the rows appended, instead of converting the pool every step. */
+int hk_kv_dequant_fp8_rows(const uint8_t* kv_fp8, const float* kv_scale, int64_t num_slots,
+                           int32_t row_elems, int32_t page_rows, const int32_t* slots,
+                           int64_t n_rows, uint16_t* kv_bf16, void* stream);
 
 /* GQA rows (config 1): k_new/v_new[T][kv_heads*head_dim] fp32 -> k_cache/v_cache[slot][..]. */
 int hk_kv_append_f32(const float* k_new, const float* v_new, const int32_t* slot_mapping,

@@ -639,3 +639,22 @@ def test_mla_tcgen05_prefill_chunk_with_decode_lanes(hk, orc, cuda):
     out, lse, want, want_lse = _run_mla(hk, orc, cuda, lay, inp, impl=2)
     assert rel_err(out, want) <= TOL
     assert np.abs(lse - want_lse).max() <= 1e-3
+
+
+def test_kv_dequant_fp8_rows_keeps_a_mirror_current(hk, orc, cuda):
+    """A bf16 mirror converted once, then refreshed row by row after FP8 appends, equals a
+    full conversion of the pool bit for bit."""
+    rng = W.Rng(43)
+    slots = 64 * 6
+    kv = W.f32_to_bf16_bits(rng.normal(slots * 576).astype(np.float32)).reshape(slots, 576)
+    c8 = torch.zeros((slots, 576), dtype=torch.uint8, device=cuda)
+    s8 = torch.zeros(slots, dtype=torch.float32, device=cuda)
+    hk.kv_append_fp8(bf16_dev(kv, cuda), dev(np.arange(slots, dtype=np.int32), cuda), c8, s8)
+    mirror = hk.kv_dequant_fp8(c8, s8)
+    new = W.f32_to_bf16_bits(rng.normal(7 * 576).astype(np.float32) * 3).reshape(7, 576)
+    where = dev(np.array([5, 64, 65, 200, 383, 0, 127], np.int32), cuda)
+    hk.kv_append_fp8(bf16_dev(new, cuda), where, c8, s8)
+    hk.kv_dequant_fp8_rows(c8, s8, where, mirror)
+    full = hk.kv_dequant_fp8(c8, s8)
+    hk.check_errors()
+    assert torch.equal(mirror.view(torch.int16), full.view(torch.int16))
