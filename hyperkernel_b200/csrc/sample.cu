@@ -28,9 +28,10 @@
 //     where the count reaches n / k; with top_k > 0 the whole reference computation then
 //     runs on those k entries in shared memory, sums left to right as in the reference;
 //   * top_k == 0: the top-p cut and the draw are running-sum crossings over the whole row:
-//     bucket sums (f64) up to the crossing bucket, then that bucket's elements in order.
-//     Those sums are not left to right, so a draw could differ from the reference only where
-//     u lies within a few ulps of a boundary.
+//     bucket sums up to the crossing bucket (f64 exponentials, rounded to 2^-40 and summed
+//     exactly as integers), then that bucket's entries in order with the reference's
+//     arithmetic.  Those sums are not left to right, so a draw could differ from the
+//     reference only where u lies within ~1e-12 of a boundary.
 // A crossing bucket with more than kCap elements (near-constant rows) falls back to a full
 // stable radix sort of the row in global scratch.
 #include "common.cuh"
@@ -511,13 +512,14 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(
     } else {
       for (int i = tid; i < kBuckets; i += kThreads) { hist_c[i] = 0u; hist_w[i] = 0ull; }
       __syncthreads();
-      // Bucket sums only place a crossing to within ~1e-12 of the mass; the crossing bucket's
-      // own entries are then summed exactly.  So single-precision exponentials suffice here.
+      // The sum of the buckets before the crossing one shifts every running sum inside it, so
+      // a draw agrees with the reference only if that sum is accurate to far below the
+      // probability of one entry: f64 exponentials (the fixed point adds ~1e-12).
+      const double inv_t = 1.0 / temp;
       unsigned long long loc = 0;
       for_row(x, vocab, [&](int, float v) {
         const int bk = row.bucket(v);
-        const unsigned long long w =
-            __double2ull_rn((double)expf((float)((double)v / temp - most)) * kFix);
+        const unsigned long long w = __double2ull_rn(exp((double)v * inv_t - most) * kFix);
         atomicAdd(&hist_c[bk], 1u);
         atomicAdd(&hist_w[bk], w);
         loc += w;

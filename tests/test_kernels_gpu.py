@@ -658,3 +658,24 @@ def test_kv_dequant_fp8_rows_keeps_a_mirror_current(hk, orc, cuda):
     full = hk.kv_dequant_fp8(c8, s8)
     hk.check_errors()
     assert torch.equal(mirror.view(torch.int16), full.view(torch.int16))
+
+
+def test_sample_verify_flat_rows_draw_exactly(hk, cuda):
+    """Near-flat rows over a 129,280-token vocabulary, where an entry's probability (~1e-5)
+    is tiny: every draw still matches the oracle's left-to-right arithmetic (64 lanes, plain
+    temperature and top-p 0.95)."""
+    from oracle import sample as S
+
+    rng = np.random.default_rng(44)
+    lanes, V = 64, 129280
+    logits = (rng.standard_normal((lanes, V)) * 0.3).astype(np.float32)
+    cu = np.arange(lanes + 1, dtype=np.int32)
+    samplings = [dict(temperature=1.0, top_k=0, top_p=1.0 if b % 2 else 0.95) for b in range(lanes)]
+    states = [int(v) for v in rng.integers(0, 2**63, lanes)]
+    drafts = np.zeros((lanes, 0), np.int32)
+    want_ids, _, want_states = S.sample_verify(logits, cu, samplings, states, drafts, 1, 0)
+    st = torch.tensor(np.array(states, dtype=np.uint64).view(np.int64), device=cuda)
+    ids, _ = hk.sample_verify(dev(logits, cuda), dev(cu, cuda), hk.sampling_array(samplings, cuda), st,
+                              torch.zeros(1, dtype=torch.int32, device=cuda), 1, 0)
+    hk.check_errors()
+    assert np.array_equal(ids.cpu().numpy(), want_ids)
