@@ -594,53 +594,69 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(
   }
 }
 
+// One warp per lane: lane 0 walks the chain, then the warp writes the ids and logprob rows.
 __global__ void sample_chain_kernel(const float* __restrict__ logits, int32_t vocab,
                                     const int32_t* __restrict__ cu, int32_t lanes, int32_t block,
                                     const hk_sampling* __restrict__ sampling, uint64_t* state,
                                     const int32_t* __restrict__ drafts, int32_t n_logprobs,
                                     int32_t* __restrict__ ids, float* __restrict__ lp, Scratch s,
                                     unsigned long long* err) {
-  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  const int b = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  const int t32 = threadIdx.x & 31;
   if (b >= lanes) return;
   const int width = 2 * n_logprobs + 1;
-  for (int j = 0; j < block; ++j) {
-    ids[(int64_t)b * block + j] = -2;
-    if (n_logprobs > 0)
-      for (int q = 0; q < width; ++q) lp[((int64_t)b * block + j) * width + q] = 0.f;
-  }
   const int r0 = cu[b], rows = cu[b + 1] - r0;
-  if (rows < 0 || rows > block) {
-    hk_flag(err, hk::kErrMoeRow, (unsigned)b);
+  const bool bad_rows = rows < 0 || rows > block;
+  // accepted rows, and whether the last of them is a non-finite row (-1)
+  int m = 0, last_bad = 0;
+  if (t32 == 0 && !bad_rows) {
+    const bool sampled = !greedy(sampling[b]);
+    uint64_t draws = 0;
+    for (int j = 0; j < rows; ++j) {
+      const RowStat rs = s.stats[r0 + j];
+      ++m;
+      if (rs.flags & 1) {
+        last_bad = 1;
+        break;
+      }
+      draws += sampled ? 1 : 0;
+      if (j + 1 < rows && rs.token != drafts[(int64_t)b * (block - 1) + j]) break;
+    }
+    state[b] += draws * kGamma;
+  }
+  if (bad_rows) {
+    if (t32 == 0) hk_flag(err, hk::kErrMoeRow, (unsigned)b);
+    for (int j = t32; j < block; j += 32) ids[(int64_t)b * block + j] = -2;
     return;
   }
-  const bool sampled = !greedy(sampling[b]);
-  uint64_t draws = 0;
-  for (int j = 0; j < rows; ++j) {
+  m = __shfl_sync(0xffffffffu, m, 0);
+  last_bad = __shfl_sync(0xffffffffu, last_bad, 0);
+  for (int j = t32; j < block; j += 32) {
+    int32_t v = -2;
+    if (j < m) v = (j == m - 1 && last_bad) ? -1 : s.stats[r0 + j].token;
+    ids[(int64_t)b * block + j] = v;
+  }
+  if (n_logprobs == 0) return;
+  for (int j = 0; j < block; ++j) {
+    float* row = lp + ((int64_t)b * block + j) * width;
+    const bool live = j < m && !(j == m - 1 && last_bad);
+    if (!live) {
+      for (int q = t32; q < width; q += 32) row[q] = 0.f;
+      continue;
+    }
     const int r = r0 + j;
     const RowStat rs = s.stats[r];
-    int32_t* out = ids + (int64_t)b * block + j;
-    if (rs.flags & 1) {
-      *out = -1;
-      break;
-    }
-    const int t = rs.token;
-    draws += sampled ? 1 : 0;
-    *out = t;
-    if (n_logprobs > 0) {
-      float* row = lp + ((int64_t)b * block + j) * width;
-      for (int q = 0; q < n_logprobs; ++q) {
-        if (q < rs.ntop) {
-          row[2 * q] = (float)s.top[(int64_t)r * kMaxLogprobs + q];
-          row[2 * q + 1] = (float)((double)s.topv[(int64_t)r * kMaxLogprobs + q] - rs.lse);
-        } else {
-          row[2 * q] = -1.f;
-        }
+    for (int q = t32; q < n_logprobs; q += 32) {
+      if (q < rs.ntop) {
+        row[2 * q] = (float)s.top[(int64_t)r * kMaxLogprobs + q];
+        row[2 * q + 1] = (float)((double)s.topv[(int64_t)r * kMaxLogprobs + q] - rs.lse);
+      } else {
+        row[2 * q] = -1.f;
+        row[2 * q + 1] = 0.f;
       }
-      row[2 * n_logprobs] = (float)((double)logits[(int64_t)r * vocab + t] - rs.lse);
     }
-    if (j + 1 < rows && t != drafts[(int64_t)b * (block - 1) + j]) break;
+    if (t32 == 0) row[2 * n_logprobs] = (float)((double)logits[(int64_t)r * vocab + rs.token] - rs.lse);
   }
-  state[b] += draws * kGamma;
 }
 
 }  // namespace
@@ -679,7 +695,7 @@ int hk_sample_verify(const float* logits, int32_t vocab, const int32_t* cu_rows,
                                                              sampling, state, n_logprobs, s, hk::err_word());
     HK_TRY_LAUNCH("sample_rows_kernel");
   }
-  sample_chain_kernel<<<(num_lanes + 63) / 64, 64, 0, st>>>(logits, vocab, cu_rows, num_lanes, block, sampling,
+  sample_chain_kernel<<<(num_lanes + 3) / 4, 128, 0, st>>>(logits, vocab, cu_rows, num_lanes, block, sampling,
                                                             state, drafts, n_logprobs, ids, lp, s, hk::err_word());
   HK_TRY_LAUNCH("sample_chain_kernel");
   return HK_OK;
