@@ -23,8 +23,11 @@
 #include <stdint.h>
 #include <string.h>
 
+#include <atomic>
+#include <chrono>
 #include <deque>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "common.cuh"
@@ -167,8 +170,9 @@ __device__ __forceinline__ uint64_t rd64(const uint8_t* b, uint32_t at) {
 // Applies n_msgs encoded commands in order (one CTA; commands of a batch can depend on each
 // other, e.g. a Seat then the Prompt of the same lane).  Prompt replies go to replies[] in
 // order.
-__global__ void apply_kernel(Dev d, const uint8_t* stream, uint64_t stream_bytes, int n_msgs,
-                             int32_t* replies) {
+// Applies n_msgs messages of an encoded stream (every thread of one CTA calls it).
+__device__ void apply_messages(const Dev& d, const uint8_t* stream, uint64_t stream_bytes, int n_msgs,
+                               int32_t* replies) {
   __shared__ int s_lane, s_pos, s_ok, s_reply;
   int n_replies = 0;
   for (int m = 0; m < n_msgs; ++m) {
@@ -261,12 +265,15 @@ __global__ void apply_kernel(Dev d, const uint8_t* stream, uint64_t stream_bytes
   }
 }
 
+__global__ void apply_kernel(Dev d, const uint8_t* stream, uint64_t stream_bytes, int n_msgs,
+                             int32_t* replies) {
+  apply_messages(d, stream, stream_bytes, n_msgs, replies);
+}
+
 // One decode step (the test device's step, tests/engine.rs:173-193): each live lane with
 // reserved rows left emits 1 + ((step + lane) mod block) tokens, stopping early at its
 // reserved rows or the context's last position.  out[lane][block], -2 past a lane's tokens.
-__global__ void step_kernel(Dev d, uint32_t step, int32_t* out) {
-  const int l = blockIdx.x * blockDim.x + threadIdx.x;
-  if (l >= d.width) return;
+__device__ void step_lane(const Dev& d, uint32_t step, int l, int32_t* out) {
   int32_t* o = out + (size_t)l * d.block;
   for (int k = 0; k < d.block; ++k) o[k] = -2;
   LaneState st = d.lanes[l];
@@ -289,6 +296,105 @@ __global__ void step_kernel(Dev d, uint32_t step, int32_t* out) {
   }
   d.lanes[l].pos = (int32_t)pos;
   d.lanes[l].tok = tok;
+}
+
+__global__ void step_kernel(Dev d, uint32_t step, int32_t* out) {
+  const int l = blockIdx.x * blockDim.x + threadIdx.x;
+  if (l < d.width) step_lane(d, step, l, out);
+}
+
+// ---------------------------------------------------------------------------------------
+// ring transport: a resident executor polls a mailbox in host-mapped memory
+// ---------------------------------------------------------------------------------------
+
+constexpr uint32_t kItemApply = 1, kItemStep = 2, kItemExit = 3;
+constexpr int kExecThreads = 256;
+
+// The mailbox, in pinned host memory mapped into the device's address space.  The host
+// fills the item fields, then publishes `posted`; the executor runs the item, copies the
+// device error word into `err` and publishes `done`.  Pointers are the device's view.
+struct RingCtl {
+  unsigned long long posted;
+  unsigned long long done;
+  unsigned long long err[3];
+  uint32_t kind, n_msgs;
+  unsigned long long bytes;
+  uint32_t step, out_base;
+  unsigned long long src, dst, out;
+};
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long now_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// One CTA.  Waits for items (polling with a short sleep) and exits when none arrives for
+// idle_ns or on an exit item; the host relaunches it when it posts to an exited executor.
+__global__ void __launch_bounds__(kExecThreads, 1)
+    executor_kernel(Dev d, RingCtl* ctl, unsigned long long idle_ns) {
+  __shared__ int s_go;
+  __shared__ uint32_t s_kind, s_n, s_step, s_base;
+  __shared__ unsigned long long s_bytes, s_src, s_dst, s_out;
+  unsigned long long next = ld_acquire_sys(&ctl->done);
+  for (;;) {
+    if (threadIdx.x == 0) {
+      const unsigned long long t0 = now_ns();
+      int go = 0;
+      for (;;) {
+        if (ld_acquire_sys(&ctl->posted) > next) {
+          go = 1;
+          break;
+        }
+        if (now_ns() - t0 > idle_ns) break;
+        __nanosleep(500);
+      }
+      if (go) {
+        const volatile RingCtl* c = ctl;
+        s_kind = c->kind;
+        s_n = c->n_msgs;
+        s_bytes = c->bytes;
+        s_step = c->step;
+        s_base = c->out_base;
+        s_src = c->src;
+        s_dst = c->dst;
+        s_out = c->out;
+      }
+      s_go = go;
+    }
+    __syncthreads();
+    if (!s_go) break;
+    if (s_kind == kItemApply) {
+      // the stream into device memory first: mapped host memory is read uncached, once
+      const volatile uint32_t* src = reinterpret_cast<const volatile uint32_t*>(s_src);
+      uint32_t* dst = reinterpret_cast<uint32_t*>(s_dst);
+      for (unsigned long long i = threadIdx.x; i < s_bytes / 4; i += kExecThreads) dst[i] = src[i];
+      __syncthreads();
+      apply_messages(d, reinterpret_cast<const uint8_t*>(s_dst), s_bytes, (int)s_n,
+                     reinterpret_cast<int32_t*>(s_out) + s_base);
+    } else if (s_kind == kItemStep) {
+      for (int l = threadIdx.x; l < d.width; l += kExecThreads) step_lane(d, s_step, l, reinterpret_cast<int32_t*>(s_out));
+    }
+    __threadfence_system();  // this thread's replies, before `done`
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      volatile RingCtl* c = ctl;
+      for (int k = 0; k < 3; ++k) c->err[k] = reinterpret_cast<volatile unsigned long long*>(d.err)[k];
+      __threadfence_system();
+      st_release_sys(&ctl->done, next + 1);
+    }
+    ++next;
+    if (s_kind == kItemExit) break;
+    __syncthreads();
+  }
 }
 
 // ---------------------------------------------------------------------------------------
@@ -545,6 +651,14 @@ struct hk_handle {
   std::vector<hk_event> events;
   std::vector<int32_t> ids;
   std::string error;
+  // ring transport (cfg.transport == HK_TRANSPORT_RING)
+  bool ring = false;
+  cudaStream_t exec_stream = nullptr;
+  RingCtl* ctl = nullptr;      // host view of the mapped mailbox
+  RingCtl* d_ctl = nullptr;    // device view
+  uint8_t* d_h_stream = nullptr;  // device view of h_stream (mapped)
+  int32_t* d_h_out = nullptr;     // device view of h_out (mapped)
+  unsigned long long posted = 0;
 };
 
 namespace {
@@ -566,29 +680,31 @@ int grow_device(uint8_t** p, size_t* cap, size_t need) {
   return HK_OK;
 }
 
-int grow_host(uint8_t** p, size_t* cap, size_t need) {
+// Pinned host memory, also mapped into the device's address space when `mapped_dev` is given.
+int grow_host(uint8_t** p, size_t* cap, size_t need, uint8_t** mapped_dev = nullptr) {
   if (need <= *cap) return HK_OK;
   if (*p) cudaFreeHost(*p);
   *p = nullptr;
   *cap = 0;
   size_t n = 1 << 16;
   while (n < need) n *= 2;
-  HK_TRY_CUDA(cudaMallocHost(p, n));
+  if (mapped_dev) {
+    HK_TRY_CUDA(cudaHostAlloc(p, n, cudaHostAllocMapped));
+    HK_TRY_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(mapped_dev), *p, 0));
+  } else {
+    HK_TRY_CUDA(cudaMallocHost(p, n));
+  }
   *cap = n;
   return HK_OK;
 }
 
 // Copies `words` of d_out and the three error words back and synchronises; a recorded fault
 // becomes HK_EDEVICE with the test device's wording.
-int readback(hk_handle* h, size_t words) {
-  if (words) HK_TRY_CUDA(cudaMemcpyAsync(h->h_out, h->d_out, 4 * words, cudaMemcpyDeviceToHost, h->stream));
-  HK_TRY_CUDA(cudaMemcpyAsync(h->h_err, h->dev.err, 3 * sizeof(unsigned long long), cudaMemcpyDeviceToHost,
-                              h->stream));
-  HK_TRY_CUDA(cudaStreamSynchronize(h->stream));
-  const unsigned long long w = h->h_err[0];
+int fault_status(const unsigned long long* err) {
+  const unsigned long long w = err[0];
   if (!(w >> 63)) return HK_OK;
   const unsigned site = (unsigned)((w >> 32) & 0x7fffffff);
-  const long long lane = (long long)h->h_err[1], pos = (long long)h->h_err[2];
+  const long long lane = (long long)err[1], pos = (long long)err[2];
   switch (site) {
     case kFaultScratchWrite:
       return hk::fail(HK_EDEVICE, "lane %lld writes position %lld to the scratch page", lane, pos);
@@ -611,10 +727,61 @@ int readback(hk_handle* h, size_t words) {
   }
 }
 
+int readback(hk_handle* h, size_t words) {
+  if (words) HK_TRY_CUDA(cudaMemcpyAsync(h->h_out, h->d_out, 4 * words, cudaMemcpyDeviceToHost, h->stream));
+  HK_TRY_CUDA(cudaMemcpyAsync(h->h_err, h->dev.err, 3 * sizeof(unsigned long long), cudaMemcpyDeviceToHost,
+                              h->stream));
+  HK_TRY_CUDA(cudaStreamSynchronize(h->stream));
+  return fault_status(h->h_err);
+}
+
+constexpr unsigned long long kExecIdleNs = 50000000ull;  // an executor exits after 50 ms idle
+constexpr double kRingTimeoutS = 30.0;
+
+int launch_executor(hk_handle* h) {
+  executor_kernel<<<1, kExecThreads, 0, h->exec_stream>>>(h->dev, h->d_ctl, kExecIdleNs);
+  HK_TRY_LAUNCH("executor_kernel");
+  return HK_OK;
+}
+
+// Posts one item to the executor and waits for it (relaunching an executor that went idle).
+int ring_run(hk_handle* h, uint32_t kind, uint32_t n_msgs, uint64_t bytes, uint32_t step, uint32_t out_base) {
+  volatile RingCtl* c = h->ctl;
+  c->kind = kind;
+  c->n_msgs = n_msgs;
+  c->bytes = bytes;
+  c->step = step;
+  c->out_base = out_base;
+  c->src = (unsigned long long)(uintptr_t)h->d_h_stream;
+  c->dst = (unsigned long long)(uintptr_t)h->d_stream;
+  c->out = (unsigned long long)(uintptr_t)h->d_h_out;
+  std::atomic_thread_fence(std::memory_order_seq_cst);
+  c->posted = ++h->posted;
+  std::atomic_thread_fence(std::memory_order_seq_cst);
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    if (c->done >= h->posted) break;
+    const cudaError_t q = cudaStreamQuery(h->exec_stream);
+    if (q == cudaSuccess) {
+      if (c->done >= h->posted) break;
+      HK_TRY(launch_executor(h));  // it had gone idle before the item was posted
+    } else if (q != cudaErrorNotReady) {
+      return hk::cuda_fail(q, "ring executor");
+    }
+    if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > kRingTimeoutS)
+      return hk::fail(HK_EDEVICE, "ring executor gave no answer in %.0f s", kRingTimeoutS);
+    std::this_thread::yield();
+  }
+  std::atomic_thread_fence(std::memory_order_seq_cst);
+  unsigned long long err[3];
+  for (int k = 0; k < 3; ++k) err[k] = c->err[k];
+  return fault_status(err);
+}
+
 // Encodes and applies a batch; appends its Prompted replies to the events.
 int apply_batch(hk_handle* h, const std::vector<Cmd>& batch) {
   const size_t bytes = stream_bytes(batch, h->cfg.chunk);
-  HK_TRY(grow_host(&h->h_stream, &h->h_stream_cap, bytes));
+  HK_TRY(grow_host(&h->h_stream, &h->h_stream_cap, bytes, h->ring ? &h->d_h_stream : nullptr));
   HK_TRY(grow_device(&h->d_stream, &h->d_stream_cap, bytes));
   std::string err;
   if (!encode_commands(h->cfg, batch, h->h_stream, &err)) return hk::fail(HK_EINVAL, "%s", err.c_str());
@@ -628,7 +795,26 @@ int apply_batch(hk_handle* h, const std::vector<Cmd>& batch) {
     h->h_out = nullptr;
     h->out_cap = base + std::max<size_t>(prompts, 64);
     HK_TRY_CUDA(cudaMalloc(&h->d_out, 4 * h->out_cap));
-    HK_TRY_CUDA(cudaMallocHost(&h->h_out, 4 * h->out_cap));
+    if (h->ring) {
+      HK_TRY_CUDA(cudaHostAlloc(&h->h_out, 4 * h->out_cap, cudaHostAllocMapped));
+      HK_TRY_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&h->d_h_out), h->h_out, 0));
+    } else {
+      HK_TRY_CUDA(cudaMallocHost(&h->h_out, 4 * h->out_cap));
+    }
+  }
+  if (h->ring) {
+    HK_TRY(ring_run(h, kItemApply, (uint32_t)batch.size(), bytes, 0, (uint32_t)base));
+    size_t k = 0;
+    for (const Cmd& c : batch) {
+      if (c.c.kind != HK_CMD_PROMPT) continue;
+      hk_event e{};
+      e.kind = HK_EV_PROMPTED;
+      e.lane = c.c.lane;
+      e.token = h->h_out[base + k++];
+      e.clipped = h->cfg.clip;
+      h->events.push_back(e);
+    }
+    return HK_OK;
   }
   HK_TRY_CUDA(cudaMemcpyAsync(h->d_stream, h->h_stream, bytes, cudaMemcpyHostToDevice, h->stream));
   apply_kernel<<<1, 256, 0, h->stream>>>(h->dev, h->d_stream, bytes, (int)batch.size(), h->d_out + base);
@@ -653,12 +839,16 @@ int apply_batch(hk_handle* h, const std::vector<Cmd>& batch) {
 }
 
 int run_step(hk_handle* h) {
-  const int threads = 128;
-  const int blocks = (int)((h->cfg.width + threads - 1) / threads);
-  step_kernel<<<blocks, threads, 0, h->stream>>>(h->dev, h->s, h->d_out);
-  HK_TRY_LAUNCH("step_kernel");
   const size_t words = (size_t)h->cfg.width * h->cfg.block;
-  HK_TRY(readback(h, words));
+  if (h->ring) {
+    HK_TRY(ring_run(h, kItemStep, 0, 0, h->s, 0));
+  } else {
+    const int threads = 128;
+    const int blocks = (int)((h->cfg.width + threads - 1) / threads);
+    step_kernel<<<blocks, threads, 0, h->stream>>>(h->dev, h->s, h->d_out);
+    HK_TRY_LAUNCH("step_kernel");
+    HK_TRY(readback(h, words));
+  }
   hk_event e{};
   e.kind = HK_EV_STEP;
   e.step = h->s;
@@ -721,6 +911,17 @@ int run(hk_handle* h) {
 
 void release(hk_handle* h) {
   if (!h) return;
+  if (h->ring && h->ctl && h->exec_stream) {
+    if (cudaStreamQuery(h->exec_stream) == cudaErrorNotReady) {  // ask a running executor to exit
+      volatile RingCtl* c = h->ctl;
+      c->kind = kItemExit;
+      std::atomic_thread_fence(std::memory_order_seq_cst);
+      c->posted = ++h->posted;
+    }
+    cudaStreamSynchronize(h->exec_stream);
+  }
+  if (h->ctl) cudaFreeHost(h->ctl);
+  if (h->exec_stream) cudaStreamDestroy(h->exec_stream);
   cudaFree(h->dev.rows);
   cudaFree(h->dev.pool);
   cudaFree(h->dev.windows);
@@ -754,6 +955,8 @@ int check_config(const hk_config* c) {
   HK_REQUIRE(c->pages >= 1 && c->window_pages >= 1 && c->pages < (1ull << 31) && c->window_pages < (1ull << 31),
              "pool sizes must be in 1..2^31");
   HK_REQUIRE((uint64_t)c->entries * c->page_rows < (1ull << 31), "a row covers at most 2^31 positions");
+  HK_REQUIRE(c->transport == HK_TRANSPORT_LAUNCH || c->transport == HK_TRANSPORT_RING,
+             "transport %u: HK_TRANSPORT_LAUNCH (0) or HK_TRANSPORT_RING (1)", c->transport);
   return HK_OK;
 }
 
@@ -807,6 +1010,20 @@ int hk_open(const hk_config* config, hk_handle** handle) {
   if (e == cudaSuccess) e = cudaMemsetAsync(d.err, 0, 4 * sizeof(unsigned long long), h->stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(h->stream);
   if (e != cudaSuccess) return fail(hk::cuda_fail(e, "hk_open"));
+  if (c.transport == HK_TRANSPORT_RING) {
+    h->ring = true;
+    cudaFreeHost(h->h_out);
+    h->h_out = nullptr;
+    e = cudaStreamCreateWithFlags(&h->exec_stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaHostAlloc(&h->h_out, 4 * h->out_cap, cudaHostAllocMapped);
+    if (e == cudaSuccess) e = cudaHostGetDevicePointer(reinterpret_cast<void**>(&h->d_h_out), h->h_out, 0);
+    if (e == cudaSuccess) e = cudaHostAlloc(&h->ctl, sizeof(RingCtl), cudaHostAllocMapped);
+    if (e == cudaSuccess) e = cudaHostGetDevicePointer(reinterpret_cast<void**>(&h->d_ctl), h->ctl, 0);
+    if (e != cudaSuccess) return fail(hk::cuda_fail(e, "hk_open (ring)"));
+    memset(h->ctl, 0, sizeof(RingCtl));
+    const int rc = launch_executor(h);
+    if (rc != HK_OK) return fail(rc);
+  }
   *handle = h;
   return HK_OK;
 }

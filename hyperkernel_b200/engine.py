@@ -50,7 +50,8 @@ class Config(C.Structure):
     """hk_config: the device kernel's pool and model shape."""
     _fields_ = [("model", U32), ("page_rows", U32), ("entries", U32), ("window", U32),
                 ("width", U32), ("context", U32), ("chunk", U32), ("block", U32),
-                ("pages", U64), ("window_pages", U64), ("clip", I32), ("device", I32)]
+                ("pages", U64), ("window_pages", U64), ("clip", I32), ("device", I32),
+                ("transport", U32), ("reserved", U32)]
 
 
 class EngineConfig(C.Structure):

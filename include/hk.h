@@ -413,7 +413,20 @@ typedef struct {
     uint64_t window_pages;   /* window page pool size, unit 0 = scratch */
     int32_t clip;            /* the `clipped` flag the test model returns with prompt replies */
     int32_t device;          /* CUDA device ordinal */
+    uint32_t transport;      /* HK_TRANSPORT_LAUNCH or HK_TRANSPORT_RING */
+    uint32_t reserved;
 } hk_config;
+
+/* How hk_drain drives the device.  LAUNCH: one kernel launch per applied batch and per step,
+ * each followed by a synchronous read-back.  RING: a resident executor kernel (one CTA)
+ * polls a mailbox in pinned, device-mapped host memory (the reference's device-polled
+ * request ring, src/gpu/ring.rs, src/gpu/feed.rs:104-155): the host posts each batch's
+ * encoded bytes or a step and waits for the executor's answer, which it writes, with the
+ * step's ids and prompt replies, into mapped host memory.  The executor exits after 50 ms
+ * without work (every poll is bounded) and is relaunched by the next post; hk_close stops
+ * it.  Both transports produce the same events. */
+#define HK_TRANSPORT_LAUNCH 0
+#define HK_TRANSPORT_RING 1
 
 /* Opens a device kernel: allocates the pools, the block-table rows and the lane state on
  * `device` and returns its handle.  One handle per process and GPU; a handle's calls are

@@ -270,10 +270,11 @@ def engine_config(sc):
                            budget=sc.plan.budget, every=sc.plan.every, headroom=sc.plan.headroom)
 
 
-def device_config(sc, device=0):
+def device_config(sc, device=0, transport=0):
+    """transport 0: a launch per batch and step; 1: the resident ring executor."""
     return H.Config(model=H.MODEL_FNV, page_rows=PAGE_ROWS, entries=ENTRIES, window=ENTRIES, width=WIDTH,
                     context=CONTEXT, chunk=CHUNK, block=sc.block, pages=sc.pages, window_pages=sc.windows,
-                    clip=int(sc.clip), device=device)
+                    clip=int(sc.clip), device=device, transport=transport)
 
 
 def run_hk(sc, port) -> Result:

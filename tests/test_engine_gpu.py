@@ -21,10 +21,13 @@ from oracle import engine as E
 pytestmark = pytest.mark.gpu
 
 
+@pytest.mark.parametrize("transport", [0, 1], ids=["launch", "ring"])
 @pytest.mark.parametrize("sc", P.scenarios(), ids=repr)
-def test_device_matches_oracle_share_by_share(cuda, sc):
+def test_device_matches_oracle_share_by_share(cuda, sc, transport):
+    """Both transports: a kernel launch per batch and step, and the resident executor that
+    polls a mailbox in mapped host memory."""
     want = P.run_oracle(sc)
-    dev = H.Device(P.device_config(sc))
+    dev = H.Device(P.device_config(sc, transport=transport))
     try:
         got = P.run_hk(sc, P.DevicePort(dev))
     finally:
@@ -32,12 +35,13 @@ def test_device_matches_oracle_share_by_share(cuda, sc):
     P.assert_same(got, want)
 
 
+@pytest.mark.parametrize("transport", [0, 1], ids=["launch", "ring"])
 @pytest.mark.parametrize("name", ["prefixes_default", "small_pool_budget_keep", "drafts_clips"])
-def test_device_through_native_ops(cuda, name):
+def test_device_through_native_ops(cuda, name, transport):
     """The engine calling the device kernel through hk_kernel_ops_of: no Python in the loop."""
     sc = next(s for s in P.scenarios() if s.name == name)
     want = P.run_oracle(sc)
-    dev = H.Device(P.device_config(sc))
+    dev = H.Device(P.device_config(sc, transport=transport))
     try:
         got = P.run_hk_native(sc, dev)
     finally:
@@ -102,10 +106,11 @@ def test_device_refuses_a_share_out_of_step(cuda):
         dev.close()
 
 
-def test_device_reports_a_chunk_without_window_pages(cuda):
+@pytest.mark.parametrize("transport", [0, 1], ids=["launch", "ring"])
+def test_device_reports_a_chunk_without_window_pages(cuda, transport):
     """tests/engine.rs:153-160: a prompt chunk whose window entry is the scratch window page is
     a device-side violation; hk_drain fails with the reference's wording."""
-    dev = H.Device(P.device_config(P.Scenario("x", [])))
+    dev = H.Device(P.device_config(P.Scenario("x", []), transport=transport))
     try:
         samp = H.Sampling(0.0, 1.0, 0, 0, 0)
         share, keep = H.make_share(0, 2, [
@@ -122,10 +127,11 @@ def test_device_reports_a_chunk_without_window_pages(cuda):
         dev.close()
 
 
-def test_device_prompt_and_decode_by_hand(cuda):
+@pytest.mark.parametrize("transport", [0, 1], ids=["launch", "ring"])
+def test_device_prompt_and_decode_by_hand(cuda, transport):
     """One lane through the raw boundary: its prompt reply and decode tokens are the model's
     `next` over the sequence, steps stop at the reserved rows, and Idle follows."""
-    dev = H.Device(P.device_config(P.Scenario("x", [])))
+    dev = H.Device(P.device_config(P.Scenario("x", []), transport=transport))
     try:
         samp = H.Sampling(0.0, 1.0, 0, 0, 0)
         prompt = [11, 12, 13, 14, 15]
@@ -152,5 +158,45 @@ def test_device_prompt_and_decode_by_hand(cuda):
         got = [ids[4 * i] for i in range(2)]  # lane 0's first id of each step (width 4, block 1)
         assert got == want
         assert evs[-1][0] == H.EV_IDLE
+    finally:
+        dev.close()
+
+
+def test_ring_executor_is_relaunched_after_going_idle(cuda):
+    """The resident executor exits after 50 ms without work; the next drain's first post
+    relaunches it and the lane carries on where it stopped."""
+    import time
+
+    dev = H.Device(P.device_config(P.Scenario("x", []), transport=1))
+    try:
+        samp = H.Sampling(0.0, 1.0, 0, 0, 0)
+        prompt = [21, 22, 23]
+        row = [1, 2] + [0] * 14 + [1, 2] + [0] * 14
+        share, keep = H.make_share(0, 0, [
+            (H.CMD_PAGES, 0, 0, 3, row, (0, 0, 0), None),
+            (H.CMD_SEAT, 0, 0, 0, [], (7, 7, 7), samp),
+            (H.CMD_PROMPT, 0, 0, 0, prompt, (0, 0, 0), None),
+        ])
+        assert dev.push_raw(share) == 0
+        rc, evs, _ = _drain(dev)
+        assert rc == 0, _lib.last_error()
+        seq = list(prompt)
+        assert evs[0] == (H.EV_PROMPTED, 0, 0, E.next_token(seq))
+        seq.append(E.next_token(seq))
+        time.sleep(0.3)  # the executor has gone idle and exited
+        share, keep = H.make_share(1, 3, [
+            (H.CMD_PAGES, 0, 0, 5, row, (0, 0, 0), None),  # positions 3 and 4 reserved
+            (H.CMD_START, 0, 0, 0, [], (0, 0, 0), None),
+        ])
+        assert dev.push_raw(share) == 0
+        rc, evs, ids = _drain(dev)
+        assert rc == 0, _lib.last_error()
+        steps = [e for e in evs if e[0] == H.EV_STEP]
+        assert len(steps) == 2
+        want = []
+        for _ in range(2):
+            want.append(E.next_token(seq))
+            seq.append(want[-1])
+        assert [ids[4 * i] for i in range(2)] == want
     finally:
         dev.close()
