@@ -34,6 +34,8 @@
 //     reference only where u lies within ~1e-12 of a boundary.
 // A crossing bucket with more than kCap elements (near-constant rows) falls back to a full
 // stable radix sort of the row in global scratch.
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 
 namespace {
@@ -380,10 +382,15 @@ __device__ int draw_sorted(int m, W w, I id, const hk_sampling& smp, uint64_t bi
   return id(0);
 }
 
+// One cluster of CTAs per row: each CTA reads a contiguous slice of the row, the slices'
+// histograms are merged over distributed shared memory, and the gathers land in the first
+// CTA's list, which sorts and draws.  Every read of another CTA's shared memory is followed
+// by a cluster barrier before that memory changes or its CTA leaves.
 __global__ void __launch_bounds__(kThreads) sample_rows_kernel(
     const float* __restrict__ logits, int32_t vocab, const int32_t* __restrict__ cu, int32_t lanes,
     int32_t rows, const hk_sampling* __restrict__ sampling, const uint64_t* __restrict__ state,
     int32_t n_logprobs, Scratch s, unsigned long long* err) {
+  namespace cg = cooperative_groups;
   extern __shared__ __align__(16) uint8_t dyn[];
   uint32_t* hist_c = reinterpret_cast<uint32_t*>(dyn);
   unsigned long long* hist_w = reinterpret_cast<unsigned long long*>(dyn + kBuckets * 4);
@@ -397,19 +404,29 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(
   __shared__ float smax[kWarps], smin[kWarps];
   __shared__ int sarg[kWarps], sbad[kWarps];
   __shared__ int list_n, result;
-  const int r = blockIdx.x;
-  if (r >= rows) return;
+  __shared__ float p_max, p_min;       // this CTA's slice: max, min, first argmax, non-finite
+  __shared__ int p_arg, p_bad;
+  __shared__ double p_e, res_incl;     // slice log-sum-exp partial; the leader's crossing sum
+  cg::cluster_group cl = cg::this_cluster();
+  const int C = (int)cl.num_blocks(), rank = (int)cl.block_rank();
+  const int r = blockIdx.x / C;
+  if (r >= rows) return;  // whole clusters only: rows * C blocks are launched
+  const bool leader = rank == 0;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int b = lane_of(cu, lanes, r);
   const hk_sampling smp = sampling[b];
   const int j = r - cu[b];  // the row's position in its lane: draws before it
   const float* x = logits + (int64_t)r * vocab;
   RowStat* st = s.stats + r;
+  // this CTA's slice, a multiple of 4 entries long
+  const int seg = (((vocab + C - 1) / C) + 3) & ~3;
+  const int lo = min(vocab, rank * seg), hi = min(vocab, lo + seg);
+  auto for_slice = [&](auto f) { for_row(x + lo, hi - lo, [&](int i, float v) { f(lo + i, v); }); };
 
-  // ---- maximum (first index), minimum, finiteness, log-sum-exp
+  // ---- maximum (first index), minimum, finiteness: slices, then merged in rank order
   float mx = -INFINITY, mn = INFINITY;
   int arg = 0x7fffffff, bad = 0;
-  for_row(x, vocab, [&](int i, float v) {
+  for_slice([&](int i, float v) {
     if (!isfinite(v)) { bad = 1; return; }
     if (v > mx || (v == mx && i < arg)) { mx = v; arg = i; }
     mn = fminf(mn, v);
@@ -424,16 +441,52 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(
   }
   if (lane == 0) { smax[warp] = mx; smin[warp] = mn; sarg[warp] = arg; sbad[warp] = bad; }
   __syncthreads();
-  mx = smax[0]; mn = smin[0]; arg = sarg[0]; bad = sbad[0];
-  for (int w = 1; w < kWarps; ++w) {
-    if (smax[w] > mx || (smax[w] == mx && sarg[w] < arg)) { mx = smax[w]; arg = sarg[w]; }
-    mn = fminf(mn, smin[w]);
-    bad |= sbad[w];
+  if (tid == 0) {
+    float m = smax[0], n_ = smin[0];
+    int a = sarg[0], bd = sbad[0];
+    for (int w = 1; w < kWarps; ++w) {
+      if (smax[w] > m || (smax[w] == m && sarg[w] < a)) { m = smax[w]; a = sarg[w]; }
+      n_ = fminf(n_, smin[w]);
+      bd |= sbad[w];
+    }
+    p_max = m; p_min = n_; p_arg = a; p_bad = bd;
   }
+  cl.sync();
+  mx = -INFINITY; mn = INFINITY; arg = 0x7fffffff; bad = 0;
+  for (int q = 0; q < C; ++q) {
+    const float m2 = *cl.map_shared_rank(&p_max, q);
+    const int a2 = *cl.map_shared_rank(&p_arg, q);
+    if (m2 > mx || (m2 == mx && a2 < arg)) { mx = m2; arg = a2; }
+    mn = fminf(mn, *cl.map_shared_rank(&p_min, q));
+    bad |= *cl.map_shared_rank(&p_bad, q);
+  }
+  cl.sync();
   if (bad) {
-    if (tid == 0) { st->flags = 1; st->argmax = 0; st->token = -1; st->ntop = 0; st->lse = 0.0; }
+    if (leader && tid == 0) { st->flags = 1; st->argmax = 0; st->token = -1; st->ntop = 0; st->lse = 0.0; }
     return;
   }
+  // Replaces this CTA's histograms with the cluster's sums (bins tid, tid + kThreads, ...).
+  auto merge_hist = [&](bool weights) {
+    constexpr int kPer = kBuckets / kThreads;
+    uint32_t mc[kPer];
+    unsigned long long mw[kPer];
+    for (int q = 0; q < kPer; ++q) { mc[q] = 0u; mw[q] = 0ull; }
+    cl.sync();
+    for (int o = 0; o < C; ++o) {
+      const uint32_t* rc = cl.map_shared_rank(hist_c, o);
+      const unsigned long long* rw = cl.map_shared_rank(hist_w, o);
+      for (int q = 0; q < kPer; ++q) {
+        mc[q] += rc[tid + q * kThreads];
+        if (weights) mw[q] += rw[tid + q * kThreads];
+      }
+    }
+    cl.sync();
+    for (int q = 0; q < kPer; ++q) {
+      hist_c[tid + q * kThreads] = mc[q];
+      if (weights) hist_w[tid + q * kThreads] = mw[q];
+    }
+    __syncthreads();
+  };
   double lse = 0.0;  // log-sum-exp for the logprob rows (computed with the top-n pass)
   const bool sampled = !greedy(smp);
   const Row row{x, vocab, mx, mx > mn ? (float)kBuckets / (mx - mn) : 0.f};
@@ -444,6 +497,8 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(
   bool sorted_full = false;
   uint32_t* k0 = s.keys + (int64_t)r * 2 * vocab;
   int32_t* i0 = s.idx + (int64_t)r * 2 * vocab;
+  uint64_t* list0 = cl.map_shared_rank(list, 0);
+  int* list_n0 = cl.map_shared_rank(&list_n, 0);
 
   // ---- the top max(n, k) in order: buckets up to the count crossing, gathered and sorted
   const int c = max(n, k);
@@ -452,51 +507,60 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(
     __syncthreads();
     // single-precision exponentials (one rounding each) summed in f64 for the log-sum-exp
     double e = 0.0;
-    for_row(x, vocab, [&](int, float v) {
+    for_slice([&](int, float v) {
       atomicAdd(&hist_c[row.bucket(v)], 1u);
       if (n > 0) e += (double)expf(v - mx);
     });
-    lse = (double)mx + log(block_sum(e, red));  // block_sum's barriers close the histogram
+    const double e_cta = block_sum(e, red);  // its barriers close the histogram
+    if (tid == 0) p_e = e_cta;
+    merge_hist(false);  // begins with a cluster barrier, so every p_e is in place
+    double e_all = 0.0;
+    for (int q = 0; q < C; ++q) e_all += *cl.map_shared_rank(&p_e, q);
+    lse = (double)mx + log(e_all);
     uint32_t before;
     const int bc = count_cross(hist_c, (uint32_t)c, &before, redu);
     const uint32_t upto = before + hist_c[bc];  // elements in buckets 0..bc
-    if (tid == 0) list_n = 0;
-    __syncthreads();
+    if (leader && tid == 0) list_n = 0;
+    cl.sync();  // the p_e reads are done and the leader's list is empty
     if (upto <= (uint32_t)kCap) {
-      for_row(x, vocab, [&](int i, float v) {
-        if (row.bucket(v) <= bc) list[atomicAdd(&list_n, 1)] = composite(v, i);
+      for_slice([&](int i, float v) {
+        if (row.bucket(v) <= bc) list0[atomicAdd(list_n0, 1)] = composite(v, i);
       });
-      __syncthreads();
-      bitonic(list, (int)upto);
-      for (int q = tid; q < n; q += kThreads) {
-        const uint64_t L = list[q];
-        s.top[(int64_t)r * kMaxLogprobs + q] = (int32_t)(uint32_t)L;
-        s.topv[(int64_t)r * kMaxLogprobs + q] = key_value((uint32_t)(L >> 32));
-      }
-      if (k > 0) {  // the exponentials in parallel, the sums by one thread in order
-        const double temp = (double)smp.temperature;
-        const double most = (double)key_value((uint32_t)(list[0] >> 32)) / temp;
-        for (int q = tid; q < k; q += kThreads)
-          wbuf[q] = exp((double)key_value((uint32_t)(list[q] >> 32)) / temp - most);
-        __syncthreads();
-        if (tid == 0)
-          token = draw_sorted(
-              k, [&](int i) { return wbuf[i]; }, [&](int i) { return (int)(uint32_t)list[i]; }, smp, bits);
+      cl.sync();
+      if (leader) {
+        bitonic(list, (int)upto);
+        for (int q = tid; q < n; q += kThreads) {
+          const uint64_t L = list[q];
+          s.top[(int64_t)r * kMaxLogprobs + q] = (int32_t)(uint32_t)L;
+          s.topv[(int64_t)r * kMaxLogprobs + q] = key_value((uint32_t)(L >> 32));
+        }
+        if (k > 0) {  // the exponentials in parallel, the sums by one thread in order
+          const double temp = (double)smp.temperature;
+          const double most = (double)key_value((uint32_t)(list[0] >> 32)) / temp;
+          for (int q = tid; q < k; q += kThreads)
+            wbuf[q] = exp((double)key_value((uint32_t)(list[q] >> 32)) / temp - most);
+          __syncthreads();
+          if (tid == 0)
+            token = draw_sorted(
+                k, [&](int i) { return wbuf[i]; }, [&](int i) { return (int)(uint32_t)list[i]; }, smp, bits);
+        }
       }
     } else {
-      full_sort(x, vocab, k0, k0 + vocab, i0, i0 + vocab, shist, sbase, srun, wcnt);
       sorted_full = true;
-      for (int q = tid; q < n; q += kThreads) {
-        s.top[(int64_t)r * kMaxLogprobs + q] = i0[q];
-        s.topv[(int64_t)r * kMaxLogprobs + q] = key_value(k0[q]);
+      if (leader) {
+        full_sort(x, vocab, k0, k0 + vocab, i0, i0 + vocab, shist, sbase, srun, wcnt);
+        for (int q = tid; q < n; q += kThreads) {
+          s.top[(int64_t)r * kMaxLogprobs + q] = i0[q];
+          s.topv[(int64_t)r * kMaxLogprobs + q] = key_value(k0[q]);
+        }
+        if (k > 0 && tid == 0)
+          token = draw_sorted(
+              k, [&](int i) { return exp((double)key_value(k0[i]) / (double)smp.temperature -
+                                    (double)key_value(k0[0]) / (double)smp.temperature); },
+              [&](int i) { return i0[i]; }, smp, bits);
       }
-      if (k > 0 && tid == 0)
-        token = draw_sorted(
-            k, [&](int i) { return exp((double)key_value(k0[i]) / (double)smp.temperature -
-                                  (double)key_value(k0[0]) / (double)smp.temperature); },
-            [&](int i) { return i0[i]; }, smp, bits);
     }
-    __syncthreads();
+    cl.sync();
   }
 
   // ---- top_k == 0: the top-p cut and the draw as running-sum crossings over the whole row
@@ -504,7 +568,7 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(
     const double temp = (double)smp.temperature;
     const double most = (double)mx / temp;
     if (sorted_full) {
-      if (tid == 0)
+      if (leader && tid == 0)
         token = draw_sorted(
             vocab, [&](int i) { return exp((double)key_value(k0[i]) / (double)smp.temperature -
                                   (double)key_value(k0[0]) / (double)smp.temperature); },
@@ -516,16 +580,18 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(
       // a draw agrees with the reference only if that sum is accurate to far below the
       // probability of one entry: f64 exponentials (the fixed point adds ~1e-12).
       const double inv_t = 1.0 / temp;
-      unsigned long long loc = 0;
-      for_row(x, vocab, [&](int, float v) {
+      for_slice([&](int, float v) {
         const int bk = row.bucket(v);
         const unsigned long long w = __double2ull_rn(exp((double)v * inv_t - most) * kFix);
         atomicAdd(&hist_c[bk], 1u);
         atomicAdd(&hist_w[bk], w);
-        loc += w;
       });
+      __syncthreads();
+      merge_hist(true);
+      unsigned long long loc = 0;
+      for (int q = tid; q < kBuckets; q += kThreads) loc += hist_w[q];
       unsigned long long tot_fix;
-      block_excl<unsigned long long>(loc, redl, &tot_fix);  // includes the barrier the histograms need
+      block_excl<unsigned long long>(loc, redl, &tot_fix);
       const double total = (double)tot_fix / kFix;
       // Running-sum crossing of `target` (unnormalised): the element, and the sum through it.
       auto cross = [&](double target, double* incl) -> int {
@@ -534,31 +600,33 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(
         const uint32_t cnt = hist_c[bk];
         __syncthreads();
         if (cnt > (uint32_t)kCap) return -1;
-        if (tid == 0) list_n = 0;
-        __syncthreads();
-        for_row(x, vocab, [&](int i, float v) {
-          if (row.bucket(v) == bk) list[atomicAdd(&list_n, 1)] = composite(v, i);
+        if (leader && tid == 0) list_n = 0;
+        cl.sync();
+        for_slice([&](int i, float v) {
+          if (row.bucket(v) == bk) list0[atomicAdd(list_n0, 1)] = composite(v, i);
         });
-        __syncthreads();
-        bitonic(list, (int)cnt);
-        for (uint32_t q = tid; q < cnt; q += kThreads)
-          wbuf[q] = exp((double)key_value((uint32_t)(list[q] >> 32)) / temp - most);
-        __syncthreads();
-        if (tid == 0) {
-          double acc = before;
-          int pick = -1;
-          for (uint32_t q = 0; q < cnt; ++q) {
-            acc += wbuf[q];
-            if (acc > target) { pick = (int)(uint32_t)list[q]; break; }
+        cl.sync();
+        if (leader) {
+          bitonic(list, (int)cnt);
+          for (uint32_t q = tid; q < cnt; q += kThreads)
+            wbuf[q] = exp((double)key_value((uint32_t)(list[q] >> 32)) / temp - most);
+          __syncthreads();
+          if (tid == 0) {
+            double acc = before;
+            int pick = -1;
+            for (uint32_t q = 0; q < cnt; ++q) {
+              acc += wbuf[q];
+              if (acc > target) { pick = (int)(uint32_t)list[q]; break; }
+            }
+            if (pick < 0 && cnt > 0) pick = (int)(uint32_t)list[cnt - 1];
+            result = pick;
+            res_incl = acc;
           }
-          if (pick < 0 && cnt > 0) pick = (int)(uint32_t)list[cnt - 1];
-          result = pick;
-          red[0] = acc;
         }
-        __syncthreads();
-        *incl = red[0];
-        const int out = result;
-        __syncthreads();
+        cl.sync();
+        *incl = *cl.map_shared_rank(&res_incl, 0);
+        const int out = *cl.map_shared_rank(&result, 0);
+        cl.sync();
         return out;
       };
       double kept = total;
@@ -575,17 +643,17 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(
         ok = t >= 0;
         token = t;
       }
-      if (!ok) {  // a crossing bucket too full to gather: sort the row
+      if (!ok && leader) {  // a crossing bucket too full to gather: sort the row
         full_sort(x, vocab, k0, k0 + vocab, i0, i0 + vocab, shist, sbase, srun, wcnt);
         if (tid == 0)
           token = draw_sorted(
               vocab, [&](int i) { return exp((double)key_value(k0[i]) / (double)smp.temperature -
                                   (double)key_value(k0[0]) / (double)smp.temperature); },
-            [&](int i) { return i0[i]; }, smp, bits);
+              [&](int i) { return i0[i]; }, smp, bits);
       }
     }
   }
-  if (tid == 0) {
+  if (leader && tid == 0) {
     st->flags = 0;
     st->argmax = arg;
     st->token = sampled ? token : arg;
@@ -691,9 +759,25 @@ int hk_sample_verify(const float* logits, int32_t vocab, const int32_t* cu_rows,
     attr = true;
   }
   if (num_rows > 0) {
-    sample_rows_kernel<<<num_rows, kThreads, kDynSmem, st>>>(logits, vocab, cu_rows, num_lanes, num_rows,
-                                                             sampling, state, n_logprobs, s, hk::err_word());
-    HK_TRY_LAUNCH("sample_rows_kernel");
+    // a cluster of up to 8 CTAs per row, as many as the SMs allow in one wave
+    int per_row = hk::sm_count() / num_rows;
+    per_row = per_row < 1 ? 1 : per_row > 8 ? 8 : per_row;
+    if (per_row > vocab / 4) per_row = vocab / 4 > 0 ? vocab / 4 : 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(num_rows * per_row));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kDynSmem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)per_row;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    HK_TRY_CUDA(cudaLaunchKernelEx(&cfg, sample_rows_kernel, logits, vocab, cu_rows, num_lanes, num_rows, sampling,
+                                   (const uint64_t*)state, n_logprobs, s, hk::err_word()));
+    hk::note_launch();
   }
   sample_chain_kernel<<<(num_lanes + 3) / 4, 128, 0, st>>>(logits, vocab, cu_rows, num_lanes, block, sampling,
                                                             state, drafts, n_logprobs, ids, lp, s, hk::err_word());
