@@ -35,6 +35,8 @@ SIGNATURES = {
     "hk_kv_append_fp8": (C.c_int, [P, P, I32, I32, P, P, I64, P]),
     "hk_kv_dequant_fp8": (C.c_int, [P, P, I64, I32, I32, P, I64, P, P]),
     "hk_kv_dequant_fp8_rows": (C.c_int, [P, P, I64, I32, I32, P, I64, P, P]),
+    "hk_pages_within": (C.c_int, [P, U64, P, P]),
+    "hk_plan_pools": (C.c_int, [P, P, P, P, P, P]),
     "hk_kv_append_f32": (C.c_int, [P, P, P, I32, I32, P, P, I64, P]),
     "hk_gqa_decode_f32": (C.c_int, [P, P, P, P, I32, P, P, I32, I32, I32, I32, I32, I32, I64, F32, P, P, P]),
     "hk_mla_workspace_size": (SZ, [I32, I32, I32, I32]),
@@ -448,3 +450,52 @@ def rope_table(rows, dim, base, original_seq_len, factor, beta_fast, beta_slow):
     check(lib().hk_rope_table(rows, dim, base, original_seq_len, factor, beta_fast, beta_slow,
                               t.ctypes.data_as(C.c_void_p)))
     return t
+
+
+# ---- pool sizing (host arithmetic; hk_plan_pools reads cudaMemGetInfo when free == 0) ----
+
+UNIT_PAGE, UNIT_WINDOW = 0, 1
+
+
+class PoolStateC(C.Structure):
+    _fields_ = [("home", C.c_uint32), ("unit", C.c_uint32), ("bytes", C.c_uint64)]
+
+
+class PoolSizingC(C.Structure):
+    _fields_ = [("pages", C.c_uint64), ("window_pages", C.c_uint64), ("entries", C.c_uint64),
+                ("slots", C.c_uint64), ("states", C.POINTER(PoolStateC)), ("n_states", C.c_size_t)]
+
+
+class PoolBudgetC(C.Structure):
+    _fields_ = [("free", C.c_uint64), ("other", C.c_uint64), ("slack", C.c_uint64),
+                ("lanes", C.c_uint32), ("context", C.c_uint32), ("device", C.c_int32),
+                ("reserved", C.c_uint32)]
+
+
+def _pool_c(pages, window_pages, entries, slots, states):
+    arr = (PoolStateC * max(len(states), 1))(*[PoolStateC(h, u, b) for h, u, b in states])
+    return PoolSizingC(pages, window_pages, entries, slots, arr, len(states)), arr
+
+
+def pages_within(pages, window_pages, entries, states, nbytes, slots=0):
+    """(pages, window_pages) for a pool of `states` [(home, unit, bytes per unit)] within
+    `nbytes`, or None when the bytes hold no sequence (src/gpu/load.rs:903-908)."""
+    pool, _keep = _pool_c(pages, window_pages, entries, slots, states)
+    n, w = C.c_size_t(), C.c_size_t()
+    rc = lib().hk_pages_within(C.byref(pool), nbytes, C.byref(n), C.byref(w))
+    if rc == HK_ESPACE:
+        return None
+    check(rc)
+    return n.value, w.value
+
+
+def plan_pools(pages, window_pages, entries, slots, states, *, lanes, context, other=0, slack=0,
+               free=0, device=0):
+    """(pages, window_pages, slots, used bytes) of the loader's pool plan; free = 0 reads the
+    device's free memory.  Raises HKError with the reference's wording."""
+    pool, _keep = _pool_c(pages, window_pages, entries, slots, states)
+    b = PoolBudgetC(free, other, slack, lanes, context, device, 0)
+    n, w, sl, used = C.c_size_t(), C.c_size_t(), C.c_size_t(), C.c_uint64()
+    check(lib().hk_plan_pools(C.byref(pool), C.byref(b), C.byref(n), C.byref(w), C.byref(sl),
+                              C.byref(used)))
+    return n.value, w.value, sl.value, used.value

@@ -435,6 +435,51 @@ int hk_open(const hk_config* config, hk_handle** handle);
 void hk_close(hk_handle* handle);
 /* Kernel::pools: (pages, window_pages). */
 int hk_pools(const hk_handle* handle, size_t* pages, size_t* window_pages);
+/* Pool sizing: how many pages (and window pages) a GPU's free memory holds for a bundle's
+ * pools.  Each pool state costs `bytes` per unit of its kind (a page of `page_rows` token rows,
+ * or a window page); the window pages are taken whole, the rest of the bytes go to pages, at
+ * most the bundle's `pages`, and the result must hold more than one sequence's row of
+ * `entries` pages.  Replaces pages_within (src/gpu/load.rs:903-908). */
+#define HK_UNIT_PAGE 0
+#define HK_UNIT_WINDOW 1
+
+typedef struct {
+    uint32_t home;           /* PoolState.home: the device buffer the state lives in */
+    uint32_t unit;           /* HK_UNIT_PAGE or HK_UNIT_WINDOW */
+    uint64_t bytes;          /* bytes of this state per unit */
+} hk_pool_state;
+
+typedef struct {
+    uint64_t pages;          /* Pool.pages: the bundle's most pages */
+    uint64_t window_pages;   /* Pool.window_pages */
+    uint64_t entries;        /* Pool.entries: page entries of one row */
+    uint64_t slots;          /* Pool.slots: lane slots (lanes + 1 scratch) */
+    const hk_pool_state* states;
+    size_t n_states;
+} hk_pool_sizing;
+
+/* pages_within: HK_ESPACE (and no outputs) when the bytes do not cover the window pages or
+ * hold no more than `entries` pages; HK_EINVAL for a null argument or an overflowing cost. */
+int hk_pages_within(const hk_pool_sizing* pool, uint64_t bytes, size_t* pages, size_t* window_pages);
+
+typedef struct {
+    uint64_t free;           /* device bytes free; 0 = read cudaMemGetInfo on `device` */
+    uint64_t other;          /* the kernel's other device bytes (weights, workspace, staging) */
+    uint64_t slack;          /* bytes left unused */
+    uint32_t lanes;          /* the widest decode batch */
+    uint32_t context;        /* Model.context (for the error message) */
+    int32_t device;          /* CUDA device ordinal, read when free == 0 */
+    uint32_t reserved;
+} hk_pool_budget;
+
+/* The pool part of the loader's plan (src/gpu/load.rs:510-533): pools get free - other -
+ * slack bytes, sized by hk_pages_within; the lanes need lanes + 1 <= slots.  Outputs the
+ * pages, window pages, slots and the bytes the pools use (sum over states of bytes x units).
+ * Errors carry the reference's wording in hk_last_error(): HK_ESPACE for memory, HK_EINVAL
+ * for lanes past the slots. */
+int hk_plan_pools(const hk_pool_sizing* pool, const hk_pool_budget* budget, size_t* pages,
+                  size_t* window_pages, size_t* slots, uint64_t* used);
+
 /* Kernel::push: copies the share (the caller keeps ownership of its arrays).  share->at must
  * be the previous horizon + 1 (HK_ESTATE otherwise) and horizon >= at (HK_EINVAL). */
 int hk_push(hk_handle* handle, const hk_share* share);

@@ -679,3 +679,20 @@ def test_sample_verify_flat_rows_draw_exactly(hk, cuda):
                               torch.zeros(1, dtype=torch.int32, device=cuda), 1, 0)
     hk.check_errors()
     assert np.array_equal(ids.cpu().numpy(), want_ids)
+
+
+def test_plan_pools_reads_the_devices_free_memory(cuda):
+    """free = 0: hk_plan_pools sizes the pools from cudaMemGetInfo of the device."""
+    from hyperkernel_b200 import _lib
+    from oracle import pools as O
+
+    page = 61 * 64 * 576 * 2
+    states = [(0, O.PAGE, page), (1, O.WINDOW, 4096)]
+    before = torch.cuda.mem_get_info(0)[0]
+    pages, window_pages, slots, used = _lib.plan_pools(1 << 40, 128, 2049, 65, states, lanes=64,
+                                                       context=131072, other=1 << 30, device=0)
+    after = torch.cuda.mem_get_info(0)[0]
+    free = max(before, after)
+    assert (window_pages, slots) == (128, 65)
+    assert used == pages * page + 128 * 4096
+    assert used <= free - (1 << 30) < used + page + (64 << 20)  # within a page (+ allocator drift)
