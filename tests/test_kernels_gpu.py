@@ -307,7 +307,7 @@ def test_quant_fp8_bit_exact(hk, orc, cuda):
     assert np.array_equal(gs.cpu().numpy(), sx)
 
 
-@pytest.mark.parametrize("m,n,k", [(300, 512, 1024), (640, 1536, 1792), (7, 128, 256),
+@pytest.mark.parametrize("m,n,k", [(300, 512, 1024), (640, 1536, 1792), (7, 128, 256), (200, 768, 640),
                                    (333, 400, 384), (4096, 2560, 256), (1024, 576, 2048)])
 def test_gemm_fp8_matches_oracle(hk, orc, cuda, m, n, k):
     rng = W.Rng(41)
