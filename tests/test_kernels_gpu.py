@@ -299,8 +299,10 @@ def test_lse_merge_matches_oracle(hk, orc, cuda):
 # a11 FP8 linear
 # ------------------------------------------------------------------------------------------
 
-def test_quant_fp8_bit_exact(hk, orc, cuda):
-    x = W.f32_to_bf16_bits(W.Rng(40).normal(100 * 1024).astype(np.float32) * 3).reshape(100, 1024)
+@pytest.mark.parametrize("rows,k", [(100, 1024), (7, 384), (1, 128), (33, 640)])
+def test_quant_fp8_bit_exact(hk, orc, cuda, rows, k):
+    """Unit counts (rows x k/128) that do and do not fill whole half-warp groups."""
+    x = W.f32_to_bf16_bits(W.Rng(40).normal(rows * k).astype(np.float32) * 3).reshape(rows, k)
     xq, sx = orc.quant_fp8(x)
     gq, gs = hk.quant_fp8(bf16_dev(x, cuda))
     assert np.array_equal(gq.cpu().numpy(), xq)
