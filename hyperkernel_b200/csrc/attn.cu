@@ -455,7 +455,8 @@ int hk_gqa_decode_f32(const float* q, const float* k_cache, const float* v_cache
                       int32_t q_heads, int32_t kv_heads, int32_t head_dim, int32_t page_size,
                       int64_t num_slots, float scale, float* out, float* lse, void* stream) {
   HK_TRY(hk::ensure_device());
-  HK_REQUIRE(q && k_cache && v_cache && block_table && cu_seqlens && positions && out && lse,
+  HK_REQUIRE(num_tokens == 0 ||
+                 (q && k_cache && v_cache && block_table && cu_seqlens && positions && out && lse),
              "hk_gqa_decode_f32: null pointer");
   HK_REQUIRE(kv_heads > 0 && q_heads % kv_heads == 0 && q_heads / kv_heads <= 32,
              "hk_gqa_decode_f32: %d query heads over %d KV heads", q_heads, kv_heads);
@@ -488,7 +489,7 @@ int hk_gqa_decode_f32(const float* q, const float* k_cache, const float* v_cache
 int hk_lse_merge(const float* o_parts, const float* lse_parts, int32_t n_parts, int64_t rows,
                  int32_t dv, uint16_t* out, float* lse_out, void* stream) {
   HK_TRY(hk::ensure_device());
-  HK_REQUIRE(o_parts && lse_parts && out, "hk_lse_merge: null pointer");
+  HK_REQUIRE(rows == 0 || (o_parts && lse_parts && out), "hk_lse_merge: null pointer");
   HK_REQUIRE(n_parts >= 1 && n_parts <= 256 && rows >= 0 && dv > 0 && dv % 4 == 0,
              "hk_lse_merge: %d parts of dv %d (1..256 parts, dv a multiple of 4)", n_parts, dv);
   HK_REQUIRE(((uintptr_t)o_parts % 16 == 0) && ((uintptr_t)out % 8 == 0),
@@ -504,7 +505,8 @@ int hk_mla_decode_fp8(const uint16_t* q, const uint8_t* kv_cache, const float* k
                       float scale, uint16_t* out, float* lse, void* workspace,
                       size_t workspace_bytes, void* stream) {
   HK_TRY(hk::ensure_device());
-  HK_REQUIRE(q && kv_cache && kv_scale && block_table && cu_seqlens && positions && out && lse,
+  HK_REQUIRE(num_tokens == 0 ||
+                 (q && kv_cache && kv_scale && block_table && cu_seqlens && positions && out && lse),
              "hk_mla_decode_fp8: null pointer");
   HK_REQUIRE(heads > 0 && heads % kHeadBlock == 0, "hk_mla_decode_fp8: heads %d not a multiple of 16", heads);
   HK_REQUIRE(num_lanes > 0 && num_tokens >= 0 && page_size > 0 && bt_stride > 0 && max_kv_len >= 0,
@@ -524,8 +526,8 @@ int hk_mla_partial_fp8(const uint16_t* q, const uint8_t* kv_cache, const float* 
                        int64_t num_slots, int32_t max_kv_len, float scale, float* o_part,
                        float* lse_part, void* workspace, size_t workspace_bytes, void* stream) {
   HK_TRY(hk::ensure_device());
-  HK_REQUIRE(q && kv_cache && kv_scale && block_table && cu_seqlens && positions && kv_begin &&
-                 kv_end && o_part && lse_part,
+  HK_REQUIRE(num_tokens == 0 || (q && kv_cache && kv_scale && block_table && cu_seqlens && positions &&
+                                  kv_begin && kv_end && o_part && lse_part),
              "hk_mla_partial_fp8: null pointer");
   HK_REQUIRE(heads > 0 && heads % kHeadBlock == 0, "hk_mla_partial_fp8: heads %d not a multiple of 16", heads);
   HK_REQUIRE(num_lanes > 0 && num_tokens >= 0 && page_size > 0 && bt_stride > 0,

@@ -139,7 +139,7 @@ extern "C" {
 int hk_quant_fp8(const uint16_t* x, int64_t rows, int32_t k, uint8_t* xq, float* sx,
                  void* stream) {
   HK_TRY(hk::ensure_device());
-  HK_REQUIRE(x && xq && sx, "hk_quant_fp8: null pointer");
+  HK_REQUIRE(rows == 0 || (x && xq && sx), "hk_quant_fp8: null pointer");
   HK_REQUIRE(rows >= 0 && k > 0 && k % 128 == 0, "hk_quant_fp8: k %d must be a multiple of 128", k);
   HK_REQUIRE(((uintptr_t)x % 16 == 0) && ((uintptr_t)xq % 8 == 0), "hk_quant_fp8: misaligned buffers");
   return hk::quant_fp8_launch(x, rows, k, xq, sx, (cudaStream_t)stream);
@@ -148,7 +148,7 @@ int hk_quant_fp8(const uint16_t* x, int64_t rows, int32_t k, uint8_t* xq, float*
 int hk_gemm_fp8(const uint8_t* xq, const float* sx, const uint8_t* wq, const float* sw,
                 int64_t m, int32_t n, int32_t k, uint16_t* y, void* stream) {
   HK_TRY(hk::ensure_device());
-  HK_REQUIRE(xq && sx && wq && sw && y, "hk_gemm_fp8: null pointer");
+  HK_REQUIRE(m == 0 || (xq && sx && wq && sw && y), "hk_gemm_fp8: null pointer");
   HK_REQUIRE(m >= 0 && n > 0 && n % 16 == 0 && k > 0 && k % 128 == 0,
              "hk_gemm_fp8: m %lld n %d k %d (n a multiple of 16, k of 128)", (long long)m, n, k);
   HK_REQUIRE(((uintptr_t)xq | (uintptr_t)wq) % 16 == 0, "hk_gemm_fp8: operands must be 16-byte aligned");

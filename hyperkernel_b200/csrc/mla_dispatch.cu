@@ -19,7 +19,7 @@ int hk_mla_decode(const uint16_t* q, const uint16_t* kv_cache, const int32_t* bl
                   int64_t num_slots, int32_t max_kv_len, float scale, uint16_t* out, float* lse,
                   void* workspace, size_t workspace_bytes, int32_t impl, void* stream) {
   HK_TRY(hk::ensure_device());
-  HK_REQUIRE(q && kv_cache && block_table && cu_seqlens && positions && out && lse,
+  HK_REQUIRE(num_tokens == 0 || (q && kv_cache && block_table && cu_seqlens && positions && out && lse),
              "hk_mla_decode: null pointer");
   HK_REQUIRE(heads > 0 && heads % 16 == 0, "hk_mla_decode: heads %d not a multiple of 16", heads);
   HK_REQUIRE(num_lanes > 0 && num_tokens >= 0 && page_size > 0 && bt_stride > 0 && max_kv_len >= 0,
@@ -49,8 +49,8 @@ int hk_mla_partial(const uint16_t* q, const uint16_t* kv_cache, const int32_t* b
                    int32_t max_kv_len, float scale, float* o_part, float* lse_part,
                    void* workspace, size_t workspace_bytes, void* stream) {
   HK_TRY(hk::ensure_device());
-  HK_REQUIRE(q && kv_cache && block_table && cu_seqlens && positions && kv_begin && kv_end &&
-                 o_part && lse_part,
+  HK_REQUIRE(num_tokens == 0 || (q && kv_cache && block_table && cu_seqlens && positions && kv_begin &&
+                                  kv_end && o_part && lse_part),
              "hk_mla_partial: null pointer");
   HK_REQUIRE(num_lanes > 0 && num_tokens >= 0 && page_size > 0 && bt_stride > 0 && max_kv_len >= 0,
              "hk_mla_partial: bad sizes");

@@ -451,7 +451,7 @@ int moe_grouped_run(const uint8_t* xq, const float* sx, int32_t tokens, const in
                     const float* s2, uint16_t* y, void* workspace, size_t workspace_bytes,
                     bool portable_only, unsigned long long* err, cudaStream_t s) {
   HK_TRY(hk::ensure_device());
-  HK_REQUIRE(xq && sx && offsets && perm_token && w13 && s13 && w2 && s2 && y,
+  HK_REQUIRE(rows == 0 || (xq && sx && offsets && perm_token && w13 && s13 && w2 && s2 && y),
              "hk_moe_grouped: null pointer");
   HK_REQUIRE(num_experts > 0 && num_experts <= kMaxExperts, "hk_moe_grouped: %d experts", num_experts);
   HK_REQUIRE(hidden > 0 && hidden % 128 == 0 && inter > 0 && inter % 128 == 0,
@@ -500,7 +500,7 @@ extern "C" {
 int hk_route(const float* logits, const float* bias, int32_t tokens, int32_t num_experts,
              int32_t top_k, float route_scale, int32_t* ids, float* weights, void* stream) {
   HK_TRY(hk::ensure_device());
-  HK_REQUIRE(logits && ids && weights, "hk_route: null pointer");
+  HK_REQUIRE(tokens == 0 || (logits && ids && weights), "hk_route: null pointer");
   HK_REQUIRE(num_experts > 0 && num_experts <= 256 && top_k > 0 && top_k <= 16 && top_k <= num_experts,
              "hk_route: %d experts, top %d (at most 256 experts, top 16)", num_experts, top_k);
   HK_REQUIRE(tokens >= 0, "hk_route: negative token count");
@@ -516,7 +516,8 @@ int hk_permute(const int32_t* ids, const float* weights, int32_t tokens, int32_t
                int32_t num_experts, int32_t* offsets, int32_t* perm_token, float* perm_weight,
                int32_t* inv, void* stream) {
   HK_TRY(hk::ensure_device());
-  HK_REQUIRE(ids && weights && offsets && perm_token && perm_weight && inv, "hk_permute: null pointer");
+  HK_REQUIRE(offsets && (tokens == 0 || (ids && weights && perm_token && perm_weight && inv)),
+             "hk_permute: null pointer");
   HK_REQUIRE(num_experts > 0 && num_experts <= kMaxExperts && top_k > 0 && tokens >= 0,
              "hk_permute: %d experts (at most %d), top %d", num_experts, kMaxExperts, top_k);
   const size_t smem = sizeof(int) * (size_t)num_experts * 34;
@@ -546,7 +547,7 @@ int hk_combine(const uint16_t* y, int64_t rows, const float* perm_weight, const 
                const uint16_t* shared, int32_t tokens, int32_t top_k, int32_t hidden,
                uint16_t* out, void* stream) {
   HK_TRY(hk::ensure_device());
-  HK_REQUIRE(y && perm_weight && inv && out, "hk_combine: null pointer");
+  HK_REQUIRE(tokens == 0 || (y && perm_weight && inv && out), "hk_combine: null pointer");
   HK_REQUIRE(top_k > 0 && top_k <= 16 && hidden > 0 && hidden % 8 == 0 && tokens >= 0,
              "hk_combine: top %d, hidden %d", top_k, hidden);
   HK_REQUIRE(((uintptr_t)y | (uintptr_t)out | (uintptr_t)shared) % 16 == 0,

@@ -273,7 +273,7 @@ int hk_kv_append_bf16(const uint16_t* kv_new, const int32_t* slot_mapping, int32
                       int32_t row_elems, int32_t page_rows, uint16_t* kv_cache, int64_t num_slots,
                       void* stream) {
   HK_TRY(hk::ensure_device());
-  HK_REQUIRE(kv_new && slot_mapping && kv_cache, "hk_kv_append_bf16: null pointer");
+  HK_REQUIRE(num_tokens == 0 || (kv_new && slot_mapping && kv_cache), "hk_kv_append_bf16: null pointer");
   HK_REQUIRE(num_tokens >= 0 && row_elems > 0 && row_elems % 8 == 0 && num_slots > 0,
              "hk_kv_append_bf16: row_elems %d must be a positive multiple of 8", row_elems);
   HK_REQUIRE(page_rows >= 0 && (page_rows == 0 || (row_elems % 64 == 0 && num_slots % page_rows == 0)),
@@ -301,7 +301,8 @@ int hk_kv_dequant_fp8(const uint8_t* kv_fp8, const float* kv_scale, int64_t num_
                       int32_t page_rows, const int32_t* pages, int64_t n_pages, uint16_t* kv_bf16,
                       void* stream) {
   HK_TRY(hk::ensure_device());
-  HK_REQUIRE(kv_fp8 && kv_scale && kv_bf16, "hk_kv_dequant_fp8: null pointer");
+  HK_REQUIRE((pages ? n_pages == 0 : num_slots == 0) || (kv_fp8 && kv_scale && kv_bf16),
+             "hk_kv_dequant_fp8: null pointer");
   HK_REQUIRE(num_slots >= 0 && page_rows > 0 && num_slots % page_rows == 0 && row_elems > 0 && row_elems % 64 == 0,
              "hk_kv_dequant_fp8: num_slots %lld (a multiple of page_rows %d), row_elems %d (a multiple of 64)",
              (long long)num_slots, page_rows, row_elems);
@@ -321,7 +322,7 @@ int hk_kv_dequant_fp8_rows(const uint8_t* kv_fp8, const float* kv_scale, int64_t
                            int32_t page_rows, const int32_t* slots, int64_t n_rows, uint16_t* kv_bf16,
                            void* stream) {
   HK_TRY(hk::ensure_device());
-  HK_REQUIRE(kv_fp8 && kv_scale && kv_bf16 && slots, "hk_kv_dequant_fp8_rows: null pointer");
+  HK_REQUIRE(n_rows == 0 || (kv_fp8 && kv_scale && kv_bf16 && slots), "hk_kv_dequant_fp8_rows: null pointer");
   HK_REQUIRE(num_slots >= 0 && page_rows > 0 && num_slots % page_rows == 0 && row_elems > 0 && row_elems % 64 == 0,
              "hk_kv_dequant_fp8_rows: num_slots %lld (a multiple of page_rows %d), row_elems %d (a multiple of 64)",
              (long long)num_slots, page_rows, row_elems);
@@ -341,7 +342,7 @@ int hk_kv_append_fp8(const uint16_t* kv_new, const int32_t* slot_mapping, int32_
                      int32_t row_elems, uint8_t* kv_cache, float* kv_scale, int64_t num_slots,
                      void* stream) {
   HK_TRY(hk::ensure_device());
-  HK_REQUIRE(kv_new && slot_mapping && kv_cache && kv_scale, "hk_kv_append_fp8: null pointer");
+  HK_REQUIRE(num_tokens == 0 || (kv_new && slot_mapping && kv_cache && kv_scale), "hk_kv_append_fp8: null pointer");
   HK_REQUIRE(num_tokens >= 0 && row_elems > 0 && row_elems % 8 == 0 && num_slots > 0,
              "hk_kv_append_fp8: row_elems %d must be a positive multiple of 8", row_elems);
   HK_REQUIRE(((uintptr_t)kv_new % 16 == 0) && ((uintptr_t)kv_cache % 8 == 0),
@@ -359,7 +360,8 @@ int hk_kv_append_f32(const float* k_new, const float* v_new, const int32_t* slot
                      int32_t num_tokens, int32_t row_elems, float* k_cache, float* v_cache,
                      int64_t num_slots, void* stream) {
   HK_TRY(hk::ensure_device());
-  HK_REQUIRE(k_new && v_new && slot_mapping && k_cache && v_cache, "hk_kv_append_f32: null pointer");
+  HK_REQUIRE(num_tokens == 0 || (k_new && v_new && slot_mapping && k_cache && v_cache),
+             "hk_kv_append_f32: null pointer");
   HK_REQUIRE(num_tokens >= 0 && row_elems > 0 && row_elems % 4 == 0 && num_slots > 0,
              "hk_kv_append_f32: row_elems %d must be a positive multiple of 4", row_elems);
   HK_REQUIRE(((uintptr_t)k_new | (uintptr_t)v_new | (uintptr_t)k_cache | (uintptr_t)v_cache) % 16 == 0,

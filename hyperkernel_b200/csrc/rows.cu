@@ -38,7 +38,7 @@ __global__ void scatter_rows_bytes_kernel(const V* __restrict__ src, int64_t row
 }
 
 int check_rows(const void* src, const int32_t* idx, const void* dst, int64_t rows, int32_t row_bytes) {
-  HK_REQUIRE(src && idx && dst, "null pointer");
+  HK_REQUIRE(rows == 0 || (src && idx && dst), "null pointer");
   HK_REQUIRE(rows >= 0 && rows < (1ll << 31), "rows %lld", (long long)rows);
   HK_REQUIRE(row_bytes > 0 && row_bytes % 4 == 0, "row_bytes %d must be a positive multiple of 4", row_bytes);
   HK_REQUIRE(((uintptr_t)src | (uintptr_t)dst) % 4 == 0, "rows must be 4-byte aligned");

@@ -741,11 +741,13 @@ int hk_sample_verify(const float* logits, int32_t vocab, const int32_t* cu_rows,
                      const int32_t* drafts, int32_t n_logprobs, int32_t* ids, float* lp,
                      void* workspace, size_t workspace_bytes, void* stream) {
   HK_TRY(hk::ensure_device());
-  HK_REQUIRE(logits && cu_rows && sampling && state && ids && workspace, "hk_sample_verify: null pointer");
+  HK_REQUIRE((num_rows == 0 || (logits && workspace)) && cu_rows && sampling && state && ids,
+             "hk_sample_verify: null pointer");
   HK_REQUIRE(vocab > 0 && vocab <= kMaxVocab, "hk_sample_verify: vocab %d not in 1..%d", vocab, kMaxVocab);
   HK_REQUIRE(num_lanes > 0 && num_rows >= 0 && block >= 1 && n_logprobs >= 0 && n_logprobs <= kMaxLogprobs,
              "hk_sample_verify: bad sizes");
-  HK_REQUIRE(block == 1 || drafts != nullptr, "hk_sample_verify: drafts needed for block %d", block);
+  HK_REQUIRE(block == 1 || num_rows == 0 || drafts != nullptr, "hk_sample_verify: drafts needed for block %d",
+             block);
   HK_REQUIRE(n_logprobs == 0 || lp != nullptr, "hk_sample_verify: lp needed for %d logprobs", n_logprobs);
   HK_REQUIRE((uintptr_t)workspace % 256 == 0, "hk_sample_verify: workspace must be 256-byte aligned");
   const size_t need = hk_sample_workspace_size(num_rows, vocab);

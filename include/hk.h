@@ -12,6 +12,11 @@
  * hk_check_errors() on that device reports it.  No entry point ever falls back to a CPU
  * path: without a usable sm_100 device they return HK_ENODEV.
  *
+ * Empty problems: a kernel entry point with nothing to process (no tokens, rows or pages)
+ * returns 0 without launching anything, and the arrays it would have read or written may
+ * then be NULL (as a zero-element tensor's address is).  Arrays that still receive output
+ * (hk_permute's offsets, hk_sample_verify's per-lane ids and states) stay required.
+ *
  * Reference interfaces replaced (paths inside mr-d-self-driving/Hyperkernel):
  *   - the `Kernel` trait, src/gpu/mod.rs:42-46 (pools / push / drain) and its data types
  *     Share / Command / Event / Sampled, src/gpu/mod.rs:13-40  ->  hk_open ... hk_drain;

@@ -698,3 +698,44 @@ def test_plan_pools_reads_the_devices_free_memory(cuda):
     assert (window_pages, slots) == (128, 65)
     assert used == pages * page + 128 * 4096
     assert used <= free - (1 << 30) < used + page + (64 << 20)  # within a page (+ allocator drift)
+
+
+def test_empty_problems_are_no_ops(hk, cuda):
+    """Zero tokens / rows / pages: every entry returns without a launch, its arrays may be NULL
+    (a zero-element tensor's address), and permute / sample-verify still write their per-expert
+    and per-lane outputs."""
+    from hyperkernel_b200 import _lib as L
+
+    dev = torch.device("cuda", 0)
+    z = lambda *shape, dt=torch.int32: torch.empty(shape, dtype=dt, device=dev)
+    before = hk.kernel_launches()
+    L.call("hk_quant_fp8", None, 0, 256, None, None, None)
+    L.call("hk_gemm_fp8", None, None, None, None, 0, 256, 256, None, None)
+    L.call("hk_route", None, None, 0, 256, 8, 1.0, None, None, None)
+    L.call("hk_combine", None, 0, None, None, None, 0, 8, 7168, None, None)
+    L.call("hk_kv_append_bf16", None, None, 0, 576, 64, None, 64, None)
+    L.call("hk_kv_append_fp8", None, None, 0, 576, None, None, 64, None)
+    L.call("hk_kv_dequant_fp8_rows", None, None, 64, 576, 64, None, 0, None, None)
+    L.call("hk_gather_rows", None, 0, None, 0, 64, None, None)
+    L.call("hk_lse_merge", None, None, 2, 0, 512, None, None, None)
+    L.call("hk_mla_decode", None, None, None, 1, None, None, 1, 0, 128, 64, 64, 0, 1.0, None, None,
+           None, 0, 0, None)
+    assert hk.kernel_launches() == before
+    hk.check_errors()
+
+    # permute of no tokens: every expert's offset is 0
+    offsets = z(9)
+    L.call("hk_permute", None, None, 0, 8, 8, L.ptr(offsets), None, None, None, None)
+    torch.cuda.synchronize()
+    assert offsets.cpu().tolist() == [0] * 9
+
+    # sample-verify of lanes with no rows: every id is -2 (no token) and the states stay put
+    samp = L.sampling_array([dict(temperature=1.0, top_p=1.0, top_k=0, logprobs=0, seed=5)] * 3, dev)
+    state = torch.tensor([5, 6, 7], dtype=torch.int64, device=dev)
+    ids, _ = L.sample_verify(torch.empty((0, 1000), dtype=torch.float32, device=dev),
+                             torch.zeros(4, dtype=torch.int32, device=dev), samp, state,
+                             torch.empty((3, 2), dtype=torch.int32, device=dev), 3, 0)
+    torch.cuda.synchronize()
+    assert (ids.cpu() == -2).all()
+    assert state.cpu().tolist() == [5, 6, 7]
+    hk.check_errors()
