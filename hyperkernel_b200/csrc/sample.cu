@@ -663,6 +663,10 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(
 }
 
 // One warp per lane: lane 0 walks the chain, then the warp writes the ids and logprob rows.
+// One warp per lane, one row per thread (block <= 32): every row's statistics and draft are
+// loaded at once, the accepted prefix is a ballot (the chain stops at the first non-finite
+// row, or at the first row whose token differs from the next row's draft), and the logprob
+// rows are written by the whole warp, (row, pair) by (row, pair).
 __global__ void sample_chain_kernel(const float* __restrict__ logits, int32_t vocab,
                                     const int32_t* __restrict__ cu, int32_t lanes, int32_t block,
                                     const hk_sampling* __restrict__ sampling, uint64_t* state,
@@ -671,59 +675,59 @@ __global__ void sample_chain_kernel(const float* __restrict__ logits, int32_t vo
                                     unsigned long long* err) {
   const int b = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
   const int t32 = threadIdx.x & 31;
-  if (b >= lanes) return;
+  if (b >= lanes) return;  // whole warps
   const int width = 2 * n_logprobs + 1;
   const int r0 = cu[b], rows = cu[b + 1] - r0;
-  const bool bad_rows = rows < 0 || rows > block;
-  // accepted rows, and whether the last of them is a non-finite row (-1)
-  int m = 0, last_bad = 0;
-  if (t32 == 0 && !bad_rows) {
-    const bool sampled = !greedy(sampling[b]);
-    uint64_t draws = 0;
-    for (int j = 0; j < rows; ++j) {
-      const RowStat rs = s.stats[r0 + j];
-      ++m;
-      if (rs.flags & 1) {
-        last_bad = 1;
-        break;
-      }
-      draws += sampled ? 1 : 0;
-      if (j + 1 < rows && rs.token != drafts[(int64_t)b * (block - 1) + j]) break;
-    }
-    state[b] += draws * kGamma;
-  }
-  if (bad_rows) {
+  if (rows < 0 || rows > block) {
     if (t32 == 0) hk_flag(err, hk::kErrMoeRow, (unsigned)b);
     for (int j = t32; j < block; j += 32) ids[(int64_t)b * block + j] = -2;
     return;
   }
-  m = __shfl_sync(0xffffffffu, m, 0);
-  last_bad = __shfl_sync(0xffffffffu, last_bad, 0);
-  for (int j = t32; j < block; j += 32) {
+  RowStat rs{};
+  int draft = 0;
+  const bool in = t32 < rows;
+  if (in) {
+    rs = s.stats[r0 + t32];
+    if (t32 + 1 < rows) draft = drafts[(int64_t)b * (block - 1) + t32];
+  }
+  const bool bad = in && (rs.flags & 1);
+  const bool stop = bad || (in && t32 + 1 < rows && rs.token != draft);
+  const unsigned stops = __ballot_sync(0xffffffffu, stop);
+  const unsigned bads = __ballot_sync(0xffffffffu, bad);
+  const int m = rows == 0 ? 0 : (stops ? __ffs(stops) : rows);   // accepted rows
+  const int last_bad = m > 0 ? (int)((bads >> (m - 1)) & 1u) : 0;
+  if (t32 == 0) state[b] += (greedy(sampling[b]) ? 0ull : (uint64_t)(m - last_bad)) * kGamma;
+  if (t32 < block) {
     int32_t v = -2;
-    if (j < m) v = (j == m - 1 && last_bad) ? -1 : s.stats[r0 + j].token;
-    ids[(int64_t)b * block + j] = v;
+    if (t32 < m) v = (t32 == m - 1 && last_bad) ? -1 : rs.token;
+    ids[(int64_t)b * block + t32] = v;
   }
   if (n_logprobs == 0) return;
-  for (int j = 0; j < block; ++j) {
+  const int live_rows = m - last_bad;  // rows 0 .. live_rows-1 carry logprobs
+  const int pairs = block * n_logprobs;
+  for (int base = 0; base < pairs; base += 32) {  // warp-uniform trip count: the shuffles see all lanes
+    const int idx = base + t32;
+    const int j = idx < pairs ? idx / n_logprobs : 0, q = idx < pairs ? idx % n_logprobs : 0;
+    const double lse_j = __shfl_sync(0xffffffffu, rs.lse, j);
+    const int ntop_j = __shfl_sync(0xffffffffu, rs.ntop, j);
+    if (idx >= pairs) continue;
     float* row = lp + ((int64_t)b * block + j) * width;
-    const bool live = j < m && !(j == m - 1 && last_bad);
-    if (!live) {
-      for (int q = t32; q < width; q += 32) row[q] = 0.f;
-      continue;
-    }
     const int r = r0 + j;
-    const RowStat rs = s.stats[r];
-    for (int q = t32; q < n_logprobs; q += 32) {
-      if (q < rs.ntop) {
-        row[2 * q] = (float)s.top[(int64_t)r * kMaxLogprobs + q];
-        row[2 * q + 1] = (float)((double)s.topv[(int64_t)r * kMaxLogprobs + q] - rs.lse);
-      } else {
-        row[2 * q] = -1.f;
-        row[2 * q + 1] = 0.f;
-      }
+    if (j >= live_rows) {
+      row[2 * q] = 0.f;
+      row[2 * q + 1] = 0.f;
+    } else if (q < ntop_j) {
+      row[2 * q] = (float)s.top[(int64_t)r * kMaxLogprobs + q];
+      row[2 * q + 1] = (float)((double)s.topv[(int64_t)r * kMaxLogprobs + q] - lse_j);
+    } else {
+      row[2 * q] = -1.f;
+      row[2 * q + 1] = 0.f;
     }
-    if (t32 == 0) row[2 * n_logprobs] = (float)((double)logits[(int64_t)r * vocab + rs.token] - rs.lse);
+  }
+  if (t32 < block) {
+    float* row = lp + ((int64_t)b * block + t32) * width;
+    row[2 * n_logprobs] =
+        t32 < live_rows ? (float)((double)logits[(int64_t)(r0 + t32) * vocab + rs.token] - rs.lse) : 0.f;
   }
 }
 
@@ -744,8 +748,9 @@ int hk_sample_verify(const float* logits, int32_t vocab, const int32_t* cu_rows,
   HK_REQUIRE((num_rows == 0 || (logits && workspace)) && cu_rows && sampling && state && ids,
              "hk_sample_verify: null pointer");
   HK_REQUIRE(vocab > 0 && vocab <= kMaxVocab, "hk_sample_verify: vocab %d not in 1..%d", vocab, kMaxVocab);
-  HK_REQUIRE(num_lanes > 0 && num_rows >= 0 && block >= 1 && n_logprobs >= 0 && n_logprobs <= kMaxLogprobs,
-             "hk_sample_verify: bad sizes");
+  HK_REQUIRE(num_lanes > 0 && num_rows >= 0 && block >= 1 && block <= 32 && n_logprobs >= 0 &&
+                 n_logprobs <= kMaxLogprobs,
+             "hk_sample_verify: bad sizes (block 1..32, at most %d logprobs)", kMaxLogprobs);
   HK_REQUIRE(block == 1 || num_rows == 0 || drafts != nullptr, "hk_sample_verify: drafts needed for block %d",
              block);
   HK_REQUIRE(n_logprobs == 0 || lp != nullptr, "hk_sample_verify: lp needed for %d logprobs", n_logprobs);
