@@ -603,7 +603,7 @@ int gemm_fp8_sm100(const uint8_t* xq, const float* sx, const uint8_t* wq, const 
                    int32_t n, int32_t k, uint16_t* y, cudaStream_t stream) {
   HK_REQUIRE(gemm_fp8_sm100_supported(m, n, k), "gemm_fp8_sm100: shape m %lld n %d k %d", (long long)m, n, k);
   HK_REQUIRE((uintptr_t)y % 16 == 0, "gemm_fp8_sm100: y must be 16-byte aligned");
-  if (m >= kPM) return gemm_fp8_pair(xq, sx, wq, sw, m, n, k, y, stream);
+  if (m >= kPM && sm_count() >= 2) return gemm_fp8_pair(xq, sx, wq, sw, m, n, k, y, stream);
   CUtensorMap xmap, wmap;
   HK_TRY(sm100::make_map_u8(&xmap, xq, (uint64_t)m, (uint64_t)k, kBM));
   HK_TRY(sm100::make_map_u8(&wmap, wq, (uint64_t)n, (uint64_t)k, kBN));
