@@ -187,7 +187,8 @@ def main(argv=None):
     ap.add_argument("--ctx-min", type=int, default=1024, help="profiling override of config 2")
     ap.add_argument("--ctx-max", type=int, default=131072, help="profiling override of config 2")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host round trip leg")
-    ap.add_argument("--workload", default="decode", choices=["decode", "moe", "linear", "longctx", "sample", "mixed"])
+    ap.add_argument("--workload", default="decode",
+                    choices=["decode", "moe", "linear", "longctx", "sample", "mixed", "engine"])
     ap.add_argument("--experts", type=int, default=None, help="profiling override of config 4's 256 experts")
     ap.add_argument("--full-dequant", action="store_true",
                     help="longctx: convert the whole FP8 pool to bf16 every step (no mirror)")
@@ -423,6 +424,9 @@ def run_layer(args):
     elif args.workload == "sample":
         line = _run_sample(args, torch, dist, hk, ClockSampler, world, rank, local, device, stream, gen,
                            hbm_peak, peak_src, barrier)
+    elif args.workload == "engine":
+        line = _run_engine(args, torch, dist, hk, ClockSampler, world, rank, local, device, barrier, hbm_peak,
+                           peak_src)
     else:
         line = _run_linear(args, torch, dist, hk, ClockSampler, world, rank, local, device, stream, gen,
                            fp8_peak, peak_src, barrier)
@@ -906,6 +910,135 @@ def _run_sample(args, torch, dist, hk, ClockSampler, world, rank, local, device,
                 "h2d_bytes_per_step": rows * V * 4, "d2h_bytes_per_step": L * B * (4 + (2 * n + 1) * 4)},
         "gpu_launches": int(launches), "clocks": clocks,
     }
+
+
+ENGINE_LANES, ENGINE_PAGE_ROWS, ENGINE_ENTRIES, ENGINE_CHUNK, ENGINE_BLOCK = 64, 64, 64, 512, 5
+ENGINE_REQUESTS, ENGINE_LIMIT, ENGINE_PROMPT = 256, 128, (64, 1024)
+
+
+def _engine_requests(n, seed):
+    """Seeded prompts of U[64, 1024] tokens from the test model's vocabulary (10..409)."""
+    rng = np.random.default_rng(seed)
+    return [(rng.integers(10, 410, int(rng.integers(*ENGINE_PROMPT))).tolist(), ENGINE_LIMIT) for _ in range(n)]
+
+
+def _engine_session(H, transport, device_index, requests):
+    """One session of the engine over the device kernel: every request submitted, the jobs
+    closed, hk_engine_run to the end.  Returns (seconds, iterations with tokens, tokens
+    generated, kernel launches)."""
+    from hyperkernel_b200 import _lib as hk
+
+    context = ENGINE_PAGE_ROWS * ENGINE_ENTRIES
+    pages = ENGINE_LANES * ENGINE_ENTRIES + 1
+    cfg = H.Config(model=H.MODEL_FNV, page_rows=ENGINE_PAGE_ROWS, entries=ENGINE_ENTRIES, window=ENGINE_ENTRIES,
+                   width=ENGINE_LANES, context=context, chunk=ENGINE_CHUNK, block=ENGINE_BLOCK, pages=pages,
+                   window_pages=pages, clip=0, device=device_index, transport=transport)
+    dev = H.Device(cfg)
+    try:
+        eng = H.Engine(H.engine_config(page_rows=ENGINE_PAGE_ROWS, entries=ENGINE_ENTRIES, window=ENGINE_ENTRIES,
+                                       window_keep=0, context=context, width=ENGINE_LANES, chunk=ENGINE_CHUNK,
+                                       block=ENGINE_BLOCK, pad=7, budget=None, every=1, headroom=2048),
+                       dev.ops(), keep=dev)
+        reqs = [eng.submit(pr, lim) for pr, lim in requests]
+        eng.close()
+        l0 = hk.kernel_launches()
+        t0 = time.perf_counter()
+        rc = eng.run()
+        dt = time.perf_counter() - t0
+        launches = hk.kernel_launches() - l0
+        if rc != 0:
+            raise RuntimeError(f"engine run failed: {eng.failure}")
+        _m, _acc, counts, _total = eng.metrics()
+        tokens = sum(len(eng.heard(r).tokens) for r in reqs)
+    finally:
+        dev.close()
+    return dt, int(sum(counts)), tokens, launches
+
+
+def _run_engine(args, torch, dist, hk, ClockSampler, world, rank, local, device, barrier, hbm_peak, peak_src):
+    """Rows a1-a6 and a16 through the boundary: the C++ engine (admission with the prefix tree,
+    block-table deltas, prompt chunking, pacing, spec-verify accounting) driving the device
+    kernel behind hk_kernel_ops, over the resident-ring transport, with the reference's test
+    model on the GPU (its next token is a fold over the sequence read back through the paged
+    pools).  256 requests, prompts U[64, 1024], 128 tokens each, 64 lanes, 1 + 4 draft rows.
+    The loop is host-driven, so it is timed by the host clock around hk_engine_run, and the
+    number is end to end by construction (commands in, ids out through mapped host memory).
+    N > 1: independent replicas."""
+    from hyperkernel_b200 import engine as H
+
+    requests = _engine_requests(ENGINE_REQUESTS, 11 + rank)
+    for _ in range(max(1, min(args.warmup, 2))):
+        _engine_session(H, 1, local, _engine_requests(16, 5))
+    sampler = ClockSampler(local).start()
+    barrier()
+    t0 = time.perf_counter()
+    dt, iters, tokens, launches = _engine_session(H, 1, local, requests)
+    t1 = time.perf_counter()
+    barrier()
+    sampler.stop()
+    clocks = sampler.summary(t0, t1)
+    dt_launch, iters_launch, tokens_launch, _ = _engine_session(H, 0, local, requests)
+    (dt,) = _reduce_max(torch, dist, world, device, dt * 1e3)
+    dt /= 1e3
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = _engine_cpu_baseline()
+    tps = tokens * world / dt
+    # bytes the step kernel reads per iteration: every live lane's sequence, back through its row
+    seq_bytes = sum(len(pr) + lim for pr, lim in requests) * 4 / max(len(requests), 1) * ENGINE_LANES
+    gbs = seq_bytes / (dt / max(iters, 1)) / 1e9
+    return {
+        "metric": "engine tokens/s through the Kernel boundary (test model, 64 lanes)",
+        "value": tps, "unit": "tokens/s", "n_gpus": world, "steps": iters, "warmup": max(1, min(args.warmup, 2)),
+        "ms_per_step": dt * 1e3 / max(iters, 1), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int32 (token ids)", "data": "synthetic (seeded prompts)",
+        "config": {"workload": f"{ENGINE_REQUESTS} requests, prompts U{list(ENGINE_PROMPT)}, {ENGINE_LIMIT} tokens "
+                               f"each, {ENGINE_LANES} lanes, pages of {ENGINE_PAGE_ROWS} rows, block {ENGINE_BLOCK}, "
+                               "resident-ring transport",
+                   "parallelism": f"replicas{world}" if world > 1 else "single",
+                   "timing": "host clock around hk_engine_run (host-driven loop); a step = an engine iteration "
+                             "that produced tokens",
+                   "launch_transport": {"tokens_per_s": tokens_launch * world / dt_launch,
+                                        "ms_per_step": dt_launch * 1e3 / max(iters_launch, 1)}},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
+                     "traffic": None, "kernel": "executor_kernel (apply + step of the test model)",
+                     "note": "latency-bound: a step moves a few hundred KB; the per-step time is the measure",
+                     "peak_source": peak_src},
+        "cpu_baseline": cpu,
+        "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": None, "d2h_bytes_per_step": None,
+                "note": "the engine loop is end to end: commands cross to the device and ids back every step"},
+        "gpu_launches": int(launches), "clocks": clocks,
+    }
+
+
+def _engine_cpu_baseline(n=ENGINE_REQUESTS):
+    """The oracle engine over the oracle's restatement of the reference's test device, on the
+    same requests (one thread)."""
+    from oracle import engine as E
+
+    requests = _engine_requests(n, 11)
+    context = ENGINE_PAGE_ROWS * ENGINE_ENTRIES
+    pages = ENGINE_LANES * ENGINE_ENTRIES + 1
+    jobs = E.Channel()
+    sinks = []
+    for pr, lim in requests:
+        sink = E.Sink()
+        jobs.send(E.JobRun(E.Request(list(pr), E.Sampling(), lim, [], sink)))
+        sinks.append(sink)
+    jobs.close()
+    fake = E.Fake(pages, pages, ENGINE_PAGE_ROWS, ENGINE_ENTRIES, ENGINE_LANES, context, ENGINE_CHUNK,
+                  drafts=ENGINE_BLOCK - 1)
+    t0 = time.perf_counter()
+    err = E.run(E.Model(context=context, width=ENGINE_LANES, chunk=ENGINE_CHUNK, block=ENGINE_BLOCK, pad=7),
+                E.Pool(page_rows=ENGINE_PAGE_ROWS, entries=ENGINE_ENTRIES, window=ENGINE_ENTRIES),
+                fake, jobs, E.Metrics(), E.Plan(budget=None, every=1, headroom=2048), E.EngineConfig())
+    dt = time.perf_counter() - t0
+    if err is not None:
+        raise RuntimeError(f"oracle engine failed: {err}")
+    tokens = sum(sum(1 for o in s.items if isinstance(o, E.OutToken)) for s in sinks)
+    return {"value": tokens / dt, "unit": "tokens/s", "cores": 1, "kind": "port",
+            "sample": f"the same {n} requests through the Python restatement of the engine and of the "
+                      "reference's test device"}
 
 
 def _sample_cpu_baseline(logits, cu, samplings, seeds, drafts, sample_lanes=4):

@@ -123,36 +123,114 @@ __device__ bool write_token(const Dev& d, int lane, long long p, int32_t t) {
   return true;
 }
 
-// Fake::token (tests/engine.rs:115-128) with `next` (:56-62): reads positions 0..=last back
-// through the row, checks the window over the last page_rows positions, folds.
-__device__ bool model_token(const Dev& d, int lane, long long last, int32_t* out) {
+// The failure a read of position p through the lane's row would record (page_of, then the
+// pool read), without recording it; the token in *v when it returns 0.
+__device__ __forceinline__ unsigned token_at(const Dev& d, int64_t rowbase, long long p, int32_t* v) {
+  const long long k = p / d.page_rows;
+  if (k >= d.entries) return kFaultPagePastPool;
+  const int32_t page = d.rows[rowbase + k];
+  if (page < 0 || page >= d.pages) return kFaultPagePastPool;
+  *v = d.pool[(int64_t)page * d.page_rows + p % d.page_rows];
+  if (page == 0 || *v < 0) return kFaultUnwritten;
+  return 0;
+}
+
+// The failure the window check of position q would record (window_of, the scratch window
+// page, page_of, then the mirror comparison), without recording it.
+__device__ __forceinline__ unsigned window_at(const Dev& d, int64_t rowbase, long long q) {
+  const long long k = q / d.page_rows;
+  if (k >= d.window) return kFaultPagePastPool;
+  const int32_t w = d.rows[rowbase + d.entries + k];
+  if (w < 0 || w >= d.window_pages) return kFaultPagePastPool;
+  if (w == 0) return kFaultWindowScratch;
+  if (k >= d.entries) return kFaultPagePastPool;
+  const int32_t page = d.rows[rowbase + k];
+  if (page < 0 || page >= d.pages) return kFaultPagePastPool;
+  if (d.windows[(int64_t)w * d.page_rows + q % d.page_rows] != d.pool[(int64_t)page * d.page_rows + q % d.page_rows])
+    return kFaultWindowMismatch;
+  return 0;
+}
+
+constexpr int kPerThread = 4;  // positions each thread reads per chunk of model_token_warp
+
+// Fake::token (tests/engine.rs:115-128) with `next` (:56-62), by one warp: reads positions
+// 0..=last back through the row, checks the window over the last page_rows positions and
+// folds (the fold state in *h_out; token_of maps it to the token).  Each chunk of 32 x kPerThread positions is read by the 32 threads at once; the
+// first failing position of the chunk in position order records its fault (so the fault is
+// the one the sequential read-back meets first), and the fold runs over the chunk's values
+// in position order.  Every thread returns the same result.
+__device__ bool fold_warp(const Dev& d, int lane, long long last, unsigned long long* h_out) {
+  const int t = threadIdx.x & 31;
+  const int64_t rowbase = (int64_t)lane * (d.entries + d.window);
   unsigned long long h = 1469598103ull;
-  for (long long p = 0; p <= last; ++p) {
-    const int64_t page = page_of(d, lane, p);
-    if (page < 0) return false;
-    const int32_t v = d.pool[page * d.page_rows + p % d.page_rows];
-    if (page == 0 || v < 0) {
-      fault(d, kFaultUnwritten, lane, p);
-      return false;
+  for (long long base = 0; base <= last; base += 32 * kPerThread) {
+    int32_t v[kPerThread];
+    unsigned code[kPerThread];
+#pragma unroll
+    for (int j = 0; j < kPerThread; ++j) {
+      const long long p = base + 32 * j + t;
+      v[j] = 0;
+      code[j] = p <= last ? token_at(d, rowbase, p, &v[j]) : 0u;
     }
-    h = (h ^ ((unsigned long long)(uint32_t)v + 1000ull * (unsigned long long)p)) * 1099511628211ull;
+#pragma unroll
+    for (int j = 0; j < kPerThread; ++j) {
+      const unsigned bad = __ballot_sync(0xffffffffu, code[j] != 0);
+      if (bad) {
+        const int f = __ffs(bad) - 1;
+        if (t == f) fault(d, code[j], lane, base + 32 * j + f);
+        return false;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kPerThread; ++j) {
+      const long long p0 = base + 32 * j;
+      const long long n = last - p0 + 1;  // positions of this row of the chunk (may be <= 0)
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int32_t vi = __shfl_sync(0xffffffffu, v[j], i);
+        if (i < n) h = (h ^ ((unsigned long long)(uint32_t)vi + 1000ull * (unsigned long long)(p0 + i))) *
+                       1099511628211ull;
+      }
+    }
   }
   const long long first = last + 1 > d.page_rows ? last + 1 - d.page_rows : 0;
-  for (long long q = first; q <= last; ++q) {
-    const int64_t w = window_of(d, lane, q);
-    if (w < 0) return false;
-    if (w == 0) {
-      fault(d, kFaultWindowScratch, lane, q);
-      return false;
-    }
-    const int64_t page = page_of(d, lane, q);
-    if (page < 0) return false;
-    if (d.windows[w * d.page_rows + q % d.page_rows] != d.pool[page * d.page_rows + q % d.page_rows]) {
-      fault(d, kFaultWindowMismatch, lane, q);
+  for (long long base = first; base <= last; base += 32) {
+    const long long q = base + t;
+    const unsigned code = q <= last ? window_at(d, rowbase, q) : 0u;
+    const unsigned bad = __ballot_sync(0xffffffffu, code != 0);
+    if (bad) {
+      const int f = __ffs(bad) - 1;
+      if (t == f) fault(d, code, lane, base + f);
       return false;
     }
   }
-  *out = (int32_t)(h % 400ull) + 10;
+  *h_out = h;
+  return true;
+}
+
+__device__ __forceinline__ int32_t token_of(unsigned long long h) { return (int32_t)(h % 400ull) + 10; }
+
+__device__ bool model_token_warp(const Dev& d, int lane, long long last, int32_t* out) {
+  unsigned long long h;
+  if (!fold_warp(d, lane, last, &h)) return false;
+  *out = token_of(h);
+  return true;
+}
+
+// The read-back of a sequence one position longer than the last one checked in this step:
+// positions before p passed the previous read-back and only this lane writes them, so
+// reading position p, folding it and checking its window slot gives the same token and
+// the same fault as reading the whole sequence again.  Every thread of the warp computes it.
+__device__ bool fold_one(const Dev& d, int lane, long long p, unsigned long long* h) {
+  const int64_t rowbase = (int64_t)lane * (d.entries + d.window);
+  int32_t v = 0;
+  unsigned code = token_at(d, rowbase, p, &v);
+  if (code == 0) code = window_at(d, rowbase, p);
+  if (code != 0) {
+    if ((threadIdx.x & 31) == 0) fault(d, code, lane, p);
+    return false;
+  }
+  *h = (*h ^ ((unsigned long long)(uint32_t)v + 1000ull * (unsigned long long)p)) * 1099511628211ull;
   return true;
 }
 
@@ -213,13 +291,15 @@ __device__ void apply_messages(const Dev& d, const uint8_t* stream, uint64_t str
           if (w > 0) write_token(d, s_lane, p, toks[j]);
         }
         __syncthreads();
-        if (threadIdx.x == 0) {
+        if (threadIdx.x < 32) {  // the first warp reads the chunk's sequence back
           const long long end = (long long)s_pos + lens;
           int32_t t = -1;
-          model_token(d, s_lane, end - 1, &t);
-          d.lanes[s_lane].pos = (int32_t)end;
-          d.lanes[s_lane].tok = t;
-          s_reply = t;
+          model_token_warp(d, s_lane, end - 1, &t);
+          if (threadIdx.x == 0) {
+            d.lanes[s_lane].pos = (int32_t)end;
+            d.lanes[s_lane].tok = t;
+            s_reply = t;
+          }
         }
         __syncthreads();
         if (threadIdx.x == 0) replies[n_replies] = s_reply;
@@ -273,33 +353,45 @@ __global__ void apply_kernel(Dev d, const uint8_t* stream, uint64_t stream_bytes
 // One decode step (the test device's step, tests/engine.rs:173-193): each live lane with
 // reserved rows left emits 1 + ((step + lane) mod block) tokens, stopping early at its
 // reserved rows or the context's last position.  out[lane][block], -2 past a lane's tokens.
+// One decode step of lane l by one warp: the lane state and the writes by thread 0; the
+// first token of the step reads the whole sequence back (fold_warp), each further token
+// extends that read-back by its one new position (fold_one).
 __device__ void step_lane(const Dev& d, uint32_t step, int l, int32_t* out) {
+  const int t = threadIdx.x & 31;
   int32_t* o = out + (size_t)l * d.block;
-  for (int k = 0; k < d.block; ++k) o[k] = -2;
-  LaneState st = d.lanes[l];
+  for (int k = t; k < d.block; k += 32) o[k] = -2;
+  const LaneState st = d.lanes[l];
   if (!(st.live && st.pos < st.upto)) return;
   const int c = (int)(((unsigned long long)step + (unsigned long long)l) % (unsigned long long)d.block);
   long long pos = st.pos;
   int32_t tok = st.tok;
+  unsigned long long h = 0;  // fold state of the sequence read back so far in this step
   for (int k = 0; k <= c; ++k) {
     if (k > 0 && (pos >= st.upto || pos >= d.context - 1)) break;
     if (pos >= d.context - 1) {
-      fault(d, kFaultIdle, l, pos);
+      if (t == 0) fault(d, kFaultIdle, l, pos);
       break;
     }
-    if (!write_token(d, l, pos, tok)) break;
-    int32_t t;
-    if (!model_token(d, l, pos, &t)) break;
-    o[k] = t;
-    tok = t;
+    int ok = 0;
+    if (t == 0) ok = write_token(d, l, pos, tok) ? 1 : 0;
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    __syncwarp();  // thread 0's write, before the warp reads the sequence back
+    if (!ok) break;
+    if (!(k == 0 ? fold_warp(d, l, pos, &h) : fold_one(d, l, pos, &h))) break;
+    const int32_t tk = token_of(h);
+    if (t == 0) o[k] = tk;
+    tok = tk;
     pos += 1;
   }
-  d.lanes[l].pos = (int32_t)pos;
-  d.lanes[l].tok = tok;
+  if (t == 0) {
+    d.lanes[l].pos = (int32_t)pos;
+    d.lanes[l].tok = tok;
+  }
 }
 
+// A warp per lane.
 __global__ void step_kernel(Dev d, uint32_t step, int32_t* out) {
-  const int l = blockIdx.x * blockDim.x + threadIdx.x;
+  const int l = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
   if (l < d.width) step_lane(d, step, l, out);
 }
 
@@ -308,7 +400,7 @@ __global__ void step_kernel(Dev d, uint32_t step, int32_t* out) {
 // ---------------------------------------------------------------------------------------
 
 constexpr uint32_t kItemApply = 1, kItemStep = 2, kItemExit = 3;
-constexpr int kExecThreads = 256;
+constexpr int kExecThreads = 1024;  // 32 warps: a warp per lane per round
 
 // The mailbox, in pinned host memory mapped into the device's address space.  The host
 // fills the item fields, then publishes `posted`; the executor runs the item, copies the
@@ -381,7 +473,8 @@ __global__ void __launch_bounds__(kExecThreads, 1)
       apply_messages(d, reinterpret_cast<const uint8_t*>(s_dst), s_bytes, (int)s_n,
                      reinterpret_cast<int32_t*>(s_out) + s_base);
     } else if (s_kind == kItemStep) {
-      for (int l = threadIdx.x; l < d.width; l += kExecThreads) step_lane(d, s_step, l, reinterpret_cast<int32_t*>(s_out));
+      for (int l = (int)(threadIdx.x >> 5); l < d.width; l += kExecThreads / 32)
+        step_lane(d, s_step, l, reinterpret_cast<int32_t*>(s_out));
     }
     __threadfence_system();  // this thread's replies, before `done`
     __syncthreads();
@@ -843,8 +936,8 @@ int run_step(hk_handle* h) {
   if (h->ring) {
     HK_TRY(ring_run(h, kItemStep, 0, 0, h->s, 0));
   } else {
-    const int threads = 128;
-    const int blocks = (int)((h->cfg.width + threads - 1) / threads);
+    const int threads = 128;  // 4 lanes per block, a warp each
+    const int blocks = (int)(((int64_t)h->cfg.width * 32 + threads - 1) / threads);
     step_kernel<<<blocks, threads, 0, h->stream>>>(h->dev, h->s, h->d_out);
     HK_TRY_LAUNCH("step_kernel");
     HK_TRY(readback(h, words));
