@@ -66,6 +66,7 @@ SIGNATURES = {
     "hk_pools": (C.c_int, [P, P, P]),
     "hk_push": (C.c_int, [P, P]),
     "hk_drain": (C.c_int, [P, P, SZ, P, P, SZ, P]),
+    "hk_drain_logprobs": (C.c_int, [P, P, SZ, P, P, SZ, P]),
     "hk_encode_share": (C.c_int, [P, P, P, SZ, P]),
     "hk_kernel_ops_of": (C.c_int, [P, P]),
     "hk_engine_defaults": (None, [P]),
@@ -78,6 +79,7 @@ SIGNATURES = {
     "hk_engine_run": (C.c_int, [P]),
     "hk_engine_hangup": (C.c_int, [P, U64]),
     "hk_engine_outputs": (C.c_int, [P, U64, I64, P, SZ, P, P, SZ]),
+    "hk_engine_outputs_lp": (C.c_int, [P, U64, I64, P, SZ, P, P, SZ, P, SZ, P]),
     "hk_engine_metrics": (C.c_int, [P, P, P, SZ, P, P, SZ, P]),
     "hk_rope_table": (C.c_int, [I64, I32, F32, I32, F32, F32, F32, P]),
 }

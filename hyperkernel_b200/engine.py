@@ -79,9 +79,18 @@ DrainFn = C.CFUNCTYPE(C.c_int, C.c_void_p, C.POINTER(Event), SZ, C.POINTER(SZ), 
 ErrorFn = C.CFUNCTYPE(C.c_void_p, C.c_void_p)
 
 
+class Logprob(C.Structure):
+    """hk_logprob: one (token id, logprob) pair of a Sampled's logprob list."""
+    _fields_ = [("id", U32), ("logprob", F32)]
+
+
+LogprobsFn = C.CFUNCTYPE(C.c_int, C.c_void_p, C.POINTER(U32), SZ, C.POINTER(SZ), C.POINTER(Logprob), SZ,
+                         C.POINTER(SZ))
+
+
 class KernelOps(C.Structure):
     _fields_ = [("self", C.c_void_p), ("pools", PoolsFn), ("push", PushFn), ("drain", DrainFn),
-                ("error", ErrorFn)]
+                ("error", ErrorFn), ("logprobs", LogprobsFn)]
 
 
 def engine_config(**fields) -> EngineConfig:
@@ -186,17 +195,42 @@ class Device:
 class CallbackKernel:
     """hk_kernel_ops over a Python object with pools() -> (pages, windows), push(Share) -> None
     and drain() -> (events, ids) where events are (kind, step, lane, token, clipped, ids_offset)
-    tuples.  Exceptions become HK_ESTATE with their message."""
+    tuples, and optionally logprobs() -> the last drain's logprob lists, one list of
+    (id, logprob) pairs per Sampled slot in event order (hk_drain_logprobs's layout).
+    Exceptions become HK_ESTATE with their message."""
 
     def __init__(self, impl):
         self.impl = impl
         self._msg = C.create_string_buffer(512)
         self._pending = None
+        self._pending_lp = None
+        lp = LogprobsFn(self._logprobs) if hasattr(impl, "logprobs") else LogprobsFn()
         self._fns = (PoolsFn(self._pools), PushFn(self._push), DrainFn(self._drain),
-                     ErrorFn(self._error))
+                     ErrorFn(self._error), lp)
 
     def ops(self) -> KernelOps:
         return KernelOps(None, *self._fns)
+
+    def _logprobs(self, _self, counts, counts_cap, n_counts, pairs, pairs_cap, n_pairs):
+        try:
+            if self._pending_lp is None:
+                self._pending_lp = self.impl.logprobs()
+            lists = self._pending_lp
+            total = sum(len(x) for x in lists)
+            n_counts[0], n_pairs[0] = len(lists), total
+            if len(lists) > counts_cap or total > pairs_cap:
+                return _lib.HK_ESPACE
+            k = 0
+            for i, lst in enumerate(lists):
+                counts[i] = len(lst)
+                for tid, lp in lst:
+                    pairs[k].id, pairs[k].logprob = tid, lp
+                    k += 1
+            self._pending_lp = None
+            return 0
+        except Exception as e:  # noqa: BLE001
+            self._pending_lp = None
+            return self._fail(e)
 
     def _fail(self, e) -> int:
         self._msg.value = str(e).encode()[:511]
@@ -246,6 +280,7 @@ class Heard:
     tokens: list
     end: str | None
     message: str
+    logprobs: list | None = None  # per token, its (id, logprob) pairs
 
 
 class Engine:
@@ -298,29 +333,43 @@ class Engine:
         _lib.check(_lib.lib().hk_engine_hangup(self._e, request))
 
     def outputs(self, request: int, timeout_ms: int = 0):
-        """[(kind, end, value, message)] of the request's outputs so far."""
+        """[(kind, end, value, message, logprobs)] of the request's outputs so far; a token's
+        logprobs are its (id, logprob) pairs (empty unless its Sampling asked for logprobs)."""
         buf = (Out * 256)()
         msg = C.create_string_buffer(512)
+        cap = 256 * 66
+        pairs = (Logprob * cap)()
         out = []
         while True:
-            n = SZ()
-            _lib.check(_lib.lib().hk_engine_outputs(self._e, request, timeout_ms, buf, 256, C.byref(n),
-                                                    msg, 512))
+            n, npairs = SZ(), SZ()
+            rc = _lib.lib().hk_engine_outputs_lp(self._e, request, timeout_ms, buf, 256, C.byref(n), msg, 512,
+                                                 pairs, cap, C.byref(npairs))
+            if rc == _lib.HK_ESPACE:  # one token's pairs past the buffer
+                cap = npairs.value
+                pairs = (Logprob * cap)()
+                continue
+            _lib.check(rc)
+            k = 0
             for i in range(n.value):
                 o = buf[i]
-                out.append((o.kind, o.end, o.value, msg.value.decode() if o.kind == OUT_END else ""))
-            if n.value < 256:
+                lps = []
+                if o.kind == OUT_TOKEN:
+                    lps = [(pairs[k + j].id, pairs[k + j].logprob) for j in range(o.end)]
+                    k += o.end
+                out.append((o.kind, o.end, o.value, msg.value.decode() if o.kind == OUT_END else "", lps))
+            if n.value == 0:
                 return out
-            timeout_ms = 0
+            timeout_ms = 0  # then take what else is queued, without waiting
 
     def heard(self, request: int, timeout_ms: int = 0) -> Heard:
         """The tokens and the end the request's listener saw (tests/engine.rs:270-281)."""
-        h = Heard([], [], None, "")
-        for kind, end, value, message in self.outputs(request, timeout_ms):
+        h = Heard([], [], None, "", [])
+        for kind, end, value, message, lps in self.outputs(request, timeout_ms):
             if kind == OUT_SEATED:
                 h.seated.append(value)
             elif kind == OUT_TOKEN:
                 h.tokens.append(value)
+                h.logprobs.append(lps)
             elif h.end is None:
                 h.end, h.message = END_NAMES[end], message
         return h

@@ -385,8 +385,8 @@ typedef struct {
 
 /* One Event.  Step: `ids` is the offset in the drain's id array of width * block sampled ids,
  * lane-major; a lane's list ends at its first -2 (lanes that did not decode start with -2).
- * Prompted: `token` (negative = the logits were not finite) and `clipped`.  Sampled
- * logprob rows do not cross this boundary yet: every Sampled has an empty logprob list. */
+ * Prompted: `token` (negative = the logits were not finite) and `clipped`.  Each Sampled's
+ * logprob list comes from hk_drain_logprobs. */
 typedef struct {
     uint32_t kind;
     uint32_t step;
@@ -495,6 +495,22 @@ int hk_push(hk_handle* handle, const hk_share* share);
 int hk_drain(hk_handle* handle, hk_event* events, size_t cap, size_t* n, int32_t* ids,
              size_t ids_cap, size_t* ids_n);
 
+/* One (token id, logprob) pair of a Sampled's logprob list (src/gpu/mod.rs:37-40). */
+typedef struct {
+    uint32_t id;
+    float logprob;
+} hk_logprob;
+
+/* The logprob lists of the Sampled values of the events the last successful hk_drain
+ * returned, in event order: width * block lists per Step event (one per id slot; slots past
+ * a lane's list have none) and one per Prompted event.  List i has counts[i] pairs, stored
+ * one list after another in `pairs` (the reply's top pairs, then the token's own, as
+ * src/gpu/feed.rs:202-208 reads them).  HK_ESPACE with *n_counts / *n_pairs set when a
+ * buffer is short.  The device kernel's test model samples no logprobs: its lists are
+ * empty. */
+int hk_drain_logprobs(hk_handle* handle, uint32_t* counts, size_t counts_cap, size_t* n_counts,
+                      hk_logprob* pairs, size_t pairs_cap, size_t* n_pairs);
+
 /* The request-ring encoding of a share (src/gpu/feed.rs:40-103, src/gpu/ring.rs:59-125):
  * one slot per command (u32 message id at byte 0, the message body at byte 16, slot size
  * 16 + widest body rounded up to 16 bytes) followed by the side blocks the messages' spans
@@ -519,6 +535,10 @@ typedef struct {
     int (*drain)(void* self, hk_event* events, size_t cap, size_t* n, int32_t* ids,
                  size_t ids_cap, size_t* ids_n);
     const char* (*error)(void* self);
+    /* Optional (NULL: every Sampled has an empty logprob list): hk_drain_logprobs's contract,
+     * called after each successful drain. */
+    int (*logprobs)(void* self, uint32_t* counts, size_t counts_cap, size_t* n_counts,
+                    hk_logprob* pairs, size_t pairs_cap, size_t* n_pairs);
 } hk_kernel_ops;
 
 /* Fills `ops` with the callbacks of a device handle. */
@@ -566,7 +586,7 @@ int hk_engine_run(hk_engine* engine);
 int hk_engine_hangup(hk_engine* engine, uint64_t request);
 
 #define HK_OUT_SEATED 0 /* value = cached tokens */
-#define HK_OUT_TOKEN 1  /* value = token id */
+#define HK_OUT_TOKEN 1  /* value = token id, end = the number of its logprob pairs */
 #define HK_OUT_END 2    /* end = HK_END_* */
 #define HK_END_STOP 0
 #define HK_END_LENGTH 1
@@ -583,6 +603,13 @@ typedef struct {
  * Refused end is copied into `message` (NUL-terminated, truncated to message_cap). */
 int hk_engine_outputs(hk_engine* engine, uint64_t request, int64_t timeout_ms, hk_out* out,
                       size_t cap, size_t* n, char* message, size_t message_cap);
+/* hk_engine_outputs with each token's logprobs (Token.logprobs: the token's own pair, then the
+ * top Sampling.logprobs pairs, src/engine/lanes.rs:53-73), appended to `pairs` in output order
+ * (a token's `end` is its pair count).  It stops before a token whose pairs do not fit;
+ * HK_ESPACE with *n_pairs set when not even the first output's pairs fit. */
+int hk_engine_outputs_lp(hk_engine* engine, uint64_t request, int64_t timeout_ms, hk_out* out,
+                         size_t cap, size_t* n, char* message, size_t message_cap, hk_logprob* pairs,
+                         size_t pairs_cap, size_t* n_pairs);
 
 /* StepMetrics (src/engine/metrics.rs:4-19) summed over the run, as Metrics::total. */
 typedef struct {

@@ -159,3 +159,83 @@ def test_encode_share_refuses_bad_commands():
     share, keep = H.make_share(0, 2, [(H.CMD_PAGES, 0, 30, 8, [1, 2, 3], (0, 0, 0), None)])
     with pytest.raises(_lib.HKError, match="row entries 30..33 past 32"):
         H.encode_share(cfg, share)
+
+
+def _row(t):
+    """A deterministic reply row for token t: three top pairs, then the token's own."""
+    return [((t * 7) % 400 + 10, -0.5), ((t * 13) % 400 + 10, -1.25), ((t * 17) % 400 + 10, -2.0), (t, -0.75)]
+
+
+class _LogprobFake(E.Fake):
+    """The reference's test device, with a logprob list on every sampled value."""
+
+    def drain(self):
+        evs, err = super().drain()
+        for e in evs:
+            if isinstance(e, E.Step):
+                e.lanes = [[E.Sampled(s.id, _row(s.id) if s.id >= 0 else []) for s in toks] for toks in e.lanes]
+            elif isinstance(e, E.Prompted):
+                e.token = E.Sampled(e.token.id, _row(e.token.id) if e.token.id >= 0 else [])
+        return evs, err
+
+
+class _LogprobPort(P.FakePort):
+    """FakePort that also hands over the last drain's logprob lists (hk_drain_logprobs's layout:
+    block slots per lane per Step, one per Prompted)."""
+
+    def drain(self):
+        evs, err = self.fake.drain()
+        assert err is None
+        self._lists = []
+        for e in evs:
+            if isinstance(e, E.Step):
+                for toks in e.lanes:
+                    self._lists += [toks[k].logprobs if k < len(toks) else [] for k in range(self.block)]
+            elif isinstance(e, E.Prompted):
+                self._lists.append(e.token.logprobs)
+        self.fake.drain = lambda: (evs, None)  # FakePort.drain converts the same events
+        try:
+            return super().drain()
+        finally:
+            del self.fake.drain
+
+    def logprobs(self):
+        return self._lists
+
+
+def test_tokens_carry_the_logprobs_asked():
+    """src/engine/lanes.rs:53-73 through libhk's engine: a token's logprobs are its own pair,
+    then the first `logprobs` of the top pairs the kernel returned with it (all of them when
+    fewer), none when none were asked; the same lists as the oracle engine's."""
+    asks = [P.Ask(range(1, 20), 12, sampling=E.Sampling(0.0, 1.0, 0, 0, 0)),
+            P.Ask(range(3, 30), 9, sampling=E.Sampling(0.0, 1.0, 0, 0, 2)),
+            P.Ask(range(5, 14), 7, sampling=E.Sampling(0.0, 1.0, 0, 0, 5))]
+    sc = P.Scenario("logprobs", asks, pages=80, windows=24, block=3)
+
+    def fake():
+        return _LogprobFake(sc.pages, sc.windows, P.PAGE_ROWS, P.ENTRIES, P.WIDTH, P.CONTEXT, P.CHUNK,
+                            drafts=sc.block - 1)
+
+    jobs, sinks = E.Channel(), []
+    for a in asks:
+        sink = E.Sink()
+        jobs.send(E.JobRun(E.Request(list(a.prompt), a.sampling, a.limit, list(a.stop), sink)))
+        sinks.append(sink)
+    jobs.close()
+    assert E.run(P.oracle_model(sc), P.oracle_pool(sc), fake(), jobs, E.Metrics(), sc.plan, E.EngineConfig()) is None
+    want = [[o.logprobs for o in s.items if isinstance(o, E.OutToken)] for s in sinks]
+
+    port = _LogprobPort(fake(), sc.block)
+    kern = H.CallbackKernel(port)
+    eng = H.Engine(P.engine_config(sc), kern.ops(), keep=kern)
+    reqs = [eng.submit(a.prompt, a.limit, a.stop,
+                       H.Sampling(a.sampling.temperature, a.sampling.top_p, a.sampling.top_k, a.sampling.logprobs,
+                                  a.sampling.seed)) for a in asks]
+    eng.close()
+    assert eng.run() == 0, eng.failure
+    got = [eng.heard(r).logprobs for r in reqs]
+    assert got == want
+    assert all(lp == [] for lp in got[0])
+    assert all(len(lp) == 3 for lp in got[1]) and all(len(lp) == 4 for lp in got[2])
+    own = want[1][0][0]  # the first token's list: its own pair, then the top two
+    assert want[1][0] == [own] + _row(own[0])[:2]
