@@ -925,7 +925,8 @@ def _engine_requests(n, seed):
 def _engine_session(H, transport, device_index, requests):
     """One session of the engine over the device kernel: every request submitted, the jobs
     closed, hk_engine_run to the end.  Returns (seconds, iterations with tokens, tokens
-    generated, kernel launches)."""
+    generated, kernel launches since the device was opened: with the ring transport, the
+    resident executor launched by hk_open runs every item of the timed run)."""
     from hyperkernel_b200 import _lib as hk
 
     context = ENGINE_PAGE_ROWS * ENGINE_ENTRIES
@@ -933,6 +934,7 @@ def _engine_session(H, transport, device_index, requests):
     cfg = H.Config(model=H.MODEL_FNV, page_rows=ENGINE_PAGE_ROWS, entries=ENGINE_ENTRIES, window=ENGINE_ENTRIES,
                    width=ENGINE_LANES, context=context, chunk=ENGINE_CHUNK, block=ENGINE_BLOCK, pages=pages,
                    window_pages=pages, clip=0, device=device_index, transport=transport)
+    l0 = hk.kernel_launches()
     dev = H.Device(cfg)
     try:
         eng = H.Engine(H.engine_config(page_rows=ENGINE_PAGE_ROWS, entries=ENGINE_ENTRIES, window=ENGINE_ENTRIES,
@@ -941,7 +943,6 @@ def _engine_session(H, transport, device_index, requests):
                        dev.ops(), keep=dev)
         reqs = [eng.submit(pr, lim) for pr, lim in requests]
         eng.close()
-        l0 = hk.kernel_launches()
         t0 = time.perf_counter()
         rc = eng.run()
         dt = time.perf_counter() - t0
@@ -977,7 +978,7 @@ def _run_engine(args, torch, dist, hk, ClockSampler, world, rank, local, device,
     barrier()
     sampler.stop()
     clocks = sampler.summary(t0, t1)
-    dt_launch, iters_launch, tokens_launch, _ = _engine_session(H, 0, local, requests)
+    dt_launch, iters_launch, tokens_launch, launches_launch = _engine_session(H, 0, local, requests)
     (dt,) = _reduce_max(torch, dist, world, device, dt * 1e3)
     dt /= 1e3
     cpu = None
@@ -998,8 +999,11 @@ def _run_engine(args, torch, dist, hk, ClockSampler, world, rank, local, device,
                    "parallelism": f"replicas{world}" if world > 1 else "single",
                    "timing": "host clock around hk_engine_run (host-driven loop); a step = an engine iteration "
                              "that produced tokens",
+                   "gpu_launches_note": "ring transport: the resident executor (launched once when the device "
+                                        "is opened) runs every apply and step item",
                    "launch_transport": {"tokens_per_s": tokens_launch * world / dt_launch,
-                                        "ms_per_step": dt_launch * 1e3 / max(iters_launch, 1)}},
+                                        "ms_per_step": dt_launch * 1e3 / max(iters_launch, 1),
+                                        "gpu_launches": int(launches_launch)}},
         "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
                      "traffic": None, "kernel": "executor_kernel (apply + step of the test model)",
                      "note": "latency-bound: a step moves a few hundred KB; the per-step time is the measure",
