@@ -12,7 +12,9 @@ import json
 import sys
 from pathlib import Path
 
-src = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/tests/fixtures/rope.json")
+if len(sys.argv) != 2:
+    sys.exit("usage: python tests/golden/make_rope_golden.py <reference checkout>/tests/fixtures/rope.json")
+src = Path(sys.argv[1])
 data = json.loads(src.read_text())
 out = {"source": "reference tests/fixtures/rope.json (src/gpu/load.rs:1036-1053)", "tables": []}
 for t in data["tables"]:
