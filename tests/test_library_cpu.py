@@ -20,6 +20,13 @@ def test_every_header_function_is_exported(hk):
     assert set(names) == set(hk.SIGNATURES), "ctypes prototypes out of step with include/hk.h"
 
 
+def test_every_header_function_has_a_reference_side_binding(hk):
+    """INTEGRATION.md shows the Rust declaration a maintainer adds for each entry point."""
+    text = (Path(__file__).resolve().parents[1] / "INTEGRATION.md").read_text()
+    missing = [n for n in hk.header_functions() if f"fn {n}(" not in text]
+    assert not missing, f"no Rust binding shown for: {missing}"
+
+
 def test_version_and_no_device_is_an_error(hk):
     import torch
 
