@@ -334,6 +334,24 @@ def test_gemm_fp8_matches_oracle(hk, orc, cuda, m, n, k):
 # a12-a15 MoE
 # ------------------------------------------------------------------------------------------
 
+@pytest.mark.parametrize("n,k", [(24576, 1536), (7168, 16384)])
+def test_gemm_fp8_config3_shapes_match_oracle_on_sampled_rows(hk, orc, cuda, n, k):
+    """Config 3's q_b and o projections at full size (4144 tokens) through the SM-pair kernel;
+    the oracle for 16 sampled rows (each output row depends only on its own input row)."""
+    m = 48 + 2 * 2048
+    g = torch.Generator(device=cuda).manual_seed(71)
+    x = torch.randn((m, k), generator=g, device=cuda).to(torch.bfloat16)
+    b = torch.randint(0, 256, (n, k), generator=g, device=cuda, dtype=torch.uint8)
+    wq = torch.where((b & 0x7F) == 0x7F, b ^ 1, b)
+    sw = torch.rand((n // 128, k // 128), generator=g, device=cuda) * 1e-3 + 1e-4
+    xq, sx = hk.quant_fp8(x)
+    y = hk.gemm_fp8(xq, sx, wq, sw)
+    hk.check_errors()
+    rows = np.array([0, 1, 127, 128, 255, 256, 1000, 2047, 2048, 3333, 4095, 4096, 4100, 4127, 4128, 4143])
+    want = orc.gemm_fp8(xq.cpu().numpy()[rows], sx.cpu().numpy()[rows], wq.cpu().numpy(), sw.cpu().numpy())
+    assert rel_err(to_np_bf16(y)[rows], want) <= TOL
+
+
 def test_route_bit_exact(hk, orc, cuda):
     rng = W.Rng(50)
     T, E, K = 512, 256, 8
@@ -384,6 +402,44 @@ def test_moe_layer_matches_oracle(hk, orc, cuda, T, E, H, I, K):
     hk.check_errors()
     assert rel_err(to_np_bf16(gy)[:T * K], y) <= TOL
     assert rel_err(to_np_bf16(out), want) <= TOL
+
+
+def test_moe_layer_full_size_matches_oracle_on_sampled_tokens(hk, orc, cuda):
+    """Config 4 at full size (512 tokens, 256 routed experts, top 8, hidden 7168, inter 2048:
+    11.3 GB of e4m3 weights, so every expert is hit): the whole layer on the GPU; the oracle
+    for six sampled tokens from the experts they route to (quantisation, routing and the h
+    requantisation are per token, so a token's output depends on nothing else)."""
+    T, E, H, I, K = 512, 256, 7168, 2048, 8
+    g = torch.Generator(device=cuda).manual_seed(61)
+
+    def e4m3(shape):
+        b = torch.randint(0, 256, shape, generator=g, device=cuda, dtype=torch.uint8)
+        return torch.where((b & 0x7F) == 0x7F, b ^ 1, b)
+
+    w13, w2 = e4m3((E, 2 * I, H)), e4m3((E, H, I))
+    s13 = torch.rand((E, 2 * I // 128, H // 128), generator=g, device=cuda) * 4e-5 + 2e-5
+    s2 = torch.rand((E, H // 128, I // 128), generator=g, device=cuda) * 4e-5 + 2e-5
+    logits = torch.randn((T, E), generator=g, device=cuda)
+    x = torch.randn((T, H), generator=g, device=cuda).to(torch.bfloat16)
+    gi, gw = hk.route(logits, None, K, 1.0)
+    goff, gtok, gpw, ginv = hk.permute(gi, gw, E)
+    gxq, gsx = hk.quant_fp8(x)
+    gy = hk.moe_grouped(gxq, gsx, goff, gtok, T * K, H, I, w13, s13, w2, s2)
+    out = hk.combine(gy, gpw, ginv, None, T, K)
+    hk.check_errors()
+    assert (goff.cpu().numpy()[1:] > goff.cpu().numpy()[:-1]).all(), "an expert without rows"
+
+    S = np.array([0, 77, 150, 301, 444, 511])
+    ids, w = orc.route(logits.cpu().numpy()[S], None, K, 1.0)
+    assert np.array_equal(ids, gi.cpu().numpy()[S])
+    used, cid = np.unique(ids, return_inverse=True)
+    sel = torch.from_numpy(used.astype(np.int64)).to(cuda)
+    host = [t.index_select(0, sel).cpu().numpy() for t in (w13, s13, w2, s2)]
+    off, tok, pw, inv = orc.permute(cid.reshape(ids.shape).astype(np.int32), w, len(used))
+    xq, sx = orc.quant_fp8(x.view(torch.int16).cpu().numpy().view(np.uint16)[S])
+    y = orc.moe_grouped(xq, sx, off, tok, H, I, *host)
+    want = orc.combine(W.f32_to_bf16_bits(y), pw, inv, None, len(S), K)
+    assert rel_err(to_np_bf16(out)[S], want) <= TOL
 
 
 def test_combine_matches_oracle(hk, orc, cuda):
