@@ -210,6 +210,36 @@ def test_mla_decode_128_heads_matches_oracle(hk, orc, cuda, impl):
     assert np.abs(lse - want_lse).max() <= 1e-3
 
 
+def test_mla_tcgen05_million_token_lane_on_sampled_heads(hk, orc, cuda):
+    """Config 5's 1,048,576-token lane (a 16,384-page block-table row, pages scattered over the
+    pool) with 1 + 4 rows, beside a short lane, through pack, append and the tcgen05 kernel;
+    the oracle for 4 sampled heads of every row."""
+    lay = W.config5_layout(seed=45, long_ctx=1 << 20, short_lanes=1, lo=4096, hi=8192, rows=5)
+    T = lay.num_tokens
+    rng = W.Rng(46)
+    q_bits = W.f32_to_bf16_bits(rng.normal(T * 128 * 576).astype(np.float32)).reshape(T, 128, 576)
+    new_bits = W.f32_to_bf16_bits(rng.normal(T * 576).astype(np.float32)).reshape(T, 576)
+    g = torch.Generator(device=cuda).manual_seed(47)
+    c = torch.randn((lay.num_slots, 576), generator=g, device=cuda).to(torch.bfloat16)
+    cache = c.view(torch.int16).cpu().numpy().view(np.uint16).copy()
+    p = orc.pack(lay.new_rows, lay.context, lay.block_table, 64, lay.num_pages, T)
+    assert p["err"] == 0
+    gp = hk.pack(dev(lay.new_rows.astype(np.int32), cuda), dev(lay.context.astype(np.int32), cuda),
+                 dev(lay.block_table, cuda), 64, lay.num_pages, T)
+    assert np.array_equal(gp["slot_mapping"].cpu().numpy()[:T], p["slot_mapping"][:T])
+    hk.kv_append_bf16(bf16_dev(new_bits, cuda), gp["slot_mapping"], c)
+    scale = 1.0 / math.sqrt(576)
+    out, lse = hk.mla_decode(bf16_dev(q_bits, cuda), c, dev(lay.block_table, cuda), gp["cu_seqlens"],
+                             gp["positions"], 64, int(lay.kv_len.max()), scale, impl=2)
+    hk.check_errors()
+    heads = np.array([0, 37, 90, 127])
+    orc.kv_append_bf16(new_bits, p["slot_mapping"][:T], cache)
+    want, want_lse = orc.mla_decode(np.ascontiguousarray(q_bits[:, heads]), lay.block_table, p["cu_seqlens"],
+                                    p["positions"][:T], 64, scale, kv_bf16=cache)
+    assert rel_err(to_np_bf16(out)[:, heads], want) <= TOL
+    assert np.abs(lse.cpu().numpy()[:, heads] - want_lse).max() <= 1e-3
+
+
 @pytest.mark.parametrize("seed,lanes,lo,hi", [(31, 1, 1, 2), (32, 3, 30, 200), (33, 20, 64, 5000)])
 def test_mla_tcgen05_ragged_edges(hk, orc, cuda, seed, lanes, lo, hi):
     """Single-row and sub-page contexts, partial last pages, many short lanes."""
