@@ -719,6 +719,35 @@ def test_sample_verify_matches_oracle(hk, cuda, vocab, seed, n):
     assert np.abs(got - want_lp).max() <= 1e-5
 
 
+def test_sample_verify_at_the_largest_vocabulary(hk, cuda):
+    """vocab = 4,194,304 (the entry point's limit): a top-p / temperature lane of 3 rows and a
+    greedy lane of 2, drafts that the oracle's draws accept; ids, states and logprob rows as
+    the oracle's."""
+    from oracle import sample as S
+
+    vocab, block, n = 1 << 22, 3, 6
+    rng = np.random.default_rng(9)
+    cu = np.array([0, 3, 5], np.int32)
+    samplings = [dict(temperature=0.9, top_k=0, top_p=0.8), dict(temperature=0.0, top_k=0, top_p=1.0)]
+    logits = (rng.standard_normal((5, vocab)) * 2.0).astype(np.float32)
+    states = [12345, 678]
+    drafts = np.full((2, block - 1), -7, np.int32)
+    for j in range(block - 1):  # drafts equal to the oracle's draws: every row is accepted
+        ids, _, _ = S.sample_verify(logits, cu, samplings, states, drafts, block, 0)
+        drafts[:, j] = ids[:, j]
+    want_ids, want_lp, want_states = S.sample_verify(logits, cu, samplings, states, drafts, block, n)
+    assert (want_ids[0] >= 0).all() and (want_ids[1, :2] >= 0).all()
+    st = torch.tensor(np.array(states, dtype=np.uint64).view(np.int64), device=cuda)
+    ids, lp = hk.sample_verify(dev(logits, cuda), dev(cu, cuda), hk.sampling_array(samplings, cuda), st,
+                               dev(drafts, cuda), block, n)
+    hk.check_errors()
+    assert np.array_equal(ids.cpu().numpy(), want_ids)
+    assert st.cpu().numpy().view(np.uint64).tolist() == want_states
+    got = lp.cpu().numpy()
+    assert np.array_equal(got[..., 0:-1:2], want_lp[..., 0:-1:2])
+    assert np.abs(got - want_lp).max() <= 1e-5
+
+
 def test_mla_tcgen05_prefill_chunk_with_decode_lanes(hk, orc, cuda):
     """Configuration 3's shape in small: decode lanes beside a chunked-prefill segment of 160
     causal rows after 100 cached rows, through the tcgen05 kernel."""
