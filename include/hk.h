@@ -332,7 +332,8 @@ typedef struct {
  * -2; a row with a non-finite logit gives -1 and ends the lane.  lp [num_lanes][block]
  * [2 n_logprobs + 1] (may be NULL when n_logprobs = 0): per token, the n_logprobs best
  * (id, logprob) pairs of the row's log-softmax (id -1 past the vocabulary), then the token's
- * own logprob.  vocab <= 4,194,304; workspace 256-byte aligned, hk_sample_workspace_size. */
+ * own logprob.  vocab <= 4,194,304; 1 <= block <= 32; n_logprobs <= 64; workspace 256-byte
+ * aligned, hk_sample_workspace_size bytes. */
 size_t hk_sample_workspace_size(int32_t num_rows, int32_t vocab);
 int hk_sample_verify(const float* logits, int32_t vocab, const int32_t* cu_rows, int32_t num_lanes,
                      int32_t num_rows, int32_t block, const hk_sampling* sampling, uint64_t* state,
