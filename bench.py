@@ -78,6 +78,45 @@ def cpu_sample_layout(lay, target_rows: int):
     return sub, rows
 
 
+def cpu_lanes_seconds(ctx, rows, fp8=False):
+    """Times the CPU oracle (pack + append + attention) on lanes of cached lengths `ctx` with
+    `rows` new rows each (bf16 or e4m3 latent cache); returns (seconds, query-KV pairs,
+    threads)."""
+    import oracle
+    from hyperkernel_b200 import workload as W
+
+    oracle.use_all_cores()
+    sub = W.paged_layout(W.Rng(99), np.asarray(ctx, np.int64), np.asarray(rows, np.int64), PAGE)
+    g = np.random.default_rng(7)
+    T = sub.num_tokens
+    q = g.integers(0, 1 << 16, size=(T, HEADS, DK), dtype=np.uint16) & np.uint16(0xBFFF)
+    kv_new = g.integers(0, 1 << 16, size=(T, DK), dtype=np.uint16) & np.uint16(0xBFFF)
+    if fp8:
+        c8 = g.integers(0, 256, size=(sub.num_slots, DK), dtype=np.uint8)
+        c8[(c8 & 0x7F) == 0x7F] ^= 1
+        s8 = (g.random(sub.num_slots) * 0.01 + 0.001).astype(np.float32)
+    else:
+        cache = g.integers(0, 1 << 16, size=(sub.num_slots, DK), dtype=np.uint16) & np.uint16(0xBFFF)
+    t0 = time.perf_counter()
+    p = oracle.pack(sub.new_rows, sub.context, sub.block_table, PAGE, sub.num_pages, T)
+    slots = p["slot_mapping"][:T]
+    if fp8:
+        oracle.kv_append_fp8(kv_new, slots, c8, s8)
+        oracle.mla_decode(q, sub.block_table, p["cu_seqlens"], p["positions"][:T], PAGE, 1.0 / math.sqrt(DK),
+                          kv_fp8=c8, kv_scale=s8)
+    else:
+        oracle.kv_append_bf16(kv_new, slots, cache)
+        oracle.mla_decode(q, sub.block_table, p["cu_seqlens"], p["positions"][:T], PAGE, 1.0 / math.sqrt(DK),
+                          kv_bf16=cache)
+    dt = time.perf_counter() - t0
+    pairs = int(sum(int(c) * int(r) + int(r) * (int(r) + 1) // 2 for c, r in zip(ctx, rows)))
+    return dt, pairs, oracle.threads()
+
+
+def _query_kv_pairs(lay):
+    return int(sum(int(c) * int(r) + int(r) * (int(r) + 1) // 2 for c, r in zip(lay.context, lay.new_rows)))
+
+
 def cpu_step_seconds(lay, target_rows: int, reps: int = 1):
     """Times the CPU oracle (pack + append + attention) on a sample; returns
     (seconds per full step extrapolated by KV rows, sample rows, sample lanes, threads)."""
@@ -604,9 +643,10 @@ def _run_longctx(args, torch, dist, hk, par, ClockSampler, world, rank, local, d
     if kv_bf16 is not None:
         hk.kv_dequant_fp8(cache, scales, PAGE, out=kv_bf16, pages=None if world == 1 else my_pages)
 
-    def step(ev=None):
+    def step(ev=None, q_in=None, kv_in=None):
+        q_use = q if q_in is None else q_in
         pk = hk.pack(lane_tokens, lane_pos, bt, PAGE, lay.num_pages, T)
-        hk.kv_append_fp8(kv_new, pk["slot_mapping"], cache, scales)
+        hk.kv_append_fp8(kv_new if kv_in is None else kv_in, pk["slot_mapping"], cache, scales)
         if ev is not None:
             ev[0].record(stream)
         if kv_bf16 is not None:
@@ -615,12 +655,13 @@ def _run_longctx(args, torch, dist, hk, par, ClockSampler, world, rank, local, d
             else:
                 hk.kv_dequant_fp8_rows(cache, scales, pk["slot_mapping"], kv_bf16, PAGE)
         if world == 1:
-            o, lse = hk.mla_decode(q, kv_bf16, bt, pk["cu_seqlens"], pk["positions"], PAGE, max_kv, scale)
+            o, lse = hk.mla_decode(q_use, kv_bf16, bt, pk["cu_seqlens"], pk["positions"], PAGE, max_kv, scale)
         elif portable:
-            o, lse = hk.mla_partial_fp8(q, cache, scales, bt, pk["cu_seqlens"], pk["positions"], kb, ke, PAGE,
+            o, lse = hk.mla_partial_fp8(q_use, cache, scales, bt, pk["cu_seqlens"], pk["positions"], kb, ke, PAGE,
                                         max_kv, scale)
         else:
-            o, lse = hk.mla_partial(q, kv_bf16, bt, pk["cu_seqlens"], pk["positions"], kb, ke, PAGE, max_kv, scale)
+            o, lse = hk.mla_partial(q_use, kv_bf16, bt, pk["cu_seqlens"], pk["positions"], kb, ke, PAGE, max_kv,
+                                    scale)
         if ev is not None:
             ev[1].record(stream)
         if world > 1:
@@ -643,6 +684,30 @@ def _run_longctx(args, torch, dist, hk, par, ClockSampler, world, rank, local, d
     clocks = sampler.summary(t0, t1)
     hk.check_errors()
     ms, attn_ms = _reduce_max(torch, dist, world, device, ms, attn_ms)
+    # end to end: the step's queries and new latent rows from pinned host memory, its outputs
+    # (the merged long lane's on N > 1) back to pinned host memory
+    hq = torch.empty(q.shape, dtype=q.dtype).pin_memory().copy_(q.cpu())
+    hkv = torch.empty(kv_new.shape, dtype=kv_new.dtype).pin_memory().copy_(kv_new.cpu())
+    dq, dkv = torch.empty_like(q), torch.empty_like(kv_new)
+    h_out = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in step()]
+
+    def e2e(ev):
+        dq.copy_(hq, non_blocking=True)
+        dkv.copy_(hkv, non_blocking=True)
+        for h, d in zip(h_out, step(None, dq, dkv)):
+            h.copy_(d, non_blocking=True)
+
+    barrier()
+    e2e_ms, _ = _timed(torch, e2e, args.steps, stream, inner=False)
+    (e2e_ms,) = _reduce_max(torch, dist, world, device, e2e_ms)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        # one short lane of the workload with its 1 + 4 rows, scaled by query-KV pairs
+        c_dt, c_pairs, c_threads = cpu_lanes_seconds([int(lay.context[1])], [int(lay.new_rows[1])], fp8=True)
+        step_s = c_dt * _query_kv_pairs(lay) / c_pairs
+        cpu = {"value": T / step_s, "unit": "query rows/s", "cores": c_threads, "kind": "port",
+               "sample": f"pack + FP8 append + attention of one lane ({int(lay.context[1])} cached rows, "
+                         f"{int(lay.new_rows[1])} rows, 128 heads), scaled by query-KV pairs"}
     abytes = my_rows * (DK + 4) + T * H * (DK * 2 + 512 * 4 + 4)
     flops = 2 * H * (DK + 512) * sum(int(end[i]) - int(begin[i]) for i in range(L)) * int(lay.new_rows[0])
     bf16_peak = _peaks()[1] / 2.0
@@ -667,8 +732,10 @@ def _run_longctx(args, torch, dist, hk, par, ClockSampler, world, rank, local, d
                                 + ("hk_mla_decode)" if world == 1 else "hk_mla_partial over rank 0's ranges)")),
                      "kernel_ms": attn_ms, "algorithmic_flops": flops, "peak_source": f"{peak_src} bf16 burst",
                      "fp8_kv_gbs": abytes / (attn_ms / 1e3) / 1e9, "fp8_kv_frac_of_hbm": abytes / (attn_ms / 1e3) / 1e9 / hbm_peak},
-        "cpu_baseline": None,
-        "e2e": None,
+        "cpu_baseline": cpu,
+        "e2e": {"value": T * args.steps / (e2e_ms / 1e3), "unit": "query rows/s",
+                "h2d_bytes_per_step": int(q.numel() * 2 + kv_new.numel() * 2),
+                "d2h_bytes_per_step": int(sum(t.numel() * t.element_size() for t in h_out))},
         "gpu_launches": int(launches), "clocks": clocks,
     }
 
@@ -779,13 +846,13 @@ def _run_mixed(args, torch, dist, hk, ClockSampler, world, rank, local, device, 
     out = torch.empty((T, H, DV), dtype=torch.bfloat16, device=device)
     lse = torch.empty((T, H), dtype=torch.float32, device=device)
 
-    def step(ev=None):
+    def step(ev=None, q_in=None, kv_in=None):
         pk = hk.pack(lane_tokens, lane_pos, bt, PAGE, lay.num_pages, T)
-        hk.kv_append_bf16(kv_new, pk["slot_mapping"], cache)
+        hk.kv_append_bf16(kv_new if kv_in is None else kv_in, pk["slot_mapping"], cache)
         if ev is not None:
             ev[0].record(stream)
-        hk.mla_decode(q, cache, bt, pk["cu_seqlens"], pk["positions"], PAGE, max_kv, scale, out=out, lse=lse,
-                      workspace=ws)
+        hk.mla_decode(q if q_in is None else q_in, cache, bt, pk["cu_seqlens"], pk["positions"], PAGE, max_kv,
+                      scale, out=out, lse=lse, workspace=ws)
         if ev is not None:
             ev[1].record(stream)
 
@@ -805,7 +872,32 @@ def _run_mixed(args, torch, dist, hk, ClockSampler, world, rank, local, device, 
     clocks = sampler.summary(t0, t1)
     hk.check_errors()
     ms, attn_ms = _reduce_max(torch, dist, world, device, ms, attn_ms)
-    rows_kv = int(sum(int(c) * int(r) + int(r) * (int(r) + 1) // 2 for c, r in zip(lay.context, lay.new_rows)))
+    # end to end: queries and new latent rows in from pinned host memory, outputs and LSE back
+    hq = torch.empty(q.shape, dtype=q.dtype).pin_memory().copy_(q.cpu())
+    hkv = torch.empty(kv_new.shape, dtype=kv_new.dtype).pin_memory().copy_(kv_new.cpu())
+    dq, dkv = torch.empty_like(q), torch.empty_like(kv_new)
+    ho = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    hl = torch.empty(lse.shape, dtype=lse.dtype).pin_memory()
+
+    def e2e(ev):
+        dq.copy_(hq, non_blocking=True)
+        dkv.copy_(hkv, non_blocking=True)
+        step(None, dq, dkv)
+        ho.copy_(out, non_blocking=True)
+        hl.copy_(lse, non_blocking=True)
+
+    barrier()
+    e2e_ms, _ = _timed(torch, e2e, args.steps, stream, inner=False)
+    (e2e_ms,) = _reduce_max(torch, dist, world, device, e2e_ms)
+    rows_kv = _query_kv_pairs(lay)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        # the first three decode lanes, scaled by query-KV pairs
+        ctx3 = [int(c) for c in lay.context[:3]]
+        c_dt, c_pairs, c_threads = cpu_lanes_seconds(ctx3, [1, 1, 1])
+        cpu = {"value": T / (c_dt * rows_kv / c_pairs), "unit": "tokens/s", "cores": c_threads, "kind": "port",
+               "sample": f"pack + append + attention of three decode lanes ({sum(ctx3)} cached rows, 128 heads), "
+                         "scaled by query-KV pairs"}
     flops = 2 * H * (DK + DV) * rows_kv
     abytes = int(lay.kv_len.sum()) * DK * 2 + T * H * (DK * 2 + DV * 2 + 4)
     bf16_peak = _peaks()[1] / 2.0
@@ -824,7 +916,11 @@ def _run_mixed(args, torch, dist, hk, ClockSampler, world, rank, local, device, 
                      "frac": tflops / bf16_peak, "traffic": None, "kernel": "tcgen05 attention (hk_mla_decode)",
                      "kernel_ms": attn_ms, "algorithmic_flops": flops, "algorithmic_bytes": abytes,
                      "peak_source": f"{peak_src} bf16 burst"},
-        "cpu_baseline": None, "e2e": None, "gpu_launches": int(launches), "clocks": clocks,
+        "cpu_baseline": cpu,
+        "e2e": {"value": T * world * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(q.numel() * 2 + kv_new.numel() * 2),
+                "d2h_bytes_per_step": int(out.numel() * 2 + lse.numel() * 4)},
+        "gpu_launches": int(launches), "clocks": clocks,
     }
 
 
