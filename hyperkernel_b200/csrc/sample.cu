@@ -460,9 +460,9 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(
     mn = fminf(mn, *cl.map_shared_rank(&p_min, q));
     bad |= *cl.map_shared_rank(&p_bad, q);
   }
-  cl.sync();
   if (bad) {
     if (leader && tid == 0) { st->flags = 1; st->argmax = 0; st->token = -1; st->ntop = 0; st->lse = 0.0; }
+    cl.sync();  // every CTA has read the others' partials before any leaves
     return;
   }
   // Replaces this CTA's histograms with the cluster's sums (bins tid, tid + kThreads, ...).
@@ -513,6 +513,7 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(
     });
     const double e_cta = block_sum(e, red);  // its barriers close the histogram
     if (tid == 0) p_e = e_cta;
+    if (leader && tid == 0) list_n = 0;  // the gather below starts after the merge's barriers
     merge_hist(false);  // begins with a cluster barrier, so every p_e is in place
     double e_all = 0.0;
     for (int q = 0; q < C; ++q) e_all += *cl.map_shared_rank(&p_e, q);
@@ -520,8 +521,6 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(
     uint32_t before;
     const int bc = count_cross(hist_c, (uint32_t)c, &before, redu);
     const uint32_t upto = before + hist_c[bc];  // elements in buckets 0..bc
-    if (leader && tid == 0) list_n = 0;
-    cl.sync();  // the p_e reads are done and the leader's list is empty
     if (upto <= (uint32_t)kCap) {
       for_slice([&](int i, float v) {
         if (row.bucket(v) <= bc) list0[atomicAdd(list_n0, 1)] = composite(v, i);
@@ -560,7 +559,6 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(
               [&](int i) { return i0[i]; }, smp, bits);
       }
     }
-    cl.sync();
   }
 
   // ---- top_k == 0: the top-p cut and the draw as running-sum crossings over the whole row
@@ -587,6 +585,7 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(
         atomicAdd(&hist_w[bk], w);
       });
       __syncthreads();
+      if (leader && tid == 0) list_n = 0;  // the first crossing's gather follows the merge's barriers
       merge_hist(true);
       unsigned long long loc = 0;
       for (int q = tid; q < kBuckets; q += kThreads) loc += hist_w[q];
@@ -600,8 +599,7 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(
         const uint32_t cnt = hist_c[bk];
         __syncthreads();
         if (cnt > (uint32_t)kCap) return -1;
-        if (leader && tid == 0) list_n = 0;
-        cl.sync();
+        // the leader's list count is 0 here: reset before a barrier that preceded this call
         for_slice([&](int i, float v) {
           if (row.bucket(v) == bk) list0[atomicAdd(list_n0, 1)] = composite(v, i);
         });
@@ -626,6 +624,7 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(
         cl.sync();
         *incl = *cl.map_shared_rank(&res_incl, 0);
         const int out = *cl.map_shared_rank(&result, 0);
+        if (leader && tid == 0) list_n = 0;  // for the next crossing's gather, after the barrier below
         cl.sync();
         return out;
       };
@@ -660,6 +659,7 @@ __global__ void __launch_bounds__(kThreads) sample_rows_kernel(
     st->ntop = n;
     st->lse = lse;
   }
+  cl.sync();  // no CTA leaves while another may still read its shared memory
 }
 
 // One warp per lane: lane 0 walks the chain, then the warp writes the ids and logprob rows.
