@@ -10,7 +10,6 @@ restatement of the reference's scheduler (src/engine/*.rs) used to pin the C++ e
 from __future__ import annotations
 
 import ctypes as C
-from pathlib import Path
 
 import numpy as np
 

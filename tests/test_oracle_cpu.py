@@ -5,7 +5,6 @@ import math
 from pathlib import Path
 
 import numpy as np
-import pytest
 
 from hyperkernel_b200 import workload as W
 
