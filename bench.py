@@ -119,7 +119,8 @@ def _query_kv_pairs(lay):
 
 def cpu_step_seconds(lay, target_rows: int, reps: int = 1):
     """Times the CPU oracle (pack + append + attention) on a sample; returns
-    (seconds per full step extrapolated by KV rows, sample rows, sample lanes, threads)."""
+    (seconds per full step extrapolated by KV rows, sample rows, sample lanes, threads).
+    Used only to warm the host cores up before whole steps are timed."""
     import oracle
 
     oracle.use_all_cores()
@@ -141,37 +142,76 @@ def cpu_step_seconds(lay, target_rows: int, reps: int = 1):
     return best * full_rows / rows, rows, sub.lanes, oracle.threads()
 
 
+class CpuStep:
+    """The whole configuration-2 step (pack of all 64 lanes, append of their new rows,
+    attention of every lane over its full context, 128 heads) through the CPU restatement on
+    all host cores.  The inputs (2.25 GB of cached rows) are made once; each call times one
+    step."""
+
+    def __init__(self, lay):
+        import oracle
+
+        oracle.use_all_cores()
+        self.lay = lay
+        g = np.random.default_rng(7)
+        T = lay.num_tokens
+        self.q = g.integers(0, 1 << 16, size=(T, HEADS, DK), dtype=np.uint16) & np.uint16(0xBFFF)
+        self.cache = g.integers(0, 1 << 16, size=(lay.num_slots, DK), dtype=np.uint16) & np.uint16(0xBFFF)
+        self.kv_new = g.integers(0, 1 << 16, size=(T, DK), dtype=np.uint16) & np.uint16(0xBFFF)
+
+    def run(self) -> float:
+        import oracle
+
+        lay, T = self.lay, self.lay.num_tokens
+        t0 = time.perf_counter()
+        p = oracle.pack(lay.new_rows, lay.context, lay.block_table, PAGE, lay.num_pages, T)
+        oracle.kv_append_bf16(self.kv_new, p["slot_mapping"][:T], self.cache)
+        oracle.mla_decode(self.q, lay.block_table, p["cu_seqlens"], p["positions"][:T], PAGE,
+                          1.0 / math.sqrt(DK), kv_bf16=self.cache)
+        return time.perf_counter() - t0
+
+    @staticmethod
+    def threads() -> int:
+        import oracle
+
+        return oracle.threads()
+
+
+REF_STEPS_CAP = 3  # whole CPU steps take ~7-12 s each on 16-32 cores: at most this many are timed
+
+
 def run_reference(args):
-    """CPU restatement of the step on all host cores, one bounded sample per step."""
+    """CPU restatement of the step on all host cores: whole configuration-2 steps, no
+    extrapolation.  At most REF_STEPS_CAP steps are timed (the line says how many); the
+    warm-up steps run on the first lanes only (about 200K KV rows each)."""
     world, rank, _ = _dist()
     if rank != 0:
         return 0
     from hyperkernel_b200 import workload as W
 
-    lay = W.config2_layout(seed=0)
+    lay = W.config2_layout(seed=0, lanes=args.lanes, lo=args.ctx_min, hi=args.ctx_max)
     tokens = lay.num_tokens
-    target = 60_000
     for _ in range(args.warmup):
-        cpu_step_seconds(lay, target)
-    secs = []
-    for _ in range(args.steps):
-        s, rows, lanes, threads = cpu_step_seconds(lay, target)
-        secs.append(s)
+        cpu_step_seconds(lay, 200_000)
+    cpu = CpuStep(lay)
+    steps = max(1, min(args.steps, REF_STEPS_CAP))
+    secs = [cpu.run() for _ in range(steps)]
     step_s = float(np.mean(secs))
     value = tokens / step_s
+    threads = CpuStep.threads()
     line = {
         "impl": "reference", "metric": "ragged decode step tokens/s (MLA config 2)",
-        "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16 in, fp64 accumulation",
-        "data": "synthetic (seeded)",
+        "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": steps,
+        "steps_requested": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16 in, fp64 accumulation", "data": "synthetic (seeded)",
         "config": {"workload": "config2: 64 lanes, ctx log-uniform [1K,128K], 128 heads, "
-                               "MLA 512+64, page 64", "lanes": lay.lanes,
-                   "kv_rows": int(lay.kv_len.sum())},
+                               "MLA 512+64, page 64, pack+append+attention",
+                   "lanes_per_gpu": lay.lanes, "kv_rows_per_gpu": int(lay.kv_len.sum()),
+                   "l2": "inputs larger than L2 (~2 GB KV per GPU), no flush", "attn_impl": 0},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
-                         "sample": f"pack+append+attention of the first {lanes} lanes "
-                                   f"({rows} KV rows, 128 heads) per step, scaled by "
-                                   f"{int(lay.kv_len.sum())} / {rows} KV rows"},
+                         "sample": f"{steps} whole steps (all 64 lanes, {int(lay.kv_len.sum())} KV rows, "
+                                   f"128 heads), no extrapolation; warm-up on the first lanes"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -226,6 +266,8 @@ def main(argv=None):
     ap.add_argument("--ctx-min", type=int, default=1024, help="profiling override of config 2")
     ap.add_argument("--ctx-max", type=int, default=131072, help="profiling override of config 2")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host round trip leg")
+    ap.add_argument("--no-legs", action="store_true",
+                    help="skip the expert-parallel (config 4) and context-parallel (config 5) legs")
     ap.add_argument("--workload", default="decode",
                     choices=["decode", "moe", "linear", "longctx", "sample", "mixed", "engine"])
     ap.add_argument("--experts", type=int, default=None, help="profiling override of config 4's 256 experts")
@@ -324,6 +366,17 @@ def main(argv=None):
         e2e_ms = run_e2e(args, step, q, kv_new, lane_tokens, lane_pos, T, stream, barrier, world,
                          device)
     hk.check_errors()
+    legs = {}
+    if not args.no_legs:
+        from hyperkernel_b200 import parallel as par
+
+        # the headline step's buffers go first: the legs hold ~12 GB of expert weights and
+        # ~2.3 GB of FP8 pool and mirror per GPU
+        del step, cache
+        torch.cuda.empty_cache()
+        legs["ep"] = leg_ep(args, torch, dist, hk, par, world, rank, device, stream, barrier, peak_hbm())
+        torch.cuda.empty_cache()
+        legs["cp"] = leg_cp(args, torch, dist, hk, par, world, rank, device, stream, barrier, peak_hbm())
     total_tokens = T * world
     value = total_tokens * args.steps / (ms / 1e3)
     e2e_value = None if args.no_e2e else total_tokens * args.steps / (e2e_ms / 1e3)
@@ -338,10 +391,12 @@ def main(argv=None):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        s, rows, lanes, threads = cpu_step_seconds(lay, 200_000)
-        cpu = {"value": T / s, "unit": "tokens/s", "cores": threads, "kind": "port",
-               "sample": f"pack+append+attention of the first {lanes} lanes ({rows} KV rows, "
-                         f"128 heads), scaled by {int(lay.kv_len.sum())} / {rows} KV rows"}
+        cs = CpuStep(lay)
+        secs = cs.run()
+        cpu = {"value": T / secs, "unit": "tokens/s", "cores": CpuStep.threads(), "kind": "port",
+               "sample": f"one whole step (all {lay.lanes} lanes, {int(lay.kv_len.sum())} KV rows, "
+                         f"128 heads), no extrapolation"}
+        del cs
 
     if rank == 0:
         line = {
@@ -371,12 +426,240 @@ def main(argv=None):
                 "d2h_bytes_per_step": MlaDecodeStep.d2h_bytes(T, HEADS)},
             "gpu_launches": int(launches),
             "clocks": clocks,
+            **legs,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+# ------------------------------------------------------------------------------------------
+# the two shards with a real exchange, run after the headline step on every N
+# ------------------------------------------------------------------------------------------
+
+EP_SEED, CP_SEED = 4242, 555
+
+
+def _bits_equal(torch, a, b) -> bool:
+    return bool(torch.equal(a.contiguous().view(torch.int16), b.contiguous().view(torch.int16)))
+
+
+def _errs_np(got, want):
+    """(normwise, element-wise) max-abs-rel; the element-wise figure divides by each element's
+    own magnitude, floored at 10% of the largest."""
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    top = max(float(np.abs(want).max()), 1e-30)
+    d = np.abs(got - want)
+    return float(d.max() / top), float((d / np.maximum(np.abs(want), 0.1 * top)).max())
+
+
+def leg_ep(args, torch, dist, hk, par, world, rank, device, stream, barrier, hbm_peak):
+    """Config 4's MoE layer, expert parallel over the N GPUs: rank r owns routed experts
+    [r E/N, (r+1) E/N) and its own 512 tokens (weak scaling); dispatch and return are this
+    library's NVLink peer stores (hk_ep_counts / hk_ep_dispatch / hk_ep_return over symmetric
+    buffers), the shared expert is replicated.  Every rank generates the same full weight set
+    (one seed) so that rank 0 can run its tokens through all 256 experts on one GPU: the
+    parity field says whether the EP output equals that one-GPU output bit for bit."""
+    T, E, H, I, K = MOE_T, MOE_E, MOE_H, MOE_I, MOE_K
+    e0, e1 = par.expert_range(E, world, rank)
+    gw = torch.Generator(device=device)
+    gw.manual_seed(EP_SEED)
+    w13 = _rand_e4m3(torch, (E + 1, 2 * I, H), gw, device)  # expert E is the shared expert
+    w2 = _rand_e4m3(torch, (E + 1, H, I), gw, device)
+    s13 = torch.rand((E + 1, 2 * I // 128, H // 128), generator=gw, device=device) * 1e-3
+    s2 = torch.rand((E + 1, H // 128, I // 128), generator=gw, device=device) * 1e-3
+    loc = (w13[e0:e1], s13[e0:e1], w2[e0:e1], s2[e0:e1])
+    shr = (w13[E:], s13[E:], w2[E:], s2[E:])
+    gx = torch.Generator(device=device)
+    gx.manual_seed(EP_SEED + 1 + rank)
+    x = torch.randn((T, H), generator=gx, device=device).to(torch.bfloat16)
+    logits = torch.randn((T, E), generator=gx, device=device)
+    rows = T * K
+    rows_max = rows * world
+    ws = torch.empty(hk.moe_workspace_size(rows_max, H, I), dtype=torch.uint8, device=device)
+    ws_sh = torch.empty(hk.moe_workspace_size(T, H, I), dtype=torch.uint8, device=device)
+    y_buf = torch.empty((rows_max, H), dtype=torch.bfloat16, device=device)
+    y_sh = torch.empty((T, H), dtype=torch.bfloat16, device=device)
+    every = torch.arange(T, dtype=torch.int32, device=device)
+    sh_off = torch.tensor([0, T], dtype=torch.int32, device=device)
+    peer = par.EpPeer(E, T, K, H) if world > 1 else None
+
+    def step(ev=None):
+        xq, sx = hk.quant_fp8(x)
+        ids, w = hk.route(logits, None, K, 1.0)
+        off, tok, pw, inv = hk.permute(ids, w, E)
+        if peer is not None:
+            xr, sr, loff, lperm = peer.dispatch(xq, sx, off, tok)
+        if ev is not None:
+            ev[0].record(stream)
+        if peer is not None:
+            y_loc = hk.moe_grouped(xr, sr, loff, lperm, peer.rows_cap, H, I, *loc, out=y_buf, workspace=ws)
+        else:
+            y_loc = hk.moe_grouped(xq, sx, off, tok, rows, H, I, *loc, out=y_buf, workspace=ws)
+        hk.moe_grouped(xq, sx, sh_off, every, T, H, I, *shr, out=y_sh, workspace=ws_sh)
+        if ev is not None:
+            ev[1].record(stream)
+        y = peer.give_back(y_loc) if peer is not None else y_loc
+        return hk.combine(y, pw, inv, y_sh, T, K), (loff if peer is not None else off)
+
+    for _ in range(args.warmup):
+        out, off = step()
+    torch.cuda.synchronize()
+    hk.check_errors()
+    counts = (off[1:] - off[:-1]).cpu().numpy()
+    hit, rows_in = int((counts > 0).sum()), int(counts.sum())
+    wbytes = (hit + 1) * 3 * H * I + (hit + 1) * (2 * I // 128 * H // 128 + H // 128 * I // 128) * 4
+    abytes = wbytes + (rows_in + T) * (H + 2 * 2 * I + 2 * H)
+    launches0 = hk.kernel_launches()
+    barrier()
+    ms, ffn_ms = _timed(torch, lambda ev: step(ev), args.steps, stream)
+    barrier()
+    launches = hk.kernel_launches() - launches0
+    hk.check_errors()
+    ms, ffn_ms = _reduce_max(torch, dist, world, device, ms, ffn_ms)
+    out, _ = step()  # every rank takes the same exchange steps; rank 0 checks this one
+    torch.cuda.synchronize()
+    parity = None
+    if rank == 0 and world > 1:
+        xq, sx = hk.quant_fp8(x)
+        ids, w = hk.route(logits, None, K, 1.0)
+        off1, tok1, pw1, inv1 = hk.permute(ids, w, E)
+        y1 = hk.moe_grouped(xq, sx, off1, tok1, rows, H, I, w13[:E], s13[:E], w2[:E], s2[:E])
+        ys1 = hk.moe_grouped(xq, sx, sh_off, every, T, H, I, *shr)
+        one = hk.combine(y1, pw1, inv1, ys1, T, K)
+        torch.cuda.synchronize()
+        norm, elem = _errs_np(out.float().cpu().numpy(), one.float().cpu().numpy())
+        parity = {"against": "rank 0's 512 tokens through all 256 routed experts + the shared one on one GPU",
+                  "bit_exact": _bits_equal(torch, out, one), "normwise": norm, "elementwise": elem}
+    barrier()
+    achieved = abytes / (ffn_ms / 1e3) / 1e9
+    return {
+        "workload": "config4 MoE layer: 512 tokens per GPU, 256 routed experts top-8 + 1 shared, hidden 7168, "
+                    "inter 2048, FP8 128x128 block scales; quant+route+permute+dispatch+grouped FFN+return+combine",
+        "parallelism": f"ep{world}" if world > 1 else "single GPU (no exchange)",
+        "exchange": "NVLink peer stores from hk_ep_counts/hk_ep_dispatch/hk_ep_return, bounded epoch waits"
+                    if world > 1 else None,
+        "scaling": "weak", "ms_per_step": ms / args.steps, "tokens_per_s": T * world * args.steps / (ms / 1e3),
+        "routed_rows_per_s": rows * world * args.steps / (ms / 1e3), "experts_per_gpu": e1 - e0,
+        "ffn_ms_rank0_max": ffn_ms, "ffn_hbm_gbs": achieved, "ffn_frac_of_hbm": achieved / hbm_peak,
+        "gpu_launches": int(launches), "parity": parity,
+    }
+
+
+def leg_cp(args, torch, dist, hk, par, world, rank, device, stream, barrier, hbm_peak):
+    """Config 5 (one lane at 1,048,576 cached rows + 7 at U[4K, 64K], 1 + 4 spec-verify rows
+    each, FP8 latent cache), context parallel over the N GPUs: the long lane's KV is cut into
+    page-aligned position ranges, one per rank, the short lanes go round-robin; each rank keeps
+    a bf16 mirror of its pages current and runs one tcgen05 partial launch over its ranges,
+    then the long lane's (o, lse) partials are all-gathered over NCCL and merged by LSE (strong
+    scaling).  Every rank builds the same pool (one seed); rank 0 then runs the whole batch on
+    one GPU and the parity field compares the merged long-lane rows with it (on one GPU the
+    merge is checked by splitting the lane 8 ways on that GPU)."""
+    from hyperkernel_b200 import workload as W
+
+    lay = W.config5_layout(seed=0)
+    T, L, H = lay.num_tokens, lay.lanes, HEADS
+    kv = lay.kv_len.astype(np.int64)
+    begin = np.zeros(L, np.int32)
+    end = np.zeros(L, np.int32)
+    begin[0], end[0] = par.cp_ranges(int(kv[0]), world)[rank]
+    for ln in range(1, L):
+        if (ln - 1) % world == rank:
+            end[ln] = kv[ln]
+    g = torch.Generator(device=device)
+    g.manual_seed(CP_SEED)
+    cache = _rand_e4m3(torch, (lay.num_slots, DK), g, device)
+    scales = torch.rand((lay.num_slots,), generator=g, device=device) * 0.01 + 0.001
+    q = torch.randn((T, H, DK), generator=g, device=device).to(torch.bfloat16)
+    kv_new = torch.randn((T, DK), generator=g, device=device).to(torch.bfloat16)
+    lane_tokens = torch.from_numpy(lay.new_rows.astype(np.int32)).to(device)
+    lane_pos = torch.from_numpy(lay.context.astype(np.int32)).to(device)
+    bt = torch.from_numpy(lay.block_table).to(device)
+    kb, ke = torch.from_numpy(begin).to(device), torch.from_numpy(end).to(device)
+    max_kv = int(kv.max())
+    scale = 1.0 / math.sqrt(DK)
+    long_rows = int(lay.new_rows[0]) * H
+    kv_bf16 = torch.empty((lay.num_slots, DK), dtype=torch.bfloat16, device=device)
+    my_pages = torch.from_numpy(np.concatenate(
+        [lay.block_table[i, int(begin[i]) // PAGE:(int(end[i]) + PAGE - 1) // PAGE] for i in range(L)]
+    ).astype(np.int32)).to(device)
+    hk.kv_dequant_fp8(cache, scales, PAGE, out=kv_bf16, pages=None if world == 1 else my_pages)
+
+    def step(ev=None):
+        pk = hk.pack(lane_tokens, lane_pos, bt, PAGE, lay.num_pages, T)
+        hk.kv_append_fp8(kv_new, pk["slot_mapping"], cache, scales)
+        if ev is not None:
+            ev[0].record(stream)
+        hk.kv_dequant_fp8_rows(cache, scales, pk["slot_mapping"], kv_bf16, PAGE)
+        if world == 1:
+            o, lse = hk.mla_decode(q, kv_bf16, bt, pk["cu_seqlens"], pk["positions"], PAGE, max_kv, scale)
+        else:
+            o, lse = hk.mla_partial(q, kv_bf16, bt, pk["cu_seqlens"], pk["positions"], kb, ke, PAGE, max_kv,
+                                    scale)
+        if ev is not None:
+            ev[1].record(stream)
+        if world > 1:
+            return par.cp_merge(o.view(T * H, 512)[:long_rows], lse.view(T * H)[:long_rows])
+        return o.view(T * H, 512)[:long_rows], lse.view(T * H)[:long_rows]
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    hk.check_errors()
+    launches0 = hk.kernel_launches()
+    barrier()
+    ms, attn_ms = _timed(torch, step, args.steps, stream)
+    barrier()
+    launches = hk.kernel_launches() - launches0
+    hk.check_errors()
+    ms, attn_ms = _reduce_max(torch, dist, world, device, ms, attn_ms)
+    merged, merged_lse = step()
+    torch.cuda.synchronize()
+    parity = None
+    if rank == 0:
+        full = hk.kv_dequant_fp8(cache, scales, PAGE)
+        pk = hk.pack(lane_tokens, lane_pos, bt, PAGE, lay.num_pages, T)
+        whole, whole_lse = hk.mla_decode(q, full, bt, pk["cu_seqlens"], pk["positions"], PAGE, max_kv, scale)
+        whole = whole.view(T * H, 512)[:long_rows]
+        whole_lse = whole_lse.view(T * H)[:long_rows]
+        how = f"merged partials of {world} GPUs"
+        if world == 1:  # the merge on one GPU: the long lane split 8 ways, partials merged by LSE
+            parts, lses = [], []
+            for b0, b1 in par.cp_ranges(int(kv[0]), 8):
+                bb, be = np.zeros(L, np.int32), np.zeros(L, np.int32)
+                bb[0], be[0] = b0, b1
+                o, l = hk.mla_partial(q, full, bt, pk["cu_seqlens"], pk["positions"],
+                                      torch.from_numpy(bb).to(device), torch.from_numpy(be).to(device),
+                                      PAGE, max_kv, scale)
+                parts.append(o.view(T * H, 512)[:long_rows])
+                lses.append(l.view(T * H)[:long_rows])
+            merged, merged_lse = hk.lse_merge(torch.stack(parts).contiguous(), torch.stack(lses).contiguous())
+            how = "8 partials of the long lane on one GPU, merged by LSE"
+        torch.cuda.synchronize()
+        hk.check_errors()
+        norm, elem = _errs_np(merged.float().cpu().numpy(), whole.float().cpu().numpy())
+        lse_err = float((merged_lse - whole_lse).abs().max())
+        parity = {"against": "the whole long lane (5 rows x 128 heads) by hk_mla_decode on one GPU", "merged": how,
+                  "normwise": norm, "elementwise": elem, "lse_max_abs": lse_err, "tolerance": 2e-2,
+                  "ok": bool(norm <= 2e-2 and elem <= 2e-2 and lse_err <= 1e-3)}
+    barrier()
+    my_rows = int(sum(int(end[i]) - int(begin[i]) for i in range(L)))
+    flops = 2 * H * (DK + 512) * my_rows * int(lay.new_rows[0])
+    return {
+        "workload": "config5: 1 lane at 1,048,576 + 7 at U[4K,64K] cached rows, 1+4 rows each, FP8 latent KV, "
+                    "128 heads; pack+FP8 append+mirror rows+tcgen05 attention (+ all-gather and LSE merge of the "
+                    "long lane's partials across GPUs)",
+        "parallelism": f"cp{world}" if world > 1 else "single GPU",
+        "exchange": "NCCL all-gather of the long lane's (o, lse) partials (1.3 MB per rank) + hk_lse_merge"
+                    if world > 1 else None,
+        "scaling": "strong", "ms_per_step": ms / args.steps, "rows_per_s": T * args.steps / (ms / 1e3),
+        "kv_rows_total": int(kv.sum()), "kv_rows_rank0": my_rows if rank == 0 else None,
+        "attn_ms_max": attn_ms, "attn_tflops_rank": flops / (attn_ms / 1e3) / 1e12,
+        "gpu_launches": int(launches), "parity": parity,
+    }
 
 
 # ------------------------------------------------------------------------------------------
@@ -387,6 +670,10 @@ MOE_T, MOE_E, MOE_H, MOE_I, MOE_K = 512, 256, 7168, 2048, 8
 # MLA projections of one layer (DeepSeek-V3 shapes): (name, out features, in features)
 LINEAR_T = 48 + 2 * 2048
 LINEAR_PROJ = [("q_a", 1536, 7168), ("q_b", 128 * 192, 1536), ("kv_a", 576, 7168), ("o", 7168, 128 * 128)]
+
+
+def peak_hbm() -> float:
+    return _peaks()[0]
 
 
 def _peaks():

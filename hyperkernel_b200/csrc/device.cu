@@ -753,6 +753,10 @@ struct hk_handle {
   uint8_t* d_h_stream = nullptr;  // device view of h_stream (mapped)
   int32_t* d_h_out = nullptr;     // device view of h_out (mapped)
   unsigned long long posted = 0;
+  // Set when the executor gave no answer in time: it may still be running the abandoned item
+  // (and publish `done` for it later), so the handle's device state is undefined and every
+  // later hk_push / hk_drain fails with this message.
+  std::string broken;
 };
 
 namespace {
@@ -862,8 +866,11 @@ int ring_run(hk_handle* h, uint32_t kind, uint32_t n_msgs, uint64_t bytes, uint3
     } else if (q != cudaErrorNotReady) {
       return hk::cuda_fail(q, "ring executor");
     }
-    if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > kRingTimeoutS)
-      return hk::fail(HK_EDEVICE, "ring executor gave no answer in %.0f s", kRingTimeoutS);
+    if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > kRingTimeoutS) {
+      const int rc = hk::fail(HK_EDEVICE, "ring executor gave no answer in %.0f s", kRingTimeoutS);
+      h->broken = hk_last_error();
+      return rc;
+    }
     std::this_thread::yield();
   }
   std::atomic_thread_fence(std::memory_order_seq_cst);
@@ -1141,6 +1148,7 @@ int hk_pools(const hk_handle* h, size_t* pages, size_t* window_pages) {
 
 int hk_push(hk_handle* h, const hk_share* share) {
   HK_REQUIRE(h && share, "hk_push: null argument");
+  if (!h->broken.empty()) return handle_fail(h, hk::fail(HK_EDEVICE, "%s", h->broken.c_str()));
   if ((int64_t)share->at != h->horizon + 1)
     return handle_fail(h, hk::fail(HK_ESTATE, "a share at %u past a horizon of %lld", share->at,
                                    (long long)h->horizon));
@@ -1158,6 +1166,7 @@ int hk_push(hk_handle* h, const hk_share* share) {
 int hk_drain(hk_handle* h, hk_event* events, size_t cap, size_t* n, int32_t* ids, size_t ids_cap,
              size_t* ids_n) {
   HK_REQUIRE(h && n && ids_n, "hk_drain: null argument");
+  if (!h->broken.empty()) return handle_fail(h, hk::fail(HK_EDEVICE, "%s", h->broken.c_str()));
   HK_TRY_CUDA(cudaSetDevice(h->cfg.device));
   int rc = run(h);
   if (rc != HK_OK) return handle_fail(h, rc);

@@ -21,7 +21,9 @@
 //
 // Flags are epochs (a step counter the caller increments), so nothing is reset between steps.
 // Every wait is bounded (timeout_us); on a timeout the kernel records the error word and
-// returns, leaving the buffers undefined for that step.
+// returns, leaving the buffers undefined for that step.  A count exchange that timed out marks
+// the step's plan invalid (send_base = -1, local_off[El] = -1): dispatch and return then move no
+// row and raise no flag, so the other ranks' waits run out too and every rank reports the step.
 #include "common.cuh"
 
 namespace {
@@ -85,7 +87,13 @@ __global__ void ep_counts_kernel(const int32_t* __restrict__ offsets, int32_t E,
     if (!ok) hk_flag(err, hk::kErrWaitTimeout, 970);
   }
   __syncthreads();
-  if (!ok) return;
+  if (!ok) {
+    // Mark this step's plan invalid, so hk_ep_dispatch and hk_ep_return skip (and flag) every
+    // row instead of moving rows at stale offsets.
+    for (int e = threadIdx.x; e < E; e += blockDim.x) send_base[e] = -1;
+    for (int el = threadIdx.x; el <= El; el += blockDim.x) local_off[el] = el == El ? -1 : 0;
+    return;
+  }
   const int32_t* cnt = reinterpret_cast<const int32_t*>(counts.p[rank]);  // [world][E], all rows present
   // 3. send_base[e]: destination d = e / El, local el = e % El
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
@@ -120,8 +128,11 @@ __device__ __forceinline__ void copy_row(const uint4* src, uint4* dst, int vecs,
   for (int i = lane; i < svecs; i += 32) sdst[i] = ssrc[i];
 }
 
-// Raises flag word `slot` (+ rank) on every rank once every CTA of the grid is done.
-__device__ void last_cta_signals(uint32_t* done_ctr, Peers flags, int world, int rank, int slot, uint32_t epoch) {
+// Raises flag word `slot` (+ rank) on every rank once every CTA of the grid is done (when
+// `raise` is false the counter is still reset but no flag goes up, so the other ranks' waits
+// run out and report the failed step).
+__device__ void last_cta_signals(uint32_t* done_ctr, Peers flags, int world, int rank, int slot, uint32_t epoch,
+                                 bool raise = true) {
   __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -129,8 +140,9 @@ __device__ void last_cta_signals(uint32_t* done_ctr, Peers flags, int world, int
     if (prev == gridDim.x - 1) {
       *done_ctr = 0;  // ready for the next step (every CTA of this launch has counted)
       __threadfence_system();
-      for (int d = 0; d < world; ++d)
-        store_release_sys(reinterpret_cast<uint32_t*>(flags.p[d]) + slot + rank, epoch);
+      if (raise)
+        for (int d = 0; d < world; ++d)
+          store_release_sys(reinterpret_cast<uint32_t*>(flags.p[d]) + slot + rank, epoch);
     }
   }
 }
@@ -143,6 +155,10 @@ __global__ void ep_dispatch_kernel(const uint8_t* __restrict__ xq, const float* 
                                    unsigned long long* err) {
   const int El = E / world, kb = hidden / 128;
   const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+  // send_base[0] < 0: this step's count exchange failed; move nothing and raise no flag.
+  const bool valid = send_base[0] >= 0;
+  if (!valid && blockIdx.x == 0 && threadIdx.x == 0) hk_flag(err, hk::kErrMoeRow, 0x7ffffffeu);
+  if (!valid) rows = 0;
   for (int p = blockIdx.x * warps + (threadIdx.x >> 5); p < rows; p += gridDim.x * warps) {
     int lo = 0, hi = E;  // expert e with offsets[e] <= p < offsets[e+1]
     while (hi - lo > 1) {
@@ -160,17 +176,22 @@ __global__ void ep_dispatch_kernel(const uint8_t* __restrict__ xq, const float* 
              reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(recv_x.p[d]) + (int64_t)dst * hidden), hidden / 16,
              sx + (int64_t)src * kb, reinterpret_cast<float*>(recv_s.p[d]) + (int64_t)dst * kb, kb, lane);
   }
-  last_cta_signals(done_ctr, flags, world, rank, kFlagDispatch, epoch);
+  last_cta_signals(done_ctr, flags, world, rank, kFlagDispatch, epoch, valid);
 }
 
 __global__ void ep_return_kernel(const uint16_t* __restrict__ y, int32_t E, int32_t world, int32_t rank,
                                  int32_t hidden, const int32_t* __restrict__ local_off,
                                  const int32_t* __restrict__ counts, const int32_t* __restrict__ ret_base,
-                                 int32_t back_cap, Peers back_y, Peers flags, uint32_t* done_ctr, uint32_t epoch,
-                                 unsigned long long* err) {
+                                 int32_t back_cap, int32_t rows_bound, Peers back_y, Peers flags,
+                                 uint32_t* done_ctr, uint32_t epoch, unsigned long long* err) {
   const int El = E / world;
   const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
-  const int rows = local_off[El];
+  // local_off[El] comes from counts the peers wrote: never read y past its rows_bound rows,
+  // and move nothing when this step's count exchange failed (local_off[El] < 0).
+  const int total = local_off[El];
+  const bool valid = total >= 0 && total <= rows_bound;
+  if (!valid && blockIdx.x == 0 && threadIdx.x == 0) hk_flag(err, hk::kErrMoeRow, 0x7fffffffu);
+  const int rows = valid ? total : 0;
   for (int j = blockIdx.x * warps + (threadIdx.x >> 5); j < rows; j += gridDim.x * warps) {
     int lo = 0, hi = El;  // local expert of row j
     while (hi - lo > 1) {
@@ -189,7 +210,7 @@ __global__ void ep_return_kernel(const uint16_t* __restrict__ y, int32_t E, int3
              reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(back_y.p[s]) + (int64_t)pos * hidden),
              hidden * 2 / 16, nullptr, nullptr, 0, lane);
   }
-  last_cta_signals(done_ctr, flags, world, rank, kFlagReturn, epoch);
+  last_cta_signals(done_ctr, flags, world, rank, kFlagReturn, epoch, valid);
 }
 
 __global__ void ep_wait_kernel(const uint32_t* flags, int32_t slot, int32_t world, uint32_t epoch,
@@ -262,8 +283,8 @@ int hk_ep_return(const uint16_t* y, int32_t num_experts, int32_t world, int32_t 
              "hk_ep_return: hidden %d experts %d world %d", hidden, num_experts, world);
   const int grid = std::max(1, std::min(hk::sm_count(), (rows_bound + 7) / 8));
   ep_return_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(y, num_experts, world, rank, hidden, local_off, counts,
-                                                           ret_base, back_cap, b, f, done_ctr, epoch,
-                                                           hk::err_word());
+                                                           ret_base, back_cap, rows_bound, b, f, done_ctr,
+                                                           epoch, hk::err_word());
   HK_TRY_LAUNCH("ep_return_kernel");
   return HK_OK;
 }

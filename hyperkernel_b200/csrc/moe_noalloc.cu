@@ -18,7 +18,8 @@
 // them.  Calls whose executions overlap on the GPU (two streams, or two host threads) race on
 // the array and corrupt each other's results; serialise them.  Rows whose indices are out of
 // range are skipped as in hk_moe_grouped but are not recorded in the device error word
-// (recording would need the error word that the library allocates on first use).
+// (recording would need the error word that the library allocates on first use); offsets that
+// are not a valid scan give an empty tile list, so y is left unwritten, also unreported.
 //
 // The first call on a device looks the array's device address up with cudaGetSymbolAddress
 // (host code cannot use the symbol itself: in host code it names a host-side shadow, not

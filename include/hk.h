@@ -70,7 +70,7 @@ int hk_check_errors(void);
  * seq_lens[num_lanes] = lane_pos + lane_tokens (KV rows after the append, 0 if idle);
  * positions[T], slot_mapping[T] = block_table[lane][pos / page_size] * page_size +
  * pos % page_size, token_lane[T]; active[0] = number of non-idle lanes, active[1..] their
- * lane ids in ascending order.  T = sum(lane_tokens) must be <= max_tokens, else the
+ * lane ids in ascending order (entries after them are not written).  T = sum(lane_tokens) must be <= max_tokens, else the
  * rows past max_tokens are not written and the device error word is set.  A row whose
  * page is 0 (the scratch page) or past num_pages is written with slot -1 and flags the
  * error word.  Bit-exact: integer only. */
@@ -253,7 +253,8 @@ int hk_moe_grouped(const uint8_t* xq, const float* sx, int32_t tokens, const int
  * gathered rows the tensor-core kernels read).  All calls share the array: calls that overlap on the GPU race and must
  * be serialised.  The first call on a device looks the array up (cudaGetSymbolAddress) and
  * should come before any stream capture.  Out-of-range rows are skipped but not recorded in
- * the device error word. */
+ * the device error word; offsets that are not a valid scan (offsets[0] != 0, decreasing, or
+ * offsets[num_experts] > rows) leave y entirely unwritten and are not reported either. */
 int hk_moe_grouped_noalloc(const uint8_t* xq, const float* sx, int32_t tokens,
                            const int32_t* offsets, const int32_t* perm_token, int64_t rows,
                            int32_t num_experts, int32_t hidden, int32_t inter,
@@ -284,7 +285,11 @@ int hk_scatter_rows(const void* src, int64_t rows, const int32_t* idx, int64_t d
  *   hk_ep_dispatch: copies routed row p (xq[perm_token[p]] and its scales) straight into its
  *     owner's receive buffer; raises the dispatch flag on every rank when done.
  *   hk_ep_return: copies received row j of y (expert-major, local_off order) back into its
- *     source's back_y at its permuted position; raises the return flag on every rank.
+ *     source's back_y at its permuted position; raises the return flag on every rank.  y holds
+ *     rows_bound rows: a received total above that (counts a peer wrote for another
+ *     configuration) moves no row, sets the device error word and raises no flag.
+ *   After a count exchange that timed out, dispatch and return move no row and raise no flag
+ *   (the step's plan is marked invalid), so every rank's next wait runs out and reports it.
  *   hk_ep_wait: waits until every rank raised flag set `which` (0 counts, 1 dispatch, 2 return)
  *     in this rank's flags with the epoch.
  * done_ctr: one zeroed device word per launch kind, private to this rank. */
@@ -430,7 +435,10 @@ typedef struct {
  * encoded bytes or a step and waits for the executor's answer, which it writes, with the
  * step's ids and prompt replies, into mapped host memory.  The executor exits after 50 ms
  * without work (every poll is bounded) and is relaunched by the next post; hk_close stops
- * it.  Both transports produce the same events. */
+ * it.  Both transports produce the same events.  An executor that gives no answer within 30 s
+ * fails that call with HK_EDEVICE and leaves the handle failed: every later hk_push / hk_drain
+ * returns HK_EDEVICE with the same message, and hk_close first waits for the executor to
+ * finish the abandoned item and exit (each item and each idle poll is bounded). */
 #define HK_TRANSPORT_LAUNCH 0
 #define HK_TRANSPORT_RING 1
 

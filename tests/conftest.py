@@ -45,3 +45,17 @@ def cuda(hk):
     assert major == 10, f"sm_{major}{minor}: these kernels are built for sm_100a"
     torch.cuda.set_device(0)
     return torch.device("cuda", 0)
+
+
+def pytest_sessionfinish(session, exitstatus):
+    """With HK_ERR_REPORT set, writes the normwise and element-wise max-abs-rel figures of
+    every floating-point comparison the GPU kernel tests made (JSON lines)."""
+    path = os.environ.get("HK_ERR_REPORT")
+    mod = sys.modules.get("test_kernels_gpu") or sys.modules.get("tests.test_kernels_gpu")
+    if not path or mod is None:
+        return
+    import json
+
+    with open(path, "w") as f:
+        for test, norm, elem in getattr(mod, "ERRS", []):
+            f.write(json.dumps({"test": test, "normwise": norm, "elementwise": elem}) + "\n")

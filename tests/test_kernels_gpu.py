@@ -1,10 +1,18 @@
 """GPU parity of every kernel behind include/hk.h against the CPU oracle.
 
 Integer work (pack, slot mapping, appends, route ids, permutation) must be bit-exact;
-floating point is compared as max|gpu - oracle| / max|oracle| (normwise max-abs-rel):
-  - GQA fp32 attention (config 1): absolute 1e-5;
-  - bf16 / e4m3 attention, FP8 GEMM, MoE: max-abs-rel <= 2e-2 against the fp64-accumulated
-    oracle on the same bf16 / e4m3 inputs.
+floating point is compared two ways, and both must hold:
+  - normwise max-abs-rel, max|gpu - oracle| / max|oracle|: <= 2e-2 for bf16 / e4m3 attention,
+    FP8 GEMM and MoE against the fp64-accumulated oracle on the same bf16 / e4m3 inputs (the
+    tolerance BASELINE's north star states); GQA fp32 attention (config 1) 1e-5 absolute;
+  - element-wise max-abs-rel, max over elements of |gpu - oracle| / max(|oracle|, floor) with
+    floor = 10% of max|oracle| (every element at least a tenth of the largest within the bound
+    of its own magnitude, smaller ones within the bound of that tenth): <= 5e-2.  The tensor-core
+    attention rounds the softmax weights to bf16 for the P.V product (2^-9 relative per weight),
+    and the FP8 -> bf16 mirror rounds each dequantised K/V value once more, which puts its
+    element-wise figure at 1-3e-2 while the normwise one stays at 2-4e-3.
+Both figures of every comparison are collected and written out when HK_ERR_REPORT names a
+file.
 """
 import math
 
@@ -19,10 +27,29 @@ pytestmark = pytest.mark.gpu
 TOL = 2e-2
 
 
-def rel_err(got, want):
+ELEM_FLOOR = 0.1  # element-wise figure: magnitudes below 10% of the largest count as that 10%
+ELEM_TOL = 5e-2
+ERRS = []  # (test, normwise, element-wise) of every comparison, for HK_ERR_REPORT
+
+
+def errs(got, want):
+    """(normwise, element-wise) max-abs-rel of got against want."""
     got = np.asarray(got, np.float64)
     want = np.asarray(want, np.float64)
-    return float(np.abs(got - want).max() / max(np.abs(want).max(), 1e-30))
+    top = max(float(np.abs(want).max()), 1e-30)
+    d = np.abs(got - want)
+    return float(d.max() / top), float((d / np.maximum(np.abs(want), ELEM_FLOOR * top)).max())
+
+
+def rel_err(got, want):
+    """The normwise max-abs-rel (the caller holds it to its tolerance); the element-wise figure
+    is checked here against ELEM_TOL, and both are recorded."""
+    import os
+
+    norm, elem = errs(got, want)
+    ERRS.append((os.environ.get("PYTEST_CURRENT_TEST", "?").split(" ")[0], norm, elem))
+    assert elem <= ELEM_TOL, f"element-wise max-abs-rel {elem:.3e} > {ELEM_TOL} (normwise {norm:.3e})"
+    return norm
 
 
 def dev(a, cuda):
@@ -60,8 +87,10 @@ def test_pack_matches_oracle_bit_exact(hk, orc, cuda):
     got = hk.pack(dev(lay.new_rows.astype(np.int32), cuda), dev(lay.context.astype(np.int32), cuda),
                   dev(lay.block_table, cuda), 64, lay.num_pages, T + 3)
     hk.check_errors()
-    for k in ("cu_seqlens", "seq_lens", "active"):
+    for k in ("cu_seqlens", "seq_lens"):
         assert np.array_equal(got[k].cpu().numpy(), want[k]), k
+    n = int(want["active"][0])  # active[0] lanes, their ids after it; entries past them are unspecified
+    assert np.array_equal(got["active"].cpu().numpy()[:n + 1], want["active"][:n + 1])
     for k in ("positions", "slot_mapping", "token_lane"):
         assert np.array_equal(got[k].cpu().numpy()[:T], want[k][:T]), k
 
@@ -257,25 +286,41 @@ def test_mla_tcgen05_spec_verify_rows(hk, orc, cuda):
     assert np.abs(lse - want_lse).max() <= 1e-3
 
 
-def test_mla_tcgen05_matches_portable_at_config2_scale(hk, cuda):
-    """Full configuration-2 batch (64 lanes, ~1.95 M cached rows): the tcgen05 kernel and the
-    portable kernel agree (the CPU oracle is too slow at this size)."""
+def test_mla_tcgen05_config2_full_scale_matches_oracle_on_sampled_lanes_and_heads(hk, orc, cuda):
+    """The full configuration-2 batch (64 lanes, contexts log-uniform in [1K, 128K], ~1.95 M
+    cached rows scattered over a permuted page pool) through pack, append and the tcgen05
+    kernel, every lane split over SM pairs and merged by LSE; the CPU oracle computes 6 lanes
+    (the longest, the shortest and 4 more) for 4 heads each (a lane's rows depend only on its
+    own pages and a head only on its own query)."""
     lay = W.config2_layout(seed=0)
     T = lay.num_tokens
     g = torch.Generator(device=cuda)
     g.manual_seed(5)
     cache = torch.randn((lay.num_slots, 576), generator=g, device=cuda).to(torch.bfloat16)
     q = torch.randn((T, 128, 576), generator=g, device=cuda).to(torch.bfloat16)
+    new = torch.randn((T, 576), generator=g, device=cuda).to(torch.bfloat16)
+    cache_host = cache.view(torch.int16).cpu().numpy().view(np.uint16)
     pk = hk.pack(dev(lay.new_rows.astype(np.int32), cuda), dev(lay.context.astype(np.int32), cuda),
                  dev(lay.block_table, cuda), 64, lay.num_pages, T)
-    bt = dev(lay.block_table, cuda)
-    args = (q, cache, bt, pk["cu_seqlens"], pk["positions"], 64, int(lay.kv_len.max()), 1 / 24.0)
-    o1, l1 = hk.mla_decode(*args, impl=1)
-    o2, l2 = hk.mla_decode(*args, impl=2)
+    hk.kv_append_bf16(new, pk["slot_mapping"], cache)
+    scale = 1 / 24.0
+    out, lse = hk.mla_decode(q, cache, dev(lay.block_table, cuda), pk["cu_seqlens"], pk["positions"], 64,
+                             int(lay.kv_len.max()), scale, impl=2)
     hk.check_errors()
-    a, b = o1.float().cpu().numpy(), o2.float().cpu().numpy()
-    assert rel_err(b, a) <= TOL
-    assert np.abs(l1.cpu().numpy() - l2.cpu().numpy()).max() <= 1e-3
+    p = orc.pack(lay.new_rows, lay.context, lay.block_table, 64, lay.num_pages, T)
+    assert np.array_equal(pk["slot_mapping"].cpu().numpy()[:T], p["slot_mapping"][:T])
+    orc.kv_append_bf16(new.view(torch.int16).cpu().numpy().view(np.uint16), p["slot_mapping"][:T], cache_host)
+    order = np.argsort(lay.kv_len)
+    lanes = np.unique(np.concatenate([[order[-1], order[0]], W.Rng(9).permutation(64)[:4]]))
+    heads = np.array([0, 37, 90, 127])
+    rows = np.concatenate([np.arange(p["cu_seqlens"][b], p["cu_seqlens"][b + 1]) for b in lanes])
+    cu = np.concatenate([[0], np.cumsum(lay.new_rows[lanes])]).astype(np.int32)
+    q_rows = q.view(torch.int16).cpu().numpy().view(np.uint16)[rows][:, heads]
+    want, want_lse = orc.mla_decode(np.ascontiguousarray(q_rows), np.ascontiguousarray(lay.block_table[lanes]),
+                                    cu, p["positions"][rows], 64, scale, kv_bf16=cache_host)
+    got = to_np_bf16(out)[rows][:, heads]
+    assert rel_err(got, want) <= TOL
+    assert np.abs(lse.cpu().numpy()[rows][:, heads] - want_lse).max() <= 1e-3
 
 
 def test_mla_fp8_spec_verify_matches_oracle(hk, orc, cuda):
@@ -435,9 +480,10 @@ def test_moe_layer_matches_oracle(hk, orc, cuda, T, E, H, I, K):
 
 
 def test_moe_layer_full_size_matches_oracle_on_sampled_tokens(hk, orc, cuda):
-    """Config 4 at full size (512 tokens, 256 routed experts, top 8, hidden 7168, inter 2048:
-    11.3 GB of e4m3 weights, so every expert is hit): the whole layer on the GPU; the oracle
-    for six sampled tokens from the experts they route to (quantisation, routing and the h
+    """Config 4 at full size (512 tokens, 256 routed experts + 1 shared, top 8, hidden 7168,
+    inter 2048: 11.3 GB of e4m3 weights, so every expert is hit): the whole layer on the GPU,
+    the shared expert over every token added in the combine; the oracle for six sampled tokens
+    from the experts they route to and the shared expert (quantisation, routing and the h
     requantisation are per token, so a token's output depends on nothing else)."""
     T, E, H, I, K = 512, 256, 7168, 2048, 8
     g = torch.Generator(device=cuda).manual_seed(61)
@@ -446,16 +492,19 @@ def test_moe_layer_full_size_matches_oracle_on_sampled_tokens(hk, orc, cuda):
         b = torch.randint(0, 256, shape, generator=g, device=cuda, dtype=torch.uint8)
         return torch.where((b & 0x7F) == 0x7F, b ^ 1, b)
 
-    w13, w2 = e4m3((E, 2 * I, H)), e4m3((E, H, I))
-    s13 = torch.rand((E, 2 * I // 128, H // 128), generator=g, device=cuda) * 4e-5 + 2e-5
-    s2 = torch.rand((E, H // 128, I // 128), generator=g, device=cuda) * 4e-5 + 2e-5
+    w13, w2 = e4m3((E + 1, 2 * I, H)), e4m3((E + 1, H, I))  # expert E is the shared expert
+    s13 = torch.rand((E + 1, 2 * I // 128, H // 128), generator=g, device=cuda) * 4e-5 + 2e-5
+    s2 = torch.rand((E + 1, H // 128, I // 128), generator=g, device=cuda) * 4e-5 + 2e-5
     logits = torch.randn((T, E), generator=g, device=cuda)
     x = torch.randn((T, H), generator=g, device=cuda).to(torch.bfloat16)
     gi, gw = hk.route(logits, None, K, 1.0)
     goff, gtok, gpw, ginv = hk.permute(gi, gw, E)
     gxq, gsx = hk.quant_fp8(x)
-    gy = hk.moe_grouped(gxq, gsx, goff, gtok, T * K, H, I, w13, s13, w2, s2)
-    out = hk.combine(gy, gpw, ginv, None, T, K)
+    gy = hk.moe_grouped(gxq, gsx, goff, gtok, T * K, H, I, w13[:E], s13[:E], w2[:E], s2[:E])
+    every = torch.arange(T, dtype=torch.int32, device=cuda)
+    shared_off = torch.tensor([0, T], dtype=torch.int32, device=cuda)
+    gys = hk.moe_grouped(gxq, gsx, shared_off, every, T, H, I, w13[E:], s13[E:], w2[E:], s2[E:])
+    out = hk.combine(gy, gpw, ginv, gys, T, K)
     hk.check_errors()
     assert (goff.cpu().numpy()[1:] > goff.cpu().numpy()[:-1]).all(), "an expert without rows"
 
@@ -468,7 +517,11 @@ def test_moe_layer_full_size_matches_oracle_on_sampled_tokens(hk, orc, cuda):
     off, tok, pw, inv = orc.permute(cid.reshape(ids.shape).astype(np.int32), w, len(used))
     xq, sx = orc.quant_fp8(x.view(torch.int16).cpu().numpy().view(np.uint16)[S])
     y = orc.moe_grouped(xq, sx, off, tok, H, I, *host)
-    want = orc.combine(W.f32_to_bf16_bits(y), pw, inv, None, len(S), K)
+    shared_host = [t[E:].cpu().numpy() for t in (w13, s13, w2, s2)]
+    ys = orc.moe_grouped(xq, sx, np.array([0, len(S)], np.int32), np.arange(len(S), dtype=np.int32), H, I,
+                         *shared_host)
+    want = orc.combine(W.f32_to_bf16_bits(y), pw, inv, W.f32_to_bf16_bits(ys), len(S), K)
+    assert rel_err(to_np_bf16(gys)[S], ys) <= TOL
     assert rel_err(to_np_bf16(out)[S], want) <= TOL
 
 
@@ -746,6 +799,22 @@ def test_sample_verify_at_the_largest_vocabulary(hk, cuda):
     got = lp.cpu().numpy()
     assert np.array_equal(got[..., 0:-1:2], want_lp[..., 0:-1:2])
     assert np.abs(got - want_lp).max() <= 1e-5
+
+
+def test_sample_verify_non_finite_greedy_rows_give_minus_one(hk, cuda):
+    """The reference's greedy rows (src/evo2/draw.rs:65-71): [0, 3, 3, -1] gives the first
+    greatest (1); [NaN, inf, 2.0], which the evo2 sampler cleans to index 2, gives -1 here, the
+    boundary's id for non-finite logits; neither draw touches the generator state."""
+    logits = np.array([[0.0, 3.0, 3.0, -1.0], [np.nan, np.inf, 2.0, 0.0], [np.inf, 1.0, 0.0, 0.0]],
+                      np.float32)
+    cu = np.array([0, 1, 2, 3], np.int32)
+    greedy = dict(temperature=1.0, top_k=1, top_p=0.0)
+    st = torch.tensor([5, 6, 7], dtype=torch.int64, device=cuda)
+    ids, _ = hk.sample_verify(dev(logits, cuda), dev(cu, cuda), hk.sampling_array([greedy] * 3, cuda), st,
+                              dev(np.zeros((3, 0), np.int32), cuda), 1, 0)
+    hk.check_errors()
+    assert ids.cpu().numpy().tolist() == [[1], [-1], [-1]]
+    assert st.cpu().numpy().tolist() == [5, 6, 7]
 
 
 def test_mla_tcgen05_prefill_chunk_with_decode_lanes(hk, orc, cuda):

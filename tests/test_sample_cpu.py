@@ -93,3 +93,18 @@ def test_chain_accepts_drafts_until_the_first_mismatch_and_stops_at_non_finite_r
     assert ids.tolist() == [[3, 5, 7], [1, -2, -2], [2, 11, -1]]
     assert st == [1, 2, 3]
     assert lp[0, 0, 0] == 3 and lp[1, 1].tolist() == [0.0] * 5
+
+
+def test_greedy_past_a_nan_or_an_infinity_is_the_non_finite_rule():
+    """The reference's greedy test (src/evo2/draw.rs:65-71) draws index 2 from
+    [NaN, inf, 2.0]: the evo2 sampler cleans non-finite logits to 0.  At the decode step's
+    boundary a negative id means non-finite logits (src/gpu/mod.rs:13-40, the Sampled id the
+    engine reads as "the logits were not finite"), so this build answers -1 for that row and
+    leaves the generator state alone; the finite half of the same test is kept as it is."""
+    row = np.array([np.nan, np.inf, 2.0], np.float32)
+    greedy = dict(temperature=1.0, top_k=1, top_p=0.0)
+    ids, lp, st = S.sample_verify(row[None, :], np.array([0, 1]), [greedy], [0], np.zeros((1, 0), np.int32), 1, 0)
+    assert ids.tolist() == [[-1]] and st == [0]
+    ids, _, st = S.sample_verify(np.array([[0.0, 3.0, 3.0, -1.0]], np.float32), np.array([0, 1]), [greedy], [0],
+                                 np.zeros((1, 0), np.int32), 1, 0)
+    assert ids.tolist() == [[1]] and st == [0]

@@ -7,12 +7,11 @@ its scratch is a fixed device array inside the library.  This file is collected 
 that stops at the first failure has run every other test first; it also passes on its own in a
 fresh process.
 """
-import ctypes as C
-
 import numpy as np
 import pytest
 import torch
 
+import oracle
 from hyperkernel_b200 import workload as W
 
 pytestmark = pytest.mark.gpu
@@ -28,8 +27,13 @@ def _problem(hk, cuda, tokens, experts, hidden, inter, top_k, seed):
     offsets, perm_token, _, _ = hk.permute(ids, w, experts)
     xq, sx = hk.quant_fp8(x)
     weights = dict(w13=dev(inp["w13"]), s13=dev(inp["s13"]), w2=dev(inp["w2"]), s2=dev(inp["s2"]))
+    # the CPU oracle's expert outputs over the same routed rows (the route, permutation and
+    # quantisation are bit-exact against the oracle, so the oracle can take the GPU's copies)
+    want = oracle.moe_grouped(xq.cpu().numpy(), sx.cpu().numpy(), offsets.cpu().numpy(),
+                              perm_token.cpu().numpy(), hidden, inter, inp["w13"], inp["s13"],
+                              inp["w2"], inp["s2"])
     return dict(xq=xq, sx=sx, offsets=offsets, perm_token=perm_token, rows=tokens * top_k,
-                hidden=hidden, inter=inter, **weights)
+                hidden=hidden, inter=inter, oracle=want, **weights)
 
 
 def _call_noalloc(hk, p):
@@ -45,23 +49,30 @@ def _call_noalloc(hk, p):
     return out
 
 
+def _f32(a):
+    if isinstance(a, torch.Tensor):
+        return a.float().cpu().numpy().astype(np.float64)
+    return np.asarray(a, np.float64)
+
+
 def _rel_err(a, b):
-    a = a.float().cpu().numpy()
-    b = b.float().cpu().numpy()
+    a, b = _f32(a), _f32(b)
     return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
 
 
 def test_noalloc_matches_workspace_entry_point_twice(hk, cuda):
-    """Two calls in a row (different problems, sharing the one scratch array) each agree with
-    hk_moe_grouped given a caller workspace."""
-    problems = [_problem(hk, cuda, 96, 8, 256, 256, 2, seed=61),
-                _problem(hk, cuda, 128, 16, 384, 512, 4, seed=62)]
+    """Two calls in a row share the one scratch array: the larger problem first, then a smaller
+    one that leaves the first call's rows, h and tile list behind in the array.  Each result
+    agrees with hk_moe_grouped given a caller workspace and with the CPU oracle."""
+    problems = [_problem(hk, cuda, 128, 16, 384, 512, 4, seed=62),
+                _problem(hk, cuda, 96, 8, 256, 256, 2, seed=61)]
     for p in problems:
         want = hk.moe_grouped(p["xq"], p["sx"], p["offsets"], p["perm_token"], p["rows"],
                               p["hidden"], p["inter"], p["w13"], p["s13"], p["w2"], p["s2"])
         got = _call_noalloc(hk, p)
         torch.cuda.synchronize()
         assert _rel_err(got, want[: p["rows"]]) <= TOL
+        assert _rel_err(got, p["oracle"]) <= TOL
     hk.check_errors()
 
 
