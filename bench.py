@@ -275,6 +275,8 @@ def main(argv=None):
                     help="longctx: convert the whole FP8 pool to bf16 every step (no mirror)")
     ap.add_argument("--ep", default="peer", choices=["peer", "nccl"],
                     help="expert-parallel exchange: NVLink stores from libhk kernels, or NCCL all-to-allv")
+    ap.add_argument("--cp", default="peer", choices=["peer", "nccl"],
+                    help="context-parallel exchange: hk_cp_merge over peer memory, or NCCL all-gather + merge")
     args = ap.parse_args(argv)
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -535,6 +537,8 @@ def leg_ep(args, torch, dist, hk, par, world, rank, device, stream, barrier, hbm
         parity = {"against": "rank 0's 512 tokens through all 256 routed experts + the shared one on one GPU",
                   "bit_exact": _bits_equal(torch, out, one), "normwise": norm, "elementwise": elem}
     barrier()
+    if peer is not None:
+        peer.close()
     achieved = abytes / (ffn_ms / 1e3) / 1e9
     return {
         "workload": "config4 MoE layer: 512 tokens per GPU, 256 routed experts top-8 + 1 shared, hidden 7168, "
@@ -587,6 +591,9 @@ def leg_cp(args, torch, dist, hk, par, world, rank, device, stream, barrier, hbm
         [lay.block_table[i, int(begin[i]) // PAGE:(int(end[i]) + PAGE - 1) // PAGE] for i in range(L)]
     ).astype(np.int32)).to(device)
     hk.kv_dequant_fp8(cache, scales, PAGE, out=kv_bf16, pages=None if world == 1 else my_pages)
+    # the exchange: this library's fused peer-memory merge (hk_cp_merge over hk_sym_alloc buffers),
+    # or --cp nccl: an NCCL all-gather of the partials, then hk_lse_merge
+    peer = par.CpPeer(T * H, 512, long_rows) if world > 1 and args.cp == "peer" else None
 
     def step(ev=None):
         pk = hk.pack(lane_tokens, lane_pos, bt, PAGE, lay.num_pages, T)
@@ -596,11 +603,17 @@ def leg_cp(args, torch, dist, hk, par, world, rank, device, stream, barrier, hbm
         hk.kv_dequant_fp8_rows(cache, scales, pk["slot_mapping"], kv_bf16, PAGE)
         if world == 1:
             o, lse = hk.mla_decode(q, kv_bf16, bt, pk["cu_seqlens"], pk["positions"], PAGE, max_kv, scale)
+        elif peer is not None:
+            ob, lb = peer.next_buffers()
+            o, lse = hk.mla_partial(q, kv_bf16, bt, pk["cu_seqlens"], pk["positions"], kb, ke, PAGE, max_kv,
+                                    scale, out=ob.view(T, H, 512), lse=lb.view(T, H))
         else:
             o, lse = hk.mla_partial(q, kv_bf16, bt, pk["cu_seqlens"], pk["positions"], kb, ke, PAGE, max_kv,
                                     scale)
         if ev is not None:
             ev[1].record(stream)
+        if peer is not None:
+            return peer.merge()
         if world > 1:
             return par.cp_merge(o.view(T * H, 512)[:long_rows], lse.view(T * H)[:long_rows])
         return o.view(T * H, 512)[:long_rows], lse.view(T * H)[:long_rows]
@@ -646,6 +659,8 @@ def leg_cp(args, torch, dist, hk, par, world, rank, device, stream, barrier, hbm
                   "normwise": norm, "elementwise": elem, "lse_max_abs": lse_err, "tolerance": 2e-2,
                   "ok": bool(norm <= 2e-2 and elem <= 2e-2 and lse_err <= 1e-3)}
     barrier()
+    if peer is not None:
+        peer.close()
     my_rows = int(sum(int(end[i]) - int(begin[i]) for i in range(L)))
     flops = 2 * H * (DK + 512) * my_rows * int(lay.new_rows[0])
     return {
@@ -653,7 +668,10 @@ def leg_cp(args, torch, dist, hk, par, world, rank, device, stream, barrier, hbm
                     "128 heads; pack+FP8 append+mirror rows+tcgen05 attention (+ all-gather and LSE merge of the "
                     "long lane's partials across GPUs)",
         "parallelism": f"cp{world}" if world > 1 else "single GPU",
-        "exchange": "NCCL all-gather of the long lane's (o, lse) partials (1.3 MB per rank) + hk_lse_merge"
+        "exchange": (("hk_cp_merge: every rank's long-lane (o, lse) partial (1.3 MB) read over NVLink from its "
+                      "hk_sym_alloc buffer and merged by LSE in one kernel, bounded epoch waits")
+                     if args.cp == "peer" else
+                     "NCCL all-gather of the long lane's (o, lse) partials (1.3 MB per rank) + hk_lse_merge")
                     if world > 1 else None,
         "scaling": "strong", "ms_per_step": ms / args.steps, "rows_per_s": T * args.steps / (ms / 1e3),
         "kv_rows_total": int(kv.sum()), "kv_rows_rank0": my_rows if rank == 0 else None,
@@ -1295,137 +1313,128 @@ def _run_sample(args, torch, dist, hk, ClockSampler, world, rank, local, device,
     }
 
 
-ENGINE_LANES, ENGINE_PAGE_ROWS, ENGINE_ENTRIES, ENGINE_CHUNK, ENGINE_BLOCK = 64, 64, 64, 512, 5
-ENGINE_REQUESTS, ENGINE_LIMIT, ENGINE_PROMPT = 256, 128, (64, 1024)
+# The decode step behind the Kernel boundary (HK_MODEL_MLA): one DeepSeek-V3-shaped layer.
+ENGINE_LANES, ENGINE_PAGE_ROWS, ENGINE_CHUNK, ENGINE_BLOCK = 64, 64, 512, 1
+ENGINE_REQUESTS, ENGINE_LIMIT, ENGINE_PROMPT = 128, 64, (64, 1024)
+ENGINE_ENTRIES = (ENGINE_PROMPT[1] + ENGINE_LIMIT + ENGINE_PAGE_ROWS - 1) // ENGINE_PAGE_ROWS + 1
+ENGINE_DIMS = dict(hidden=7168, q_lora=1536, vocab=129280, experts=256, top_k=8, inter=2048, layers=1,
+                   logprobs=20, seed=1234, rope_theta=10000.0, route_scale=2.5)
 
 
-def _engine_requests(n, seed):
-    """Seeded prompts of U[64, 1024] tokens from the test model's vocabulary (10..409)."""
+def _engine_requests(n, seed, vocab=ENGINE_DIMS["vocab"]):
+    """Seeded prompts of U[64, 1024) token ids over the model's vocabulary."""
     rng = np.random.default_rng(seed)
-    return [(rng.integers(10, 410, int(rng.integers(*ENGINE_PROMPT))).tolist(), ENGINE_LIMIT) for _ in range(n)]
+    return [(rng.integers(0, vocab, int(rng.integers(*ENGINE_PROMPT))).tolist(), ENGINE_LIMIT) for _ in range(n)]
 
 
-def _engine_session(H, transport, device_index, requests):
-    """One session of the engine over the device kernel: every request submitted, the jobs
-    closed, hk_engine_run to the end.  Returns (seconds, iterations with tokens, tokens
-    generated, kernel launches since the device was opened: with the ring transport, the
-    resident executor launched by hk_open runs every item of the timed run)."""
-    from hyperkernel_b200 import _lib as hk
-
+def _engine_device(H, device_index, dims):
     context = ENGINE_PAGE_ROWS * ENGINE_ENTRIES
     pages = ENGINE_LANES * ENGINE_ENTRIES + 1
-    cfg = H.Config(model=H.MODEL_FNV, page_rows=ENGINE_PAGE_ROWS, entries=ENGINE_ENTRIES, window=ENGINE_ENTRIES,
+    cfg = H.Config(model=H.MODEL_MLA, page_rows=ENGINE_PAGE_ROWS, entries=ENGINE_ENTRIES, window=ENGINE_ENTRIES,
                    width=ENGINE_LANES, context=context, chunk=ENGINE_CHUNK, block=ENGINE_BLOCK, pages=pages,
-                   window_pages=pages, clip=0, device=device_index, transport=transport)
-    l0 = hk.kernel_launches()
-    dev = H.Device(cfg)
-    try:
-        eng = H.Engine(H.engine_config(page_rows=ENGINE_PAGE_ROWS, entries=ENGINE_ENTRIES, window=ENGINE_ENTRIES,
-                                       window_keep=0, context=context, width=ENGINE_LANES, chunk=ENGINE_CHUNK,
-                                       block=ENGINE_BLOCK, pad=7, budget=None, every=1, headroom=2048),
-                       dev.ops(), keep=dev)
-        reqs = [eng.submit(pr, lim) for pr, lim in requests]
-        eng.close()
-        t0 = time.perf_counter()
-        rc = eng.run()
-        dt = time.perf_counter() - t0
-        launches = hk.kernel_launches() - l0
-        if rc != 0:
-            raise RuntimeError(f"engine run failed: {eng.failure}")
-        _m, _acc, counts, _total = eng.metrics()
-        tokens = sum(len(eng.heard(r).tokens) for r in reqs)
-    finally:
-        dev.close()
-    return dt, int(sum(counts)), tokens, launches
+                   window_pages=pages, clip=0, device=device_index, transport=0)
+    return H.Device(cfg, H.MlaModel(**dims))
 
 
-def _run_engine(args, torch, dist, hk, ClockSampler, world, rank, local, device, barrier, hbm_peak, peak_src):
-    """Rows a1-a6 and a16 through the boundary: the C++ engine (admission with the prefix tree,
-    block-table deltas, prompt chunking, pacing, spec-verify accounting) driving the device
-    kernel behind hk_kernel_ops, over the resident-ring transport, with the reference's test
-    model on the GPU (its next token is a fold over the sequence read back through the paged
-    pools).  256 requests, prompts U[64, 1024], 128 tokens each, 64 lanes, 1 + 4 draft rows.
-    The loop is host-driven, so it is timed by the host clock around hk_engine_run, and the
-    number is end to end by construction (commands in, ids out through mapped host memory).
-    N > 1: independent replicas."""
+def _engine_session(H, dev, requests, logprobs):
+    """One session of the C++ engine over the device: every request submitted (greedy, with
+    `logprobs` pairs per token), the jobs closed, hk_engine_run to the end.  Returns (seconds,
+    engine iterations with tokens, generated tokens, prompt tokens)."""
+    context = ENGINE_PAGE_ROWS * ENGINE_ENTRIES
+    eng = H.Engine(H.engine_config(page_rows=ENGINE_PAGE_ROWS, entries=ENGINE_ENTRIES, window=ENGINE_ENTRIES,
+                                   window_keep=0, context=context, width=ENGINE_LANES, chunk=ENGINE_CHUNK,
+                                   block=ENGINE_BLOCK, pad=0, budget=None, every=1, headroom=2048),
+                   dev.ops(), keep=dev)
+    samp = H.Sampling(0.0, 1.0, 0, logprobs, 0)
+    reqs = [eng.submit(pr, lim, sampling=samp) for pr, lim in requests]
+    eng.close()
+    t0 = time.perf_counter()
+    rc = eng.run()
+    dt = time.perf_counter() - t0
+    if rc != 0:
+        raise RuntimeError(f"engine run failed: {eng.failure}")
+    m, _acc, counts, _total = eng.metrics()
+    tokens = sum(len(eng.heard(r).tokens) for r in reqs)
+    return dt, int(sum(counts)), tokens, int(m["prompt_tokens"])
+
+
+def leg_engine(args, torch, dist, hk, world, rank, local, device, barrier, hbm_peak):
+    """The whole decode step behind the reference's Kernel boundary: the C++ engine (admission,
+    prefix cache, block tables, prompt chunking, pacing) driving an HK_MODEL_MLA device through
+    hk_kernel_ops -- hk_push / hk_drain with host arrays in and sampled ids and logprob rows out
+    -- each step packing the live lanes, embedding, one DeepSeek-V3-shaped layer (FP8 q_a / q_b /
+    kv_a projections, RoPE, KV append, tcgen05 MLA attention over the paged latent cache, FP8 o
+    projection, sigmoid top-8 routing over 256 experts + the shared one, grouped FP8 expert FFN,
+    combine), the FP8 vocabulary projection and on-device sampling.  128 requests, prompts
+    U[64, 1024), 64 tokens each, 64 lanes.  Host-driven loop: timed by the host clock around
+    hk_engine_run; end to end by construction.  N > 1: independent replicas."""
     from hyperkernel_b200 import engine as H
 
-    requests = _engine_requests(ENGINE_REQUESTS, 11 + rank)
-    for _ in range(max(1, min(args.warmup, 2))):
-        _engine_session(H, 1, local, _engine_requests(16, 5))
-    sampler = ClockSampler(local).start()
-    barrier()
-    t0 = time.perf_counter()
-    dt, iters, tokens, launches = _engine_session(H, 1, local, requests)
-    t1 = time.perf_counter()
-    barrier()
-    sampler.stop()
-    clocks = sampler.summary(t0, t1)
-    dt_launch, iters_launch, tokens_launch, launches_launch = _engine_session(H, 0, local, requests)
-    (dt,) = _reduce_max(torch, dist, world, device, dt * 1e3)
-    dt /= 1e3
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = _engine_cpu_baseline()
-    tps = tokens * world / dt
-    # bytes the step kernel reads per iteration: every live lane's sequence, back through its row
-    seq_bytes = sum(len(pr) + lim for pr, lim in requests) * 4 / max(len(requests), 1) * ENGINE_LANES
-    gbs = seq_bytes / (dt / max(iters, 1)) / 1e9
+    dims = dict(ENGINE_DIMS)
+    l0 = hk.kernel_launches()
+    dev = _engine_device(H, local, dims)
+    try:
+        for _ in range(max(1, min(args.warmup, 2))):
+            _engine_session(H, dev, _engine_requests(8, 5), dims["logprobs"])
+        requests = _engine_requests(ENGINE_REQUESTS, 11 + rank)
+        barrier()
+        l1 = hk.kernel_launches()
+        dt, iters, tokens, prompt_tokens = _engine_session(H, dev, requests, dims["logprobs"])
+        launches = hk.kernel_launches() - l1
+        barrier()
+    finally:
+        dev.close()
+    (dt_ms,) = _reduce_max(torch, dist, world, device, dt * 1e3)
+    dt = dt_ms / 1e3
+    # HBM bytes of one decode step's weights (every routed expert a 64-row step hits, in
+    # expectation, plus the shared expert and the dense projections, embedding rows aside)
+    H_, QL, E, K, I, V = (dims[k] for k in ("hidden", "q_lora", "experts", "top_k", "inter", "vocab"))
+    hit = E * (1 - (1 - 1 / E) ** (ENGINE_LANES * K))
+    wbytes = (hit + 1) * 3 * H_ * I + QL * H_ + 128 * 576 * QL + 576 * H_ + H_ * 128 * 512 + E * H_ + V * H_
     return {
-        "metric": "engine tokens/s through the Kernel boundary (test model, 64 lanes)",
-        "value": tps, "unit": "tokens/s", "n_gpus": world, "steps": iters, "warmup": max(1, min(args.warmup, 2)),
-        "ms_per_step": dt * 1e3 / max(iters, 1), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "int32 (token ids)", "data": "synthetic (seeded prompts)",
-        "config": {"workload": f"{ENGINE_REQUESTS} requests, prompts U{list(ENGINE_PROMPT)}, {ENGINE_LIMIT} tokens "
-                               f"each, {ENGINE_LANES} lanes, pages of {ENGINE_PAGE_ROWS} rows, block {ENGINE_BLOCK}, "
-                               "resident-ring transport",
-                   "parallelism": f"replicas{world}" if world > 1 else "single",
-                   "timing": "host clock around hk_engine_run (host-driven loop); a step = an engine iteration "
-                             "that produced tokens",
-                   "gpu_launches_note": "ring transport: the resident executor (launched once when the device "
-                                        "is opened) runs every apply and step item",
-                   "launch_transport": {"tokens_per_s": tokens_launch * world / dt_launch,
-                                        "ms_per_step": dt_launch * 1e3 / max(iters_launch, 1),
-                                        "gpu_launches": int(launches_launch)}},
-        "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
-                     "traffic": None, "kernel": "executor_kernel (apply + step of the test model)",
-                     "note": "latency-bound: a step moves a few hundred KB; the per-step time is the measure",
-                     "peak_source": peak_src},
-        "cpu_baseline": cpu,
-        "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": None, "d2h_bytes_per_step": None,
-                "note": "the engine loop is end to end: commands cross to the device and ids back every step"},
-        "gpu_launches": int(launches), "clocks": clocks,
+        "workload": f"HK_MODEL_MLA behind hk_push/hk_drain driven by hk_engine_run: {ENGINE_REQUESTS} requests, "
+                    f"prompts U[{ENGINE_PROMPT[0]},{ENGINE_PROMPT[1]}), {ENGINE_LIMIT} tokens each, {ENGINE_LANES} "
+                    "lanes, 1 DeepSeek-V3-shaped layer (hidden 7168, MLA 128 heads 512+64, FP8 projections, 256+1 "
+                    "experts top-8, inter 2048), vocabulary 129280, greedy with 20 logprob pairs per token",
+        "parallelism": f"replicas{world}" if world > 1 else "single GPU",
+        "timing": "host clock around hk_engine_run, max over ranks (host-driven loop; commands and ids cross "
+                  "the boundary every step)",
+        "tokens_per_s": tokens * world / dt, "prompt_tokens_per_s": prompt_tokens * world / dt,
+        "seconds": dt, "iterations": iters, "ms_per_iteration": dt * 1e3 / max(iters, 1),
+        "generated_tokens": tokens * world, "prompt_tokens": prompt_tokens * world,
+        "decode_step_weight_bytes": int(wbytes), "gpu_launches": int(launches),
+        "gpu_launches_with_open": int(hk.kernel_launches() - l0),
     }
 
 
-def _engine_cpu_baseline(n=ENGINE_REQUESTS):
-    """The oracle engine over the oracle's restatement of the reference's test device, on the
-    same requests (one thread)."""
-    from oracle import engine as E
-
-    requests = _engine_requests(n, 11)
-    context = ENGINE_PAGE_ROWS * ENGINE_ENTRIES
-    pages = ENGINE_LANES * ENGINE_ENTRIES + 1
-    jobs = E.Channel()
-    sinks = []
-    for pr, lim in requests:
-        sink = E.Sink()
-        jobs.send(E.JobRun(E.Request(list(pr), E.Sampling(), lim, [], sink)))
-        sinks.append(sink)
-    jobs.close()
-    fake = E.Fake(pages, pages, ENGINE_PAGE_ROWS, ENGINE_ENTRIES, ENGINE_LANES, context, ENGINE_CHUNK,
-                  drafts=ENGINE_BLOCK - 1)
+def _run_engine(args, torch, dist, hk, ClockSampler, world, rank, local, device, barrier, hbm_peak, peak_src):
+    """--workload engine: leg_engine as its own line."""
+    sampler = ClockSampler(local).start()
     t0 = time.perf_counter()
-    err = E.run(E.Model(context=context, width=ENGINE_LANES, chunk=ENGINE_CHUNK, block=ENGINE_BLOCK, pad=7),
-                E.Pool(page_rows=ENGINE_PAGE_ROWS, entries=ENGINE_ENTRIES, window=ENGINE_ENTRIES),
-                fake, jobs, E.Metrics(), E.Plan(budget=None, every=1, headroom=2048), E.EngineConfig())
-    dt = time.perf_counter() - t0
-    if err is not None:
-        raise RuntimeError(f"oracle engine failed: {err}")
-    tokens = sum(sum(1 for o in s.items if isinstance(o, E.OutToken)) for s in sinks)
-    return {"value": tokens / dt, "unit": "tokens/s", "cores": 1, "kind": "port",
-            "sample": f"the same {n} requests through the Python restatement of the engine and of the "
-                      "reference's test device"}
+    leg = leg_engine(args, torch, dist, hk, world, rank, local, device, barrier, hbm_peak)
+    t1 = time.perf_counter()
+    sampler.stop()
+    per_step = leg["ms_per_iteration"] / 1e3
+    gbs = leg["decode_step_weight_bytes"] / per_step / 1e9 if per_step > 0 else 0.0
+    return {
+        "metric": "engine tokens/s through the Kernel boundary (HK_MODEL_MLA, 64 lanes)",
+        "value": leg["tokens_per_s"], "unit": "tokens/s", "n_gpus": world, "steps": leg["iterations"],
+        "warmup": max(1, min(args.warmup, 2)), "ms_per_step": leg["ms_per_iteration"], "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "e4m3 x e4m3 -> f32, bf16 activations",
+        "data": "synthetic (seeded prompts, seeded random weights)", "config": {"workload": leg["workload"],
+                                                                               "timing": leg["timing"]},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
+                     "traffic": None, "kernel": "whole engine iteration (decode-step weights / iteration time)",
+                     "peak_source": peak_src,
+                     "note": "iterations mix decode steps and prompt chunks; the weights a decode step streams "
+                             "bound it from below"},
+        "cpu_baseline": None,
+        "e2e": {"value": leg["tokens_per_s"], "unit": "tokens/s", "h2d_bytes_per_step": None,
+                "d2h_bytes_per_step": None,
+                "note": "end to end: hk_push copies each share's host arrays, hk_drain returns host ids and "
+                        "logprob lists"},
+        "gpu_launches": leg["gpu_launches"], "clocks": sampler.summary(t0, t1), "engine": leg,
+    }
 
 
 def _sample_cpu_baseline(logits, cu, samplings, seeds, drafts, sample_lanes=4):

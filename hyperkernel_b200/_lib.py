@@ -60,8 +60,15 @@ SIGNATURES = {
     "hk_ep_dispatch": (C.c_int, [P, P, I32, P, P, I32, I32, I32, I32, I32, I32, P, P, P, P, P, C.c_uint32, P]),
     "hk_ep_return": (C.c_int, [P, I32, I32, I32, I32, P, P, P, I32, I32, P, P, P, C.c_uint32, P]),
     "hk_ep_wait": (C.c_int, [P, I32, I32, C.c_uint32, I32, P]),
+    "hk_sym_alloc": (C.c_int, [SZ, P, P]),
+    "hk_sym_import": (C.c_int, [P, P]),
+    "hk_sym_close": (C.c_int, [P]),
+    "hk_sym_free": (C.c_int, [P]),
+    "hk_cp_merge": (C.c_int, [P, P, P, I32, I32, C.c_uint32, I32, I64, I32, P, P, P]),
     "hk_combine": (C.c_int, [P, I64, P, P, P, I32, I32, I32, P, P]),
     "hk_open": (C.c_int, [P, P]),
+    "hk_open_mla": (C.c_int, [P, P, P]),
+    "hk_model_tensor": (C.c_int, [P, C.c_uint32, C.c_char_p, P, P]),
     "hk_close": (None, [P]),
     "hk_pools": (C.c_int, [P, P, P]),
     "hk_push": (C.c_int, [P, P]),
@@ -295,13 +302,14 @@ def mla_partial_fp8(q, kv_cache, kv_scale, block_table, cu_seqlens, positions, k
 
 
 def mla_partial(q, kv_cache, block_table, cu_seqlens, positions, kv_begin, kv_end, page_size, max_kv_len,
-                scale, stream=None):
+                scale, stream=None, out=None, lse=None):
     """Partial attention of KV ranges on the tcgen05 kernel over the page-blocked bf16 cache:
-    fp32 o [T, H, 512] normalised within the range, lse [T, H] (-inf where it is empty)."""
+    fp32 o [T, H, 512] normalised within the range, lse [T, H] (-inf where it is empty), into
+    `out` / `lse` when given (e.g. a context-parallel exchange buffer)."""
     T, H, _ = q.shape
     dev = q.device
-    o = torch.empty((T, H, 512), dtype=torch.float32, device=dev)
-    lse = torch.empty((T, H), dtype=torch.float32, device=dev)
+    o = out if out is not None else torch.empty((T, H, 512), dtype=torch.float32, device=dev)
+    lse = lse if lse is not None else torch.empty((T, H), dtype=torch.float32, device=dev)
     L = cu_seqlens.shape[0] - 1
     ws = mla_workspace_size(L, T, H, max_kv_len)
     workspace = torch.empty(max(ws, 16), dtype=torch.uint8, device=dev)

@@ -120,7 +120,8 @@ int hk_check_errors(void) {
   if (v == 0) return HK_OK;
   HK_TRY_CUDA(cudaMemset(w, 0, sizeof v));
   static const char* names[] = {"?",         "pack overflow",  "pack page", "append slot",
-                                "attn page", "wait timeout",   "moe row",   "route input"};
+                                "attn page", "wait timeout",   "moe row",   "route input",
+                                "token id"};
   unsigned site = (unsigned)((v >> 32) & 0x7fffffff);
   unsigned detail = (unsigned)(v & 0xffffffffu);
   return hk::fail(HK_EDEVICE, "device error: %s (site %u, detail %u)",

@@ -32,6 +32,7 @@ enum ErrSite : unsigned {
   kErrWaitTimeout = 5,    // a bounded mbarrier wait ran out
   kErrMoeRow = 6,         // a permuted row or token index out of range
   kErrRouteInput = 7,     // non-finite router logits
+  kErrToken = 8,          // a token id outside the vocabulary (the model's embedding lookup)
 };
 
 }  // namespace hk

@@ -23,6 +23,7 @@
 #include <stdint.h>
 #include <string.h>
 
+#include <algorithm>
 #include <atomic>
 #include <chrono>
 #include <deque>
@@ -31,6 +32,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "model.cuh"
 #include "wire.h"
 
 namespace {
@@ -69,6 +71,8 @@ struct Dev {
   unsigned long long* err;  // [0] flag word, [1] lane, [2] position
   int32_t width, entries, window, page_rows, context, chunk, block;
   int64_t pages, window_pages;
+  hk_sampling* mla_sampling;  // HK_MODEL_MLA: the sampler's per-lane settings (Seat writes them)
+  uint64_t* mla_state;        // HK_MODEL_MLA: per-lane generator state (Seat seeds it)
 };
 
 __device__ void fault(const Dev& d, unsigned site, int lane, long long pos) {
@@ -328,6 +332,16 @@ __device__ void apply_messages(const Dev& d, const uint8_t* stream, uint64_t str
           for (int j = 0; j < 3; ++j) s.back[j] = (int32_t)rd32(body, kSeatBack + 4 * j);
           s.reserved = 0;
           d.sampling[lane] = s;
+          if (d.mla_sampling) {
+            hk_sampling hs;
+            hs.temperature = s.temperature;
+            hs.top_p = s.top_p;
+            hs.top_k = s.top_k;
+            hs.logprobs = s.logprobs;
+            hs.seed = ((uint64_t)s.seed_hi << 32) | s.seed_lo;
+            d.mla_sampling[lane] = hs;
+            d.mla_state[lane] = hs.seed;
+          }
         } else {
           fault(d, kFaultMessage, (int)lane, m);
         }
@@ -617,6 +631,7 @@ struct Cmd {
   uint32_t at;
   hk_command c;
   std::vector<int32_t> data;
+  int64_t start = -1;  // a Prompt's first position, set when the command is taken for its step
 };
 
 size_t round16(size_t x) { return (x + 15) / 16 * 16; }
@@ -701,7 +716,7 @@ int take_share(const hk_config& cfg, const hk_share* s, std::vector<Cmd>* out) {
     const hk_command& c = s->commands[i];
     HK_REQUIRE(c.kind <= HK_CMD_START, "command %zu: unknown kind %u", i, c.kind);
     HK_REQUIRE(c.lane < cfg.width, "command %zu: lane %u past the width %u", i, c.lane, cfg.width);
-    Cmd x{s->at, c, {}};
+    Cmd x{s->at, c, {}, -1};
     if (c.kind == HK_CMD_PAGES || c.kind == HK_CMD_PROMPT) {
       HK_REQUIRE((size_t)c.arena + c.count <= s->arena_words, "command %zu: arena words %u..%u past %zu", i,
                  c.arena, c.arena + c.count, s->arena_words);
@@ -722,7 +737,6 @@ int take_share(const hk_config& cfg, const hk_share* s, std::vector<Cmd>* out) {
 
 struct hk_handle {
   hk_config cfg;
-  size_t last_lists = 0;     // Sampled slots of the events the last successful drain returned
   cudaStream_t stream = nullptr;
   Dev dev{};
   int32_t* d_out = nullptr;  // [width * block] step ids, then prompt replies
@@ -757,6 +771,13 @@ struct hk_handle {
   // (and publish `done` for it later), so the handle's device state is undefined and every
   // later hk_push / hk_drain fails with this message.
   std::string broken;
+  // Logprob lists of the Sampled values of the pending events (one per id slot of a Step, one
+  // per Prompted), and those of the events the last successful hk_drain returned.
+  std::vector<uint32_t> pend_counts, last_counts;
+  std::vector<hk_logprob> pend_pairs, last_pairs;
+  // HK_MODEL_MLA
+  hk::MlaModel* mla = nullptr;
+  float* h_lp = nullptr;  // pinned: the step's logprob rows
 };
 
 namespace {
@@ -914,6 +935,7 @@ int apply_batch(hk_handle* h, const std::vector<Cmd>& batch) {
       e.token = h->h_out[base + k++];
       e.clipped = h->cfg.clip;
       h->events.push_back(e);
+      h->pend_counts.push_back(0);  // the test model samples no logprobs
     }
     return HK_OK;
   }
@@ -935,11 +957,129 @@ int apply_batch(hk_handle* h, const std::vector<Cmd>& batch) {
     e.token = h->h_out[base + k++];
     e.clipped = h->cfg.clip;
     h->events.push_back(e);
+    h->pend_counts.push_back(0);
   }
   return HK_OK;
 }
 
+// ---------------------------------------------------------------------------------------
+// HK_MODEL_MLA: prompt chunks prefilled through the model, decode steps verified by it
+// ---------------------------------------------------------------------------------------
+
+// One Sampled's logprob list from its row of 2n + 1 floats (the reply layout src/gpu/feed.rs:
+// 202-208 reads): the top pairs while their id is >= 0, then the token's own logprob.
+void push_logprob_list(hk_handle* h, int32_t id, const float* row, int32_t n) {
+  if (id < 0 || row == nullptr) {
+    h->pend_counts.push_back(0);
+    return;
+  }
+  uint32_t count = 0;
+  for (int32_t q = 0; q < n && row[2 * q] >= 0.0f; ++q, ++count)
+    h->pend_pairs.push_back(hk_logprob{(uint32_t)row[2 * q], row[2 * q + 1]});
+  h->pend_pairs.push_back(hk_logprob{(uint32_t)id, row[2 * n]});
+  h->pend_counts.push_back(count + 1);
+}
+
+// Copies `words` sampled ids and `lp_floats` logprob floats back, synchronises, and reports the
+// handle's error words and the library's device error word.
+int mla_readback(hk_handle* h, size_t words, size_t lp_floats) {
+  hk::MlaModel* m = h->mla;
+  HK_TRY_CUDA(cudaMemcpyAsync(h->h_out, m->out_ids, 4 * words, cudaMemcpyDeviceToHost, h->stream));
+  if (lp_floats)
+    HK_TRY_CUDA(cudaMemcpyAsync(h->h_lp, m->lp, 4 * lp_floats, cudaMemcpyDeviceToHost, h->stream));
+  HK_TRY_CUDA(cudaMemcpyAsync(h->h_err, h->dev.err, 3 * sizeof(unsigned long long), cudaMemcpyDeviceToHost,
+                              h->stream));
+  HK_TRY_CUDA(cudaStreamSynchronize(h->stream));
+  HK_TRY(fault_status(h->h_err));
+  return hk_check_errors();
+}
+
+// A group of prompt chunks of distinct lanes through one forward pass; Prompted events in the
+// group's push order.
+int mla_prompt_group(hk_handle* h, const std::vector<const Cmd*>& group) {
+  hk::MlaModel* m = h->mla;
+  std::vector<const Cmd*> by_lane = group;
+  std::sort(by_lane.begin(), by_lane.end(), [](const Cmd* a, const Cmd* b) { return a->c.lane < b->c.lane; });
+  std::vector<hk::MlaLaneRows> lanes;
+  std::vector<int32_t> tokens;
+  for (const Cmd* c : by_lane) {
+    lanes.push_back(hk::MlaLaneRows{(int32_t)c->c.lane, (int32_t)c->start, (int32_t)c->data.size()});
+    tokens.insert(tokens.end(), c->data.begin(), c->data.end());
+  }
+  HK_TRY(hk::mla_prompt_step(m, lanes, tokens, h->dev.rows, h->dev.pool, h->dev.err, h->stream));
+  const size_t row = 2 * (size_t)m->n_lp + 1;
+  HK_TRY(mla_readback(h, (size_t)h->cfg.width, m->n_lp > 0 ? (size_t)h->cfg.width * row : 0));
+  for (const Cmd* c : group) {
+    hk_event e{};
+    e.kind = HK_EV_PROMPTED;
+    e.lane = c->c.lane;
+    e.token = h->h_out[c->c.lane];
+    e.clipped = h->cfg.clip;
+    h->events.push_back(e);
+    push_logprob_list(h, e.token, m->n_lp > 0 ? h->h_lp + (size_t)c->c.lane * row : nullptr, m->n_lp);
+  }
+  return HK_OK;
+}
+
+int apply_batch_mla(hk_handle* h, const std::vector<Cmd>& batch) {
+  size_t i = 0;
+  while (i < batch.size()) {
+    if (batch[i].c.kind != HK_CMD_PROMPT) {  // pages, seats, starts and ends: the apply kernel
+      std::vector<Cmd> run;
+      while (i < batch.size() && batch[i].c.kind != HK_CMD_PROMPT) run.push_back(batch[i++]);
+      HK_TRY(apply_batch(h, run));
+      continue;
+    }
+    std::vector<const Cmd*> group;
+    std::vector<uint32_t> seen;
+    size_t rows = 0;
+    while (i < batch.size() && batch[i].c.kind == HK_CMD_PROMPT &&
+           std::find(seen.begin(), seen.end(), batch[i].c.lane) == seen.end() &&
+           (group.empty() || rows + batch[i].data.size() <= (size_t)h->mla->t_cap)) {
+      group.push_back(&batch[i]);
+      seen.push_back(batch[i].c.lane);
+      rows += batch[i].data.size();
+      ++i;
+    }
+    HK_TRY(mla_prompt_group(h, group));
+  }
+  return HK_OK;
+}
+
+int run_step_mla(hk_handle* h) {
+  hk::MlaModel* m = h->mla;
+  const hk_config& c = h->cfg;
+  std::vector<hk::MlaLaneRows> lanes;
+  for (uint32_t l = 0; l < c.width; ++l) {
+    const auto& st = h->lanes[l];
+    if (!(st.live && st.pos < st.upto)) continue;
+    if ((int64_t)st.pos >= (int64_t)c.context - 1)
+      return hk::fail(HK_EDEVICE, "lane %u decodes at the idle position", l);
+    const uint32_t rows = std::min<uint32_t>({c.block, st.upto - st.pos, c.context - 1 - st.pos});
+    lanes.push_back(hk::MlaLaneRows{(int32_t)l, (int32_t)st.pos, (int32_t)rows});
+  }
+  HK_TRY(hk::mla_decode_step(m, lanes, h->dev.rows, h->dev.pool, h->dev.err, h->stream));
+  const size_t words = (size_t)c.width * c.block, row = 2 * (size_t)m->n_lp + 1;
+  HK_TRY(mla_readback(h, words, m->n_lp > 0 ? words * row : 0));
+  hk_event e{};
+  e.kind = HK_EV_STEP;
+  e.step = h->s;
+  e.ids = (uint32_t)h->ids.size();
+  h->ids.insert(h->ids.end(), h->h_out, h->h_out + words);
+  h->events.push_back(e);
+  for (size_t k = 0; k < words; ++k)
+    push_logprob_list(h, h->h_out[k], m->n_lp > 0 ? h->h_lp + k * row : nullptr, m->n_lp);
+  for (uint32_t l = 0; l < c.width; ++l) {
+    uint32_t n = 0;
+    while (n < c.block && h->h_out[(size_t)l * c.block + n] != -2) ++n;
+    h->lanes[l].pos += n;
+  }
+  h->s += 1;
+  return HK_OK;
+}
+
 int run_step(hk_handle* h) {
+  if (h->mla) return run_step_mla(h);
   const size_t words = (size_t)h->cfg.width * h->cfg.block;
   if (h->ring) {
     HK_TRY(ring_run(h, kItemStep, 0, 0, h->s, 0));
@@ -956,6 +1096,7 @@ int run_step(hk_handle* h) {
   e.ids = (uint32_t)h->ids.size();
   h->ids.insert(h->ids.end(), h->h_out, h->h_out + words);
   h->events.push_back(e);
+  h->pend_counts.insert(h->pend_counts.end(), words, 0u);  // the test model samples no logprobs
   for (uint32_t l = 0; l < h->cfg.width; ++l) {
     uint32_t n = 0;
     while (n < h->cfg.block && h->h_out[(size_t)l * h->cfg.block + n] != -2) ++n;
@@ -970,7 +1111,7 @@ int run(hk_handle* h) {
   for (;;) {
     std::vector<Cmd> batch;
     while (!h->queue.empty()) {
-      const Cmd& c = h->queue.front();
+      Cmd& c = h->queue.front();
       const bool delta = c.c.kind != HK_CMD_PROMPT;
       if (delta && c.at > h->s) break;
       h->applied |= delta;
@@ -980,12 +1121,12 @@ int run(hk_handle* h) {
         case HK_CMD_PAGES: m.upto = c.c.upto; break;
         case HK_CMD_SEAT: m.pos = c.c.pos; break;
         case HK_CMD_START: m.live = true; break;
-        default: m.pos += (uint32_t)c.data.size(); break;
+        default: c.start = m.pos; m.pos += (uint32_t)c.data.size(); break;
       }
       batch.push_back(std::move(h->queue.front()));
       h->queue.pop_front();
     }
-    if (!batch.empty()) HK_TRY(apply_batch(h, batch));
+    if (!batch.empty()) HK_TRY(h->mla ? apply_batch_mla(h, batch) : apply_batch(h, batch));
     bool runnable = false;
     for (auto& m : h->lanes) runnable |= m.live && m.pos < m.upto;
     if (runnable && (int64_t)h->s <= h->horizon) {
@@ -1021,6 +1162,8 @@ void release(hk_handle* h) {
     }
     cudaStreamSynchronize(h->exec_stream);
   }
+  hk::mla_destroy(h->mla);
+  if (h->h_lp) cudaFreeHost(h->h_lp);
   if (h->ctl) cudaFreeHost(h->ctl);
   if (h->exec_stream) cudaStreamDestroy(h->exec_stream);
   cudaFree(h->dev.rows);
@@ -1053,7 +1196,8 @@ int c_logprobs(void* self, uint32_t* counts, size_t counts_cap, size_t* n_counts
 
 int check_config(const hk_config* c) {
   HK_REQUIRE(c, "null config");
-  HK_REQUIRE(c->model == HK_MODEL_FNV, "model %u: only HK_MODEL_FNV (%d) is built", c->model, HK_MODEL_FNV);
+  HK_REQUIRE(c->model == HK_MODEL_FNV || c->model == HK_MODEL_MLA,
+             "model %u: HK_MODEL_FNV (%d) or HK_MODEL_MLA (%d)", c->model, HK_MODEL_FNV, HK_MODEL_MLA);
   HK_REQUIRE(c->page_rows > 0 && c->entries > 0 && c->window > 0 && c->width > 0 && c->block > 0 &&
                  c->chunk > 0 && c->context >= 2,
              "page_rows, entries, window, width, block, chunk must be > 0 and context >= 2");
@@ -1069,7 +1213,12 @@ int check_config(const hk_config* c) {
 
 extern "C" {
 
-int hk_open(const hk_config* config, hk_handle** handle) {
+}  // extern "C"
+
+namespace {
+
+// The pools, block-table rows, lane state and transport of a handle (both models).
+int open_handle(const hk_config* config, hk_handle** handle) {
   HK_REQUIRE(handle, "null handle pointer");
   *handle = nullptr;
   HK_TRY(check_config(config));
@@ -1133,6 +1282,48 @@ int hk_open(const hk_config* config, hk_handle** handle) {
   return HK_OK;
 }
 
+}  // namespace
+
+extern "C" {
+
+int hk_open(const hk_config* config, hk_handle** handle) {
+  HK_REQUIRE(handle, "null handle pointer");
+  *handle = nullptr;
+  HK_REQUIRE(config && config->model == HK_MODEL_FNV,
+             "hk_open: model %u (HK_MODEL_FNV here; HK_MODEL_MLA opens with hk_open_mla)", config ? config->model : 0);
+  return open_handle(config, handle);
+}
+
+int hk_open_mla(const hk_config* config, const hk_mla_model* model, hk_handle** handle) {
+  HK_REQUIRE(handle && model, "hk_open_mla: null argument");
+  *handle = nullptr;
+  HK_REQUIRE(config && config->model == HK_MODEL_MLA, "hk_open_mla: config->model must be HK_MODEL_MLA (%d)",
+             HK_MODEL_MLA);
+  HK_TRY(check_config(config));
+  HK_TRY(hk::mla_check(*config, *model));
+  hk_handle* h = nullptr;
+  HK_TRY(open_handle(config, &h));
+  int rc = hk::mla_create(*config, *model, &h->mla, h->stream);
+  if (rc == HK_OK) {
+    const size_t floats = (size_t)config->width * config->block * (2 * (size_t)model->logprobs + 1);
+    const cudaError_t e = cudaMallocHost(&h->h_lp, 4 * floats);
+    if (e != cudaSuccess) rc = hk::cuda_fail(e, "hk_open_mla: logprob staging");
+  }
+  if (rc != HK_OK) {
+    release(h);
+    return rc;
+  }
+  h->dev.mla_sampling = h->mla->sampling;
+  h->dev.mla_state = h->mla->state;
+  *handle = h;
+  return HK_OK;
+}
+
+int hk_model_tensor(hk_handle* h, uint32_t layer, const char* name, void** ptr, size_t* bytes) {
+  HK_REQUIRE(h && h->mla, "hk_model_tensor: not an HK_MODEL_MLA handle");
+  return hk::mla_tensor(h->mla, h->dev.pool, 4 * (size_t)h->cfg.pages * h->cfg.page_rows, layer, name, ptr, bytes);
+}
+
 void hk_close(hk_handle* handle) {
   if (handle) cudaSetDevice(handle->cfg.device);
   if (handle && handle->stream) cudaStreamSynchronize(handle->stream);
@@ -1176,9 +1367,10 @@ int hk_drain(hk_handle* h, hk_event* events, size_t cap, size_t* n, int32_t* ids
     return handle_fail(h, hk::fail(HK_ESPACE, "hk_drain: %zu events and %zu ids pending", *n, *ids_n));
   if (*n) memcpy(events, h->events.data(), sizeof(hk_event) * *n);
   if (*ids_n) memcpy(ids, h->ids.data(), 4 * *ids_n);
-  h->last_lists = 0;
-  for (const hk_event& e : h->events)
-    h->last_lists += e.kind == HK_EV_STEP ? (size_t)h->cfg.width * h->cfg.block : e.kind == HK_EV_PROMPTED ? 1 : 0;
+  h->last_counts = std::move(h->pend_counts);
+  h->last_pairs = std::move(h->pend_pairs);
+  h->pend_counts.clear();
+  h->pend_pairs.clear();
   h->events.clear();
   h->ids.clear();
   return HK_OK;
@@ -1187,13 +1379,12 @@ int hk_drain(hk_handle* h, hk_event* events, size_t cap, size_t* n, int32_t* ids
 int hk_drain_logprobs(hk_handle* h, uint32_t* counts, size_t counts_cap, size_t* n_counts, hk_logprob* pairs,
                       size_t pairs_cap, size_t* n_pairs) {
   HK_REQUIRE(h && n_counts && n_pairs, "hk_drain_logprobs: null argument");
-  (void)pairs;
-  (void)pairs_cap;
-  *n_counts = h->last_lists;
-  *n_pairs = 0;  // the test model samples no logprobs
-  if (h->last_lists > counts_cap || (h->last_lists && !counts))
-    return hk::fail(HK_ESPACE, "hk_drain_logprobs: %zu lists", h->last_lists);
-  for (size_t i = 0; i < h->last_lists; ++i) counts[i] = 0;
+  *n_counts = h->last_counts.size();
+  *n_pairs = h->last_pairs.size();
+  if (*n_counts > counts_cap || (*n_counts && !counts) || *n_pairs > pairs_cap || (*n_pairs && !pairs))
+    return hk::fail(HK_ESPACE, "hk_drain_logprobs: %zu lists of %zu pairs", *n_counts, *n_pairs);
+  if (*n_counts) memcpy(counts, h->last_counts.data(), 4 * *n_counts);
+  if (*n_pairs) memcpy(pairs, h->last_pairs.data(), sizeof(hk_logprob) * *n_pairs);
   return HK_OK;
 }
 

@@ -23,7 +23,7 @@ EV_IDLE, EV_STEP, EV_PROMPTED = 0, 1, 2
 OUT_SEATED, OUT_TOKEN, OUT_END = 0, 1, 2
 END_STOP, END_LENGTH, END_REFUSED = 0, 1, 2
 END_NAMES = {END_STOP: "stop", END_LENGTH: "length", END_REFUSED: "refused"}
-MODEL_FNV = 1
+MODEL_FNV, MODEL_MLA = 1, 2
 UNBOUNDED = (1 << 64) - 1
 
 
@@ -52,6 +52,13 @@ class Config(C.Structure):
                 ("width", U32), ("context", U32), ("chunk", U32), ("block", U32),
                 ("pages", U64), ("window_pages", U64), ("clip", I32), ("device", I32),
                 ("transport", U32), ("reserved", U32)]
+
+
+class MlaModel(C.Structure):
+    """hk_mla_model: the dimensions and weight seed of the HK_MODEL_MLA decoder."""
+    _fields_ = [("hidden", U32), ("q_lora", U32), ("vocab", U32), ("experts", U32), ("top_k", U32),
+                ("inter", U32), ("layers", U32), ("logprobs", U32), ("seed", U64), ("rope_theta", F32),
+                ("route_scale", F32)]
 
 
 class EngineConfig(C.Structure):
@@ -153,12 +160,39 @@ def encode_share(config: Config, share: Share) -> bytes:
 
 
 class Device:
-    """A device kernel (hk_open): the Kernel the engine drives on a GPU."""
+    """A device kernel (hk_open, or hk_open_mla when `model` is given): the Kernel the engine
+    drives on a GPU."""
 
-    def __init__(self, config: Config):
+    def __init__(self, config: Config, model: MlaModel | None = None):
         self.config = config
+        self.model = model
         self._h = C.c_void_p()
-        _lib.check(_lib.lib().hk_open(C.byref(config), C.byref(self._h)))
+        if model is None:
+            _lib.check(_lib.lib().hk_open(C.byref(config), C.byref(self._h)))
+        else:
+            _lib.check(_lib.lib().hk_open_mla(C.byref(config), C.byref(model), C.byref(self._h)))
+
+    def tensor(self, name: str, layer: int = 0):
+        """(device address, bytes) of one of an HK_MODEL_MLA handle's tensors (hk_model_tensor)."""
+        p, n = C.c_void_p(), SZ()
+        _lib.check(_lib.lib().hk_model_tensor(self._h, layer, name.encode(), C.byref(p), C.byref(n)))
+        return p.value, n.value
+
+    def logprob_lists(self):
+        """The logprob lists of the last drain's Sampled values (hk_drain_logprobs)."""
+        n, m = SZ(), SZ()
+        L = _lib.lib()
+        rc = L.hk_drain_logprobs(self._h, None, 0, C.byref(n), None, 0, C.byref(m))
+        if rc not in (_lib.HK_OK, _lib.HK_ESPACE):
+            _lib.check(rc)
+        counts = (U32 * max(n.value, 1))()
+        pairs = (Logprob * max(m.value, 1))()
+        _lib.check(L.hk_drain_logprobs(self._h, counts, n.value, C.byref(n), pairs, m.value, C.byref(m)))
+        out, k = [], 0
+        for i in range(n.value):
+            out.append([(pairs[k + j].id, pairs[k + j].logprob) for j in range(counts[i])])
+            k += counts[i]
+        return out
 
     def close(self):
         if self._h:

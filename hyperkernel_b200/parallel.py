@@ -160,23 +160,90 @@ def cp_merge(o_part, lse_part, group=None, merge=None):
 
 
 # ------------------------------------------------------------------------------------------
+# buffers shared across the node's GPUs (hk_sym_alloc / hk_sym_import)
+# ------------------------------------------------------------------------------------------
+
+class IpcHandle(ctypes.Structure):
+    """hk_ipc_handle: the 64 bytes of a CUDA IPC memory handle."""
+    _fields_ = [("bytes", ctypes.c_uint8 * 64)]
+
+
+def all_gather_bytes(data: bytes, group=None) -> list:
+    """The default handle exchange: every rank's bytes, in rank order, over the process group
+    (any backend; only the host-side handles travel, never device data)."""
+    out = [None] * dist.get_world_size(group)
+    dist.all_gather_object(out, data, group=group)
+    return out
+
+
+class _Cai:
+    """A raw device allocation seen through __cuda_array_interface__, for torch.as_tensor."""
+
+    def __init__(self, ptr, shape, typestr):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 2, "strides": None}
+
+
+_TYPESTR = {torch.uint8: "|u1", torch.int32: "<i4", torch.float32: "<f4", torch.bfloat16: "<i2"}
+
+
+class SymBuffer:
+    """A buffer every rank allocates with hk_sym_alloc (zeroed device memory plus its IPC handle)
+    and maps every other rank's copy of with hk_sym_import, after the ranks swap handles through
+    `exchange` (bytes in, every rank's bytes out).  `ptrs` is a host array of the world's
+    addresses in this process (rank i's copy at i), the form the hk_ep_* and hk_cp_merge entry
+    points take; `tensor` views this rank's own copy.  No torch allocator and no NCCL."""
+
+    def __init__(self, shape, dtype, world, rank, exchange):
+        self.shape, self.dtype, self.world, self.rank = tuple(shape), dtype, world, rank
+        self.nbytes = int(np.prod(self.shape)) * torch.empty((), dtype=dtype).element_size()
+        p, h = ctypes.c_void_p(), IpcHandle()
+        _lib.call("hk_sym_alloc", max(self.nbytes, 16), ctypes.byref(p), ctypes.byref(h))
+        self.local = p.value
+        handles = exchange(bytes(h.bytes))
+        addrs = []
+        self._imported = []
+        for i, hb in enumerate(handles):
+            if i == rank:
+                addrs.append(self.local)
+                continue
+            ih, q = IpcHandle.from_buffer_copy(hb), ctypes.c_void_p()
+            _lib.call("hk_sym_import", ctypes.byref(ih), ctypes.byref(q))
+            self._imported.append(q.value)
+            addrs.append(q.value)
+        self.ptrs = (ctypes.c_uint64 * world)(*addrs)
+        view = torch.as_tensor(_Cai(self.local, self.shape, _TYPESTR[dtype]), device=torch.device("cuda"))
+        self.tensor = view.view(dtype) if dtype == torch.bfloat16 else view
+
+    def close(self, barrier):
+        """Unmaps the peers' copies, waits for every rank to do the same (`barrier`), then frees
+        this rank's copy."""
+        for q in self._imported:
+            _lib.call("hk_sym_close", q)
+        self._imported = []
+        barrier()
+        if self.local:
+            _lib.call("hk_sym_free", self.local)
+            self.local = None
+
+
+# ------------------------------------------------------------------------------------------
 # expert parallelism over NVLink peer memory
 # ------------------------------------------------------------------------------------------
 
 class EpPeer:
     """Expert-parallel dispatch and return written straight into the other ranks' memory
-    (hk_ep_counts / hk_ep_dispatch / hk_ep_return over symmetric buffers), so a step needs no
-    host synchronisation and no NCCL call: the counts, the routed rows and the expert outputs
-    travel as NVLink stores from our kernels, and every rank waits on epoch flags with a bound.
+    (hk_ep_counts / hk_ep_dispatch / hk_ep_return over SymBuffers), so a step needs no host
+    synchronisation and no NCCL call: the counts, the routed rows and the expert outputs travel
+    as NVLink stores from our kernels, and every rank waits on epoch flags with a bound.
 
     The receive buffer comes out expert-major, so the grouped FFN runs over it with the
-    identity permutation.  Buffers are sized for `tokens` tokens per rank routed top_k ways."""
+    identity permutation.  Buffers are sized for `tokens` tokens per rank routed top_k ways.
+    The process group only carries the IPC handles at set-up (`exchange`)."""
 
     FLAGS_COUNTS, FLAGS_DISPATCH, FLAGS_RETURN = 0, 1, 2
 
-    def __init__(self, num_experts, tokens, top_k, hidden, group=None, timeout_us=2_000_000):
-        import torch.distributed._symmetric_memory as symm
-
+    def __init__(self, num_experts, tokens, top_k, hidden, group=None, timeout_us=2_000_000, exchange=None):
         self.group = group or dist.group.WORLD
         self.world = dist.get_world_size(self.group)
         self.rank = dist.get_rank(self.group)
@@ -186,20 +253,20 @@ class EpPeer:
         self.rows_cap = tokens * top_k * self.world
         self.timeout_us = timeout_us
         dev = torch.device("cuda", torch.cuda.current_device())
+        ex = exchange or (lambda b: all_gather_bytes(b, self.group))
 
         def sym(shape, dtype):
-            t = symm.empty(shape, dtype=dtype, device=dev)
-            h = symm.rendezvous(t, self.group)
-            ptrs = (ctypes.c_uint64 * self.world)(*[int(x) for x in h.buffer_ptrs])  # host array
-            return t, h, ptrs
+            return SymBuffer(shape, dtype, self.world, self.rank, ex)
 
-        self.counts, self._hc, self.counts_ptrs = sym((self.world * num_experts,), torch.int32)
-        self.flags, self._hf, self.flags_ptrs = sym((3 * 8,), torch.int32)
-        self.recv_x, self._hx, self.recv_x_ptrs = sym((self.rows_cap, hidden), torch.uint8)
-        self.recv_s, self._hs, self.recv_s_ptrs = sym((self.rows_cap, hidden // 128), torch.float32)
-        self.back_y, self._hb, self.back_y_ptrs = sym((self.back_cap, hidden), torch.bfloat16)
-        self.flags.zero_()
-        self.counts.zero_()
+        self._bufs = [sym((self.world * num_experts,), torch.int32), sym((3 * 8,), torch.int32),
+                      sym((self.rows_cap, hidden), torch.uint8), sym((self.rows_cap, hidden // 128), torch.float32),
+                      sym((self.back_cap, hidden), torch.bfloat16)]
+        c, f, x, sc, b = self._bufs
+        self.counts, self.counts_ptrs = c.tensor, c.ptrs
+        self.flags, self.flags_ptrs = f.tensor, f.ptrs
+        self.recv_x, self.recv_x_ptrs = x.tensor, x.ptrs
+        self.recv_s, self.recv_s_ptrs = sc.tensor, sc.ptrs
+        self.back_y, self.back_y_ptrs = b.tensor, b.ptrs
         torch.cuda.synchronize()
         dist.barrier(group=self.group)
         self.send_base = torch.zeros(num_experts, dtype=torch.int32, device=dev)
@@ -208,6 +275,12 @@ class EpPeer:
         self.done = torch.zeros(2, dtype=torch.int32, device=dev)
         self.identity = torch.arange(self.rows_cap, dtype=torch.int32, device=dev)
         self.epoch = 0
+
+    def close(self):
+        torch.cuda.synchronize()
+        for b in self._bufs:
+            b.close(lambda: dist.barrier(group=self.group))
+        self._bufs = []
 
     def _wait(self, which, stream):
         _lib.call("hk_ep_wait", _lib.ptr(self.flags), which, self.world, self.epoch, self.timeout_us,
@@ -238,3 +311,52 @@ class EpPeer:
                   ctypes.addressof(self.back_y_ptrs), ctypes.addressof(self.flags_ptrs), _lib.ptr(self.done[1:2]), self.epoch, s)
         self._wait(self.FLAGS_RETURN, stream)
         return self.back_y
+
+
+# ------------------------------------------------------------------------------------------
+# context parallelism over NVLink peer memory
+# ------------------------------------------------------------------------------------------
+
+class CpPeer:
+    """The context-parallel exchange of a step's (o, lse) partials fused with their LSE merge
+    (hk_cp_merge): each rank's partial attention writes straight into its own shared buffer, and
+    the merge kernel reads every rank's over NVLink once every rank's epoch flag is up.  Two sets
+    of buffers alternate by step parity, so a rank that runs ahead writes the set no peer is
+    reading.  `rows` x `dv` partial rows per rank (the attention's whole output), of which the
+    first `merge_rows` are merged."""
+
+    def __init__(self, rows, dv, merge_rows, group=None, timeout_us=2_000_000, exchange=None):
+        self.group = group or dist.group.WORLD
+        self.world = dist.get_world_size(self.group)
+        self.rank = dist.get_rank(self.group)
+        self.rows, self.dv, self.merge_rows, self.timeout_us = rows, dv, merge_rows, timeout_us
+        ex = exchange or (lambda b: all_gather_bytes(b, self.group))
+        self._o = [SymBuffer((rows, dv), torch.float32, self.world, self.rank, ex) for _ in range(2)]
+        self._lse = [SymBuffer((rows,), torch.float32, self.world, self.rank, ex) for _ in range(2)]
+        self._flags = [SymBuffer((8,), torch.int32, self.world, self.rank, ex) for _ in range(2)]
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.out = torch.empty((merge_rows, dv), dtype=torch.bfloat16, device=dev)
+        self.lse_out = torch.empty((merge_rows,), dtype=torch.float32, device=dev)
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        self.epoch = 0
+
+    def next_buffers(self):
+        """Starts a step: the (o, lse) tensors this rank's partial attention writes into."""
+        self.epoch = (self.epoch + 1) & 0x7FFFFFFF or 1
+        k = self.epoch & 1
+        return self._o[k].tensor, self._lse[k].tensor
+
+    def merge(self, stream=None):
+        """Merges every rank's partial of this step; returns (out bf16, lse) of merge_rows rows."""
+        k = self.epoch & 1
+        _lib.call("hk_cp_merge", ctypes.addressof(self._o[k].ptrs), ctypes.addressof(self._lse[k].ptrs),
+                  ctypes.addressof(self._flags[k].ptrs), self.world, self.rank, self.epoch, self.timeout_us,
+                  self.merge_rows, self.dv, _lib.ptr(self.out), _lib.ptr(self.lse_out), _lib.stream_ptr(stream))
+        return self.out, self.lse_out
+
+    def close(self):
+        torch.cuda.synchronize()
+        for b in self._o + self._lse + self._flags:
+            b.close(lambda: dist.barrier(group=self.group))
+        self._o = self._lse = self._flags = []

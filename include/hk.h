@@ -309,6 +309,40 @@ int hk_ep_return(const uint16_t* y, int32_t num_experts, int32_t world, int32_t 
 int hk_ep_wait(const uint32_t* flags, int32_t which, int32_t world, uint32_t epoch,
                int32_t timeout_us, void* stream);
 
+/* ------------------------------------------------------------------------------------ */
+/* Buffers shared across the GPUs of one node, and the context-parallel merge            */
+/* The reference maps its ranks' buffers through VMM handles passed over its rank fabric  */
+/* (src/gpu/ranks.rs:198-244, fabric_map); here a buffer travels as a CUDA IPC handle.   */
+/* ------------------------------------------------------------------------------------ */
+
+/* The bytes of a CUDA IPC memory handle: plain data the host may send to other processes. */
+typedef struct {
+    uint8_t bytes[64];
+} hk_ipc_handle;
+
+/* Allocates `bytes` of zeroed device memory on the current device and its IPC handle. */
+int hk_sym_alloc(size_t bytes, void** ptr, hk_ipc_handle* handle);
+/* Maps another process's hk_sym_alloc buffer (its handle) into this process on the current
+ * device, peer access enabled; *ptr is the address this process's kernels use for it. */
+int hk_sym_import(const hk_ipc_handle* handle, void** ptr);
+/* Unmaps an imported buffer; frees an hk_sym_alloc buffer (after every importer closed it). */
+int hk_sym_close(void* peer_ptr);
+int hk_sym_free(void* ptr);
+
+/* Context-parallel exchange fused with the LSE merge: o_parts / lse_parts / flags are host
+ * arrays of `world` device addresses (rank i's copy of each symmetric buffer, mapped into this
+ * process): o [rows][dv] fp32 and lse [rows] partials of the same query rows (hk_mla_partial
+ * writes them), flags [8] uint32 (zero before the first step).  The kernel raises this rank's
+ * epoch flag on every rank, waits until every rank's flag carries `epoch` (bounded by timeout_us;
+ * a timeout sets the device error word and skips the merge), then reads every rank's partial
+ * over NVLink and writes out [rows][dv] bf16 = sum_i e^(lse_i - m) o_i / sum_i e^(lse_i - m),
+ * lse_out [rows] = m + log(sum_i e^(lse_i - m)), m = max lse_i.  A rank may write its next
+ * partial only into a second set of buffers (alternate sets by epoch parity): a peer may still
+ * be reading this epoch's set. */
+int hk_cp_merge(const uint64_t* o_parts, const uint64_t* lse_parts, const uint64_t* flags, int32_t world,
+                int32_t rank, uint32_t epoch, int32_t timeout_us, int64_t rows, int32_t dv, uint16_t* out,
+                float* lse_out, void* stream);
+
 /* out[t][hidden] bf16 = sum_k perm_weight[inv[t,k]] * y[inv[t,k]] (+ shared[t] when not
  * NULL), fp32 accumulation in k order; y has `rows` rows. */
 int hk_combine(const uint16_t* y, int64_t rows, const float* perm_weight, const int32_t* inv,
@@ -410,6 +444,9 @@ typedef struct {
  * tokens per lane, the draft acceptance rule of the reference's test device, capped at the
  * lane's reserved rows. */
 #define HK_MODEL_FNV 1
+/* HK_MODEL_MLA is a DeepSeek-shaped decoder (opened with hk_open_mla): the decode step of the
+ * reference's LLM bundles, rebuilt from this library's kernels (see hk_mla_model). */
+#define HK_MODEL_MLA 2
 
 typedef struct {
     uint32_t model;          /* HK_MODEL_FNV */
@@ -444,8 +481,60 @@ typedef struct {
 
 /* Opens a device kernel: allocates the pools, the block-table rows and the lane state on
  * `device` and returns its handle.  One handle per process and GPU; a handle's calls are
- * not thread-safe. */
+ * not thread-safe.  config->model must be HK_MODEL_FNV (HK_MODEL_MLA opens with hk_open_mla). */
 int hk_open(const hk_config* config, hk_handle** handle);
+
+/* The decoder behind HK_MODEL_MLA: `layers` layers of MLA attention (128 heads, a latent of 512
+ * plus 64 RoPE dims per token, absorbed projections) and an MoE FFN (`experts` routed experts,
+ * top_k sigmoid routing, one shared expert), between a bf16 token embedding and an FP8 vocabulary
+ * projection.  Every projection is e4m3 with 128x128 fp32 block scales (hk_gemm_fp8 /
+ * hk_moe_grouped); activations are bf16, quantised to e4m3 in 1x128 blocks before each
+ * projection.  One decode step of a packed batch (rows of every live lane, or the rows of the
+ * prompt chunks being applied):
+ *   x = embed[token]
+ *   per layer:  a = rmsnorm(x);  q = (rmsnorm(a Wqa)) Wqb;  kv = a Wkva
+ *               q.rope and kv.rope rotated by the row's position, kv.latent rmsnorm-ed;
+ *               kv appended at the row's slot (hk_kv_append_bf16, page-blocked, pages of 64 rows);
+ *               o = MLA attention over the lane's pages (hk_mla_decode);  x += o Wo;
+ *               h = rmsnorm(x);  x += combine(top_k experts of sigmoid(h Wr)) + shared(h)
+ *   logits = rmsnorm(x) Wvocab for the rows that are sampled; then hk_sample_verify.
+ * RMS norms carry no gain (eps 1e-6); RoPE rotates dim i with dim i + 32 of the 64 rope dims by
+ * position * rope_theta^(-i/32); attention scale 1/sqrt(576).  Weights are seeded random values
+ * (N(0, sigma) quantised, sigma = 1/sqrt(fan-in)); hk_model_tensor gives their device addresses
+ * so a loader can overwrite them.
+ * Decode steps verify `block` rows per lane: the lane's last token and block - 1 drafts found
+ * by prompt lookup (the tokens that followed the latest earlier occurrence of the last token in
+ * the lane's last 4096 positions; -1 where there is none).  Prompt chunks are prefilled in one
+ * forward pass per batch of distinct lanes and answered with a token sampled from the chunk's
+ * last row.  Each sampled token carries `logprobs` (id, logprob) pairs then its own logprob. */
+typedef struct {
+    uint32_t hidden;      /* model width, a multiple of 128 */
+    uint32_t q_lora;      /* query low-rank width, a multiple of 128 */
+    uint32_t vocab;       /* vocabulary, a multiple of 16, <= 4,194,304 */
+    uint32_t experts;     /* routed experts, a multiple of 16, <= 256 */
+    uint32_t top_k;       /* experts per token, <= 16 */
+    uint32_t inter;       /* expert intermediate width, a multiple of 128 */
+    uint32_t layers;      /* decoder layers, >= 1 */
+    uint32_t logprobs;    /* (id, logprob) pairs returned with every sampled token, <= 64 */
+    uint64_t seed;        /* weight seed */
+    float rope_theta;     /* RoPE base (0 = 10000) */
+    float route_scale;    /* routed weights' scale (0 = 1) */
+} hk_mla_model;
+
+/* Opens a device kernel running HK_MODEL_MLA (config->model == HK_MODEL_MLA, page_rows == 64,
+ * transport HK_TRANSPORT_LAUNCH): allocates the pools as hk_open does, plus the weights, a
+ * page-blocked bf16 latent cache of config->pages pages per layer and the step's buffers. */
+int hk_open_mla(const hk_config* config, const hk_mla_model* model, hk_handle** handle);
+
+/* Device address and size of one of an HK_MODEL_MLA handle's tensors: `name` is one of "embed"
+ * (bf16 [vocab][hidden]), "vocab" / "vocab.scale" (e4m3 [vocab][hidden], fp32 [vocab/128][hidden/
+ * 128]), per layer `layer`: "wqa", "wqb", "wkva", "wo", "router" (e4m3 [n][k]) and their ".scale"
+ * (fp32 [ceil(n/128)][k/128]), "w13", "w2" (e4m3 [experts + 1][..], the shared expert last) and
+ * their ".scale", "kv" (the layer's latent cache, bf16, page-blocked); "tokens" (the token pool,
+ * int32 [pages][page_rows], -1 = unwritten).  Shapes: wqa [q_lora][hidden], wqb [128*576][q_lora],
+ * wkva [576][hidden], wo [hidden][128*512], router [experts][hidden], w13 [experts+1][2*inter]
+ * [hidden], w2 [experts+1][hidden][inter]. */
+int hk_model_tensor(hk_handle* handle, uint32_t layer, const char* name, void** ptr, size_t* bytes);
 void hk_close(hk_handle* handle);
 /* Kernel::pools: (pages, window_pages). */
 int hk_pools(const hk_handle* handle, size_t* pages, size_t* window_pages);

@@ -61,6 +61,8 @@ def _rank_main(rank, port, what):
             _ep(rank, dev)
         elif what == "ep_peer":
             _ep_peer(rank, dev)
+        elif what == "cp_peer":
+            _cp_peer(rank, dev)
         else:
             _cp(rank, dev)
     finally:
@@ -119,6 +121,7 @@ def _ep_peer(rank, dev):
         torch.cuda.synchronize()
         hk.check_errors()
         assert torch.equal(back[:T * K].view(torch.int16), want.view(torch.int16)), f"rank {rank} step {step}"
+    ep.close()
 
 
 def _cp(rank, dev):
@@ -156,6 +159,55 @@ def _cp(rank, dev):
         a = out.float().cpu().numpy()
         assert np.abs(a - f).max() / np.abs(f).max() <= TOL
         assert (lse.cpu() - full_lse.reshape(-1).cpu()).abs().max().item() <= 1e-3
+
+
+def _cp_peer(rank, dev):
+    """Context parallelism through the C ABI only: each rank's tcgen05 partial over its half of a
+    20,000-row lane is written into its own hk_sym_alloc buffer, and hk_cp_merge reads both
+    ranks' partials over NVLink and merges them, for three steps (the buffer sets alternate);
+    the merged rows match the whole lane on one GPU, and the oracle on sampled heads."""
+    from hyperkernel_b200 import _lib as hk
+    from hyperkernel_b200 import parallel as P
+    import oracle
+
+    heads = 128
+    rng = W.Rng(94)
+    lay = W.paged_layout(rng, np.array([20000]), np.array([5]), 64)
+    inp = W.mla_inputs(lay, heads, seed=95)
+    T = lay.num_tokens
+    p = oracle.pack(lay.new_rows, lay.context, lay.block_table, 64, lay.num_pages, T)
+    d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    q = torch.from_numpy(inp["q"].view(np.int16)).to(dev).view(torch.bfloat16)
+    cache = torch.from_numpy(inp["kv_cache"].view(np.int16)).to(dev).view(torch.bfloat16)
+    kv = int(lay.kv_len[0])
+    bt, cu, pos = d(lay.block_table), d(p["cu_seqlens"]), d(p["positions"][:T].copy())
+    whole, whole_lse = hk.mla_decode(q, cache, bt, cu, pos, 64, kv, inp["scale"], impl=2)
+    b, e = P.cp_ranges(kv, 2)[rank]
+    kb, ke = d(np.array([b], np.int32)), d(np.array([e], np.int32))
+    cp = P.CpPeer(T * heads, 512, T * heads)
+    heads_s = np.array([0, 77, 127])
+    want, want_lse = oracle.mla_decode(np.ascontiguousarray(inp["q"][:, heads_s]), lay.block_table, p["cu_seqlens"],
+                                       p["positions"][:T], 64, inp["scale"], kv_bf16=inp["kv_cache"])
+    for step in range(3):
+        o_buf, l_buf = cp.next_buffers()
+        ws = torch.empty(hk.mla_workspace_size(1, T, heads, kv), dtype=torch.uint8, device=dev)
+        hk.call("hk_mla_partial", hk.ptr(q), hk.ptr(cache), hk.ptr(bt), bt.shape[1], hk.ptr(cu), hk.ptr(pos),
+                hk.ptr(kb), hk.ptr(ke), 1, T, heads, 64, cache.shape[0], kv, inp["scale"], hk.ptr(o_buf),
+                hk.ptr(l_buf), hk.ptr(ws), ws.numel(), hk.stream_ptr())
+        out, lse = cp.merge()
+        torch.cuda.synchronize()
+        hk.check_errors()
+        a, f = out.float().cpu().numpy(), whole.reshape(-1, 512).float().cpu().numpy()
+        assert np.abs(a - f).max() / np.abs(f).max() <= TOL, f"rank {rank} step {step}"
+        assert (lse.cpu() - whole_lse.reshape(-1).cpu()).abs().max().item() <= 1e-3
+        got = a.reshape(T, heads, 512)[:, heads_s]
+        assert np.abs(got - want).max() / np.abs(want).max() <= TOL
+    cp.close()
+
+
+@pytest.mark.skipif(not _two_gpus(), reason="needs two GPUs")
+def test_context_parallel_over_peer_memory_on_two_gpus():
+    mp.spawn(_rank_main, args=(_port(), "cp_peer"), nprocs=2, join=True)
 
 
 @pytest.mark.skipif(not _two_gpus(), reason="needs two GPUs")
