@@ -269,7 +269,7 @@ def main(argv=None):
     ap.add_argument("--no-legs", action="store_true",
                     help="skip the expert-parallel (config 4) and context-parallel (config 5) legs")
     ap.add_argument("--workload", default="decode",
-                    choices=["decode", "moe", "linear", "longctx", "sample", "mixed", "engine"])
+                    choices=["decode", "moe", "linear", "longctx", "sample", "mixed", "engine", "step"])
     ap.add_argument("--experts", type=int, default=None, help="profiling override of config 4's 256 experts")
     ap.add_argument("--full-dequant", action="store_true",
                     help="longctx: convert the whole FP8 pool to bf16 every step (no mirror)")
@@ -375,10 +375,15 @@ def main(argv=None):
         # the headline step's buffers go first: the legs hold ~12 GB of expert weights and
         # ~2.3 GB of FP8 pool and mirror per GPU
         del step, cache
-        torch.cuda.empty_cache()
-        legs["ep"] = leg_ep(args, torch, dist, hk, par, world, rank, device, stream, barrier, peak_hbm())
-        torch.cuda.empty_cache()
-        legs["cp"] = leg_cp(args, torch, dist, hk, par, world, rank, device, stream, barrier, peak_hbm())
+        for name, leg in (("ep", leg_ep), ("cp", leg_cp), ("engine", leg_engine)):
+            torch.cuda.empty_cache()
+            try:
+                if name == "engine":
+                    legs[name] = leg(args, torch, dist, hk, world, rank, local, device, barrier, peak_hbm())
+                else:
+                    legs[name] = leg(args, torch, dist, hk, par, world, rank, device, stream, barrier, peak_hbm())
+            except Exception as e:  # noqa: BLE001 - a failed leg is reported, the headline stands
+                legs[name] = {"error": f"{type(e).__name__}: {e}"[:400]}
     total_tokens = T * world
     value = total_tokens * args.steps / (ms / 1e3)
     e2e_value = None if args.no_e2e else total_tokens * args.steps / (e2e_ms / 1e3)
@@ -765,6 +770,9 @@ def run_layer(args):
     elif args.workload == "mixed":
         line = _run_mixed(args, torch, dist, hk, ClockSampler, world, rank, local, device, stream, gen,
                           hbm_peak, peak_src, barrier)
+    elif args.workload == "step":
+        line = _run_step(args, torch, dist, hk, ClockSampler, world, rank, local, device, stream, gen,
+                         hbm_peak, peak_src, barrier)
     elif args.workload == "sample":
         line = _run_sample(args, torch, dist, hk, ClockSampler, world, rank, local, device, stream, gen,
                            hbm_peak, peak_src, barrier)
@@ -1229,6 +1237,167 @@ def _run_mixed(args, torch, dist, hk, ClockSampler, world, rank, local, device, 
     }
 
 
+def _run_step(args, torch, dist, hk, ClockSampler, world, rank, local, device, stream, gen, hbm_peak,
+              peak_src, barrier):
+    """--workload step: the four parts of the decode step on one token stream, configuration 3's
+    mixed batch (48 decode lanes at U[2K, 32K] + two 2048-row chunked-prefill segments, 4144 rows)
+    through one DeepSeek-V3-shaped layer in its absorbed MLA form: the FP8 q_a / kv_a / q_b
+    projections, the latent rows appended to the paged cache, tcgen05 MLA attention (causal
+    prefill rows), the FP8 o projection, then configuration 4's MoE layer on the same 4144 tokens
+    (router GEMM, sigmoid top-8 of 256 experts, permutation, grouped FP8 expert FFN, the shared
+    expert, combine).  Every part is timed with CUDA events on the launching stream; the line
+    gives the step's tokens/s and each part's share and roofline.  N > 1: independent replicas."""
+    from hyperkernel_b200 import workload as W
+
+    lay = W.config3_attn_layout(seed=0)
+    T, Hh = lay.num_tokens, HEADS
+    HID, QL, E, K, I = 7168, 1536, MOE_E, MOE_K, MOE_I
+    projs = {"q_a": (QL, HID), "kv_a": (DK, HID), "q_b": (Hh * DK, QL), "o": (HID, Hh * DV), "router": (E, HID)}
+    ws = {n: (_rand_e4m3(torch, (a, b), gen, device),
+              torch.rand(((a + 127) // 128, b // 128), generator=gen, device=device) * 2e-4 + 1e-4)
+          for n, (a, b) in projs.items()}
+    w13 = _rand_e4m3(torch, (E + 1, 2 * I, HID), gen, device)
+    w2 = _rand_e4m3(torch, (E + 1, HID, I), gen, device)
+    s13 = torch.rand((E + 1, 2 * I // 128, HID // 128), generator=gen, device=device) * 1e-3
+    s2 = torch.rand((E + 1, HID // 128, I // 128), generator=gen, device=device) * 1e-3
+    cache = torch.randn((lay.num_slots, DK), generator=gen, device=device).to(torch.bfloat16)
+    x = torch.randn((T, HID), generator=gen, device=device).to(torch.bfloat16)
+    lane_tokens = torch.from_numpy(lay.new_rows.astype(np.int32)).to(device)
+    lane_pos = torch.from_numpy(lay.context.astype(np.int32)).to(device)
+    bt = torch.from_numpy(lay.block_table).to(device)
+    max_kv = int(lay.kv_len.max())
+    scale = 1.0 / math.sqrt(DK)
+    attn_ws = torch.empty(max(hk.mla_workspace_size(lay.lanes, T, Hh, max_kv), 16), dtype=torch.uint8, device=device)
+    o = torch.empty((T, Hh, DV), dtype=torch.bfloat16, device=device)
+    lse = torch.empty((T, Hh), dtype=torch.float32, device=device)
+    moe_ws = torch.empty(hk.moe_workspace_size(T * K, HID, I), dtype=torch.uint8, device=device)
+    ym = torch.empty((T * K, HID), dtype=torch.bfloat16, device=device)
+    ys = torch.empty((T, HID), dtype=torch.bfloat16, device=device)
+    every = torch.arange(T, dtype=torch.int32, device=device)
+    sh_off = torch.tensor([0, T], dtype=torch.int32, device=device)
+    parts = ["projections in (q_a, kv_a, q_b)", "KV append", "attention", "o projection", "MoE layer"]
+
+    def lin(aq, name):
+        w, sw = ws[name]
+        return hk.gemm_fp8(aq[0], aq[1], w, sw)
+
+    def step(ev=None, x_in=None):
+        xx = x if x_in is None else x_in
+        mark = (lambda i: ev[i].record(stream)) if ev is not None else (lambda i: None)
+        mark(0)
+        xq = hk.quant_fp8(xx)
+        qa = lin(xq, "q_a")
+        kv = lin(xq, "kv_a")
+        q = lin(hk.quant_fp8(qa), "q_b")
+        mark(1)
+        pk = hk.pack(lane_tokens, lane_pos, bt, PAGE, lay.num_pages, T)
+        hk.kv_append_bf16(kv, pk["slot_mapping"], cache)
+        mark(2)
+        hk.mla_decode(q.view(T, Hh, DK), cache, bt, pk["cu_seqlens"], pk["positions"], PAGE, max_kv, scale, out=o,
+                      lse=lse, workspace=attn_ws)
+        mark(3)
+        y = lin(hk.quant_fp8(o.view(T, Hh * DV)), "o")
+        mark(4)
+        hq, hs = hk.quant_fp8(y)
+        logits = lin((hq, hs), "router").float()
+        ids, wt = hk.route(logits, None, K, 2.5)
+        off, tok, pw, inv = hk.permute(ids, wt, E)
+        hk.moe_grouped(hq, hs, off, tok, T * K, HID, I, w13[:E], s13[:E], w2[:E], s2[:E], out=ym, workspace=moe_ws)
+        hk.moe_grouped(hq, hs, sh_off, every, T, HID, I, w13[E:], s13[E:], w2[E:], s2[E:], out=ys, workspace=moe_ws)
+        out = hk.combine(ym, pw, inv, ys, T, K)
+        mark(5)
+        return out, off
+
+    for _ in range(args.warmup):
+        _, off = step()
+    torch.cuda.synchronize()
+    hk.check_errors()
+    counts = (off[1:] - off[:-1]).cpu().numpy()
+    hit = int((counts > 0).sum())
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(args.steps)]
+    sampler = ClockSampler(local).start()
+    launches0 = hk.kernel_launches()
+    barrier()
+    t0 = time.perf_counter()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for i in range(args.steps):
+        step(evs[i])
+    end.record(stream)
+    torch.cuda.synchronize()
+    t1 = time.perf_counter()
+    barrier()
+    launches = hk.kernel_launches() - launches0
+    sampler.stop()
+    hk.check_errors()
+    ms = start.elapsed_time(end)
+    part_ms = [float(np.mean([e[j].elapsed_time(e[j + 1]) for e in evs])) for j in range(5)]
+    vals = _reduce_max(torch, dist, world, device, ms, *part_ms)
+    ms, part_ms = vals[0], list(vals[1:])
+    hx = torch.empty(x.shape, dtype=x.dtype).pin_memory().copy_(x.cpu())
+    hout = torch.empty((T, HID), dtype=torch.bfloat16).pin_memory()
+    dx = torch.empty_like(x)
+
+    def e2e(ev):
+        dx.copy_(hx, non_blocking=True)
+        out, _ = step(None, dx)
+        hout.copy_(out, non_blocking=True)
+
+    barrier()
+    e2e_ms, _ = _timed(torch, e2e, args.steps, stream, inner=False)
+    (e2e_ms,) = _reduce_max(torch, dist, world, device, e2e_ms)
+    hbm, fp8_peak, _ = _peaks()
+    bf16_peak = fp8_peak / 2
+    proj_in_flops = 2 * T * (QL * HID + DK * HID + Hh * DK * QL)
+    attn_flops = 2 * Hh * (DK + DV) * _query_kv_pairs(lay)
+    o_flops = 2 * T * HID * Hh * DV
+    wbytes = (hit + 1) * 3 * HID * I + E * HID
+    moe_bytes = wbytes + T * (K + 1) * (HID + 2 * 2 * I + 2 * HID)
+    kv_bytes = T * DK * 2 * 2
+    moe_flops = 2 * T * (K + 1) * 3 * HID * I + 2 * T * E * HID
+    step_ms = ms / args.steps
+    shares = {
+        parts[0]: {"ms": part_ms[0], "share": part_ms[0] / step_ms, "tflops": proj_in_flops / part_ms[0] / 1e9,
+                   "frac_of_fp8_peak": proj_in_flops / part_ms[0] / 1e9 / fp8_peak},
+        parts[1]: {"ms": part_ms[1], "share": part_ms[1] / step_ms, "gbs": kv_bytes / part_ms[1] / 1e6,
+                   "note": "includes hk_pack"},
+        parts[2]: {"ms": part_ms[2], "share": part_ms[2] / step_ms, "tflops": attn_flops / part_ms[2] / 1e9,
+                   "frac_of_bf16_peak": attn_flops / part_ms[2] / 1e9 / bf16_peak},
+        parts[3]: {"ms": part_ms[3], "share": part_ms[3] / step_ms, "tflops": o_flops / part_ms[3] / 1e9,
+                   "frac_of_fp8_peak": o_flops / part_ms[3] / 1e9 / fp8_peak},
+        parts[4]: {"ms": part_ms[4], "share": part_ms[4] / step_ms, "gbs": moe_bytes / part_ms[4] / 1e6,
+                   "frac_of_hbm": moe_bytes / part_ms[4] / 1e6 / hbm, "experts_hit": hit,
+                   "tflops": moe_flops / part_ms[4] / 1e9, "frac_of_fp8_peak": moe_flops / part_ms[4] / 1e9 / fp8_peak,
+                   "note": "4144 tokens x (8 routed + 1 shared) = 37,296 expert rows: at this batch the "
+                           "grouped FFN is closer to the tensor ridge than to the HBM bound"},
+    }
+    top = max(range(5), key=lambda j: part_ms[j])
+    return {
+        "metric": "decode step tokens/s, one layer (config 3 batch through projections, attention and MoE)",
+        "value": T * world * args.steps / (ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "e4m3 projections and experts, bf16 attention, fp32 accumulation",
+        "data": "synthetic (seeded)",
+        "config": {"workload": "config3 batch (48 decode lanes U[2K,32K] + 2 x 2048 prefill rows, 4144 tokens) "
+                               "through one DeepSeek-V3-shaped layer, absorbed MLA (q_b 1536->128x576, "
+                               "o 128x512->7168), then config 4's MoE (256 experts top-8 + shared, inter 2048)",
+                   "parallelism": f"replicas{world}" if world > 1 else "single",
+                   "l2": "11.3 GB of expert weights and ~1 GB of KV per step, no flush", "parts": shares},
+        "roofline": {"bound": "tensor" if top in (0, 2, 3) else "hbm",
+                     "achieved": shares[parts[top]].get("tflops", shares[parts[top]].get("gbs")),
+                     "peak": (fp8_peak if top in (0, 3) else bf16_peak) if top in (0, 2, 3) else hbm,
+                     "unit": "TFLOP/s" if top in (0, 2, 3) else "GB/s",
+                     "frac": shares[parts[top]].get("frac_of_fp8_peak", shares[parts[top]].get(
+                         "frac_of_bf16_peak", shares[parts[top]].get("frac_of_hbm"))),
+                     "traffic": None, "kernel": f"the step's largest part: {parts[top]}", "kernel_ms": part_ms[top],
+                     "peak_source": peak_src},
+        "cpu_baseline": None,
+        "e2e": {"value": T * world * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(x.numel() * 2), "d2h_bytes_per_step": int(T * HID * 2)},
+        "gpu_launches": int(launches), "clocks": sampler.summary(t0, t1),
+    }
+
+
 SAMPLE_VOCAB = 129280
 SAMPLE_LANES, SAMPLE_BLOCK, SAMPLE_LOGPROBS = 8, 5, 20
 SAMPLE_MIX = [dict(temperature=0.0, top_k=0, top_p=1.0), dict(temperature=0.7, top_k=50, top_p=1.0),
@@ -1371,12 +1540,17 @@ def leg_engine(args, torch, dist, hk, world, rank, local, device, barrier, hbm_p
     from hyperkernel_b200 import engine as H
 
     dims = dict(ENGINE_DIMS)
+    # an engine's step clock starts at 0, so every session gets a freshly opened device
+    for _ in range(max(1, min(args.warmup, 2))):
+        dev = _engine_device(H, local, dims)
+        try:
+            _engine_session(H, dev, _engine_requests(8, 5), dims["logprobs"])
+        finally:
+            dev.close()
+    requests = _engine_requests(ENGINE_REQUESTS, 11 + rank)
     l0 = hk.kernel_launches()
     dev = _engine_device(H, local, dims)
     try:
-        for _ in range(max(1, min(args.warmup, 2))):
-            _engine_session(H, dev, _engine_requests(8, 5), dims["logprobs"])
-        requests = _engine_requests(ENGINE_REQUESTS, 11 + rank)
         barrier()
         l1 = hk.kernel_launches()
         dt, iters, tokens, prompt_tokens = _engine_session(H, dev, requests, dims["logprobs"])
