@@ -275,6 +275,8 @@ def main(argv=None):
                     help="longctx: convert the whole FP8 pool to bf16 every step (no mirror)")
     ap.add_argument("--ep", default="peer", choices=["peer", "nccl"],
                     help="expert-parallel exchange: NVLink stores from libhk kernels, or NCCL all-to-allv")
+    ap.add_argument("--engine-requests", type=int, default=None,
+                    help="profiling override of the engine workload's 128 requests")
     ap.add_argument("--cp", default="peer", choices=["peer", "nccl"],
                     help="context-parallel exchange: hk_cp_merge over peer memory, or NCCL all-gather + merge")
     args = ap.parse_args(argv)
@@ -1547,7 +1549,7 @@ def leg_engine(args, torch, dist, hk, world, rank, local, device, barrier, hbm_p
             _engine_session(H, dev, _engine_requests(8, 5), dims["logprobs"])
         finally:
             dev.close()
-    requests = _engine_requests(ENGINE_REQUESTS, 11 + rank)
+    requests = _engine_requests(args.engine_requests or ENGINE_REQUESTS, 11 + rank)
     l0 = hk.kernel_launches()
     dev = _engine_device(H, local, dims)
     try:
@@ -1566,7 +1568,7 @@ def leg_engine(args, torch, dist, hk, world, rank, local, device, barrier, hbm_p
     hit = E * (1 - (1 - 1 / E) ** (ENGINE_LANES * K))
     wbytes = (hit + 1) * 3 * H_ * I + QL * H_ + 128 * 576 * QL + 576 * H_ + H_ * 128 * 512 + E * H_ + V * H_
     return {
-        "workload": f"HK_MODEL_MLA behind hk_push/hk_drain driven by hk_engine_run: {ENGINE_REQUESTS} requests, "
+        "workload": f"HK_MODEL_MLA behind hk_push/hk_drain driven by hk_engine_run: {len(requests)} requests, "
                     f"prompts U[{ENGINE_PROMPT[0]},{ENGINE_PROMPT[1]}), {ENGINE_LIMIT} tokens each, {ENGINE_LANES} "
                     "lanes, 1 DeepSeek-V3-shaped layer (hidden 7168, MLA 128 heads 512+64, FP8 projections, 256+1 "
                     "experts top-8, inter 2048), vocabulary 129280, greedy with 20 logprob pairs per token",

@@ -155,6 +155,8 @@ int hk_gemm_fp8(const uint8_t* xq, const float* sx, const uint8_t* wq, const flo
   if (m == 0) return HK_OK;
   if (hk::gemm_fp8_sm100_supported(m, n, k))
     return hk::gemm_fp8_sm100(xq, sx, wq, sw, m, n, k, y, (cudaStream_t)stream);
+  if (hk::gemm_fp8_swapab_supported(m, n, k))
+    return hk::gemm_fp8_swapab(xq, sx, wq, sw, m, n, k, y, (cudaStream_t)stream);
   return hk::gemm_fp8_portable(xq, sx, wq, sw, m, n, k, y, (cudaStream_t)stream);
 }
 

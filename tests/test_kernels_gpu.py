@@ -385,8 +385,13 @@ def test_quant_fp8_bit_exact(hk, orc, cuda, rows, k):
 
 
 @pytest.mark.parametrize("m,n,k", [(300, 512, 1024), (640, 1536, 1792), (7, 128, 256), (200, 768, 640),
-                                   (333, 400, 384), (4096, 2560, 256), (1024, 576, 2048)])
+                                   (333, 400, 384), (4096, 2560, 256), (1024, 576, 2048),
+                                   (64, 7168, 8192), (1, 576, 1024), (100, 1536, 2048), (50, 400, 384),
+                                   (127, 256, 128)])
 def test_gemm_fp8_matches_oracle(hk, orc, cuda, m, n, k):
+    """m >= 256: the SM-pair kernel; 128 <= m < 256: the one-SM kernel; m < 128: the swap-AB
+    kernel (weights on the MMA's M side; n not a multiple of 128 leaves a partial weight
+    block, m above 64 two token tiles)."""
     rng = W.Rng(41)
     x = W.f32_to_bf16_bits(rng.normal(m * k).astype(np.float32)).reshape(m, k)
     wf = (rng.normal(n * k) * 0.02).astype(np.float32).reshape(n, k)
