@@ -275,6 +275,8 @@ def main(argv=None):
                     help="longctx: convert the whole FP8 pool to bf16 every step (no mirror)")
     ap.add_argument("--ep", default="peer", choices=["peer", "nccl"],
                     help="expert-parallel exchange: NVLink stores from libhk kernels, or NCCL all-to-allv")
+    ap.add_argument("--step-batch", default="mixed", choices=["mixed", "decode"],
+                    help="--workload step: config 3's mixed batch or config 2's 64 decode lanes")
     ap.add_argument("--engine-requests", type=int, default=None,
                     help="profiling override of the engine workload's 128 requests")
     ap.add_argument("--cp", default="peer", choices=["peer", "nccl"],
@@ -1251,7 +1253,9 @@ def _run_step(args, torch, dist, hk, ClockSampler, world, rank, local, device, s
     gives the step's tokens/s and each part's share and roofline.  N > 1: independent replicas."""
     from hyperkernel_b200 import workload as W
 
-    lay = W.config3_attn_layout(seed=0)
+    # --step-batch decode: configuration 2's 64 decode lanes (one row each, contexts log-uniform
+    # in [1K, 128K]) through the same layer: the decode-sized step
+    lay = W.config2_layout(seed=0) if args.step_batch == "decode" else W.config3_attn_layout(seed=0)
     T, Hh = lay.num_tokens, HEADS
     HID, QL, E, K, I = 7168, 1536, MOE_E, MOE_K, MOE_I
     projs = {"q_a": (QL, HID), "kv_a": (DK, HID), "q_b": (Hh * DK, QL), "o": (HID, Hh * DV), "router": (E, HID)}
@@ -1370,28 +1374,36 @@ def _run_step(args, torch, dist, hk, ClockSampler, world, rank, local, device, s
         parts[4]: {"ms": part_ms[4], "share": part_ms[4] / step_ms, "gbs": moe_bytes / part_ms[4] / 1e6,
                    "frac_of_hbm": moe_bytes / part_ms[4] / 1e6 / hbm, "experts_hit": hit,
                    "tflops": moe_flops / part_ms[4] / 1e9, "frac_of_fp8_peak": moe_flops / part_ms[4] / 1e9 / fp8_peak,
-                   "note": "4144 tokens x (8 routed + 1 shared) = 37,296 expert rows: at this batch the "
-                           "grouped FFN is closer to the tensor ridge than to the HBM bound"},
+                   "note": f"{T} tokens x (8 routed + 1 shared) = {T * (K + 1)} expert rows"},
     }
     top = max(range(5), key=lambda j: part_ms[j])
+    # the MoE part is HBM-bound at decode batches (64 rows: ~1 flop per weight byte per row) and
+    # leans towards the tensor ridge at the 4144-row mixed batch; the dense parts are tensor work
+    moe_bound = "tensor" if args.step_batch != "decode" else "hbm"
+    top_bound = "tensor" if top in (0, 2, 3) or (top == 4 and moe_bound == "tensor") else "hbm"
+    top_part = shares[parts[top]]
+    if top_bound == "hbm":
+        top_ach, top_peak, top_unit = top_part["gbs"], hbm, "GB/s"
+    else:
+        top_ach = top_part["tflops"]
+        top_peak, top_unit = (bf16_peak if top == 2 else fp8_peak), "TFLOP/s"
     return {
-        "metric": "decode step tokens/s, one layer (config 3 batch through projections, attention and MoE)",
+        "metric": "decode step tokens/s, one layer (" + ("config 2" if args.step_batch == "decode" else "config 3") +
+                  " batch through projections, attention and MoE)",
         "value": T * world * args.steps / (ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "e4m3 projections and experts, bf16 attention, fp32 accumulation",
         "data": "synthetic (seeded)",
-        "config": {"workload": "config3 batch (48 decode lanes U[2K,32K] + 2 x 2048 prefill rows, 4144 tokens) "
-                               "through one DeepSeek-V3-shaped layer, absorbed MLA (q_b 1536->128x576, "
-                               "o 128x512->7168), then config 4's MoE (256 experts top-8 + shared, inter 2048)",
+        "config": {"workload": (("config3 batch (48 decode lanes U[2K,32K] + 2 x 2048 prefill rows, 4144 tokens)"
+                                 if args.step_batch != "decode" else
+                                 "config2 batch (64 decode lanes, ctx log-uniform [1K,128K], 64 tokens)") +
+                                " through one DeepSeek-V3-shaped layer, absorbed MLA (q_b 1536->128x576, "
+                                "o 128x512->7168), then config 4's MoE (256 experts top-8 + shared, inter 2048)"),
                    "parallelism": f"replicas{world}" if world > 1 else "single",
                    "l2": "11.3 GB of expert weights and ~1 GB of KV per step, no flush", "parts": shares},
-        "roofline": {"bound": "tensor" if top in (0, 2, 3) else "hbm",
-                     "achieved": shares[parts[top]].get("tflops", shares[parts[top]].get("gbs")),
-                     "peak": (fp8_peak if top in (0, 3) else bf16_peak) if top in (0, 2, 3) else hbm,
-                     "unit": "TFLOP/s" if top in (0, 2, 3) else "GB/s",
-                     "frac": shares[parts[top]].get("frac_of_fp8_peak", shares[parts[top]].get(
-                         "frac_of_bf16_peak", shares[parts[top]].get("frac_of_hbm"))),
-                     "traffic": None, "kernel": f"the step's largest part: {parts[top]}", "kernel_ms": part_ms[top],
+        "roofline": {"bound": top_bound, "achieved": top_ach, "peak": top_peak, "unit": top_unit,
+                     "frac": top_ach / top_peak, "traffic": None,
+                     "kernel": f"the step's largest part: {parts[top]}", "kernel_ms": part_ms[top],
                      "peak_source": peak_src},
         "cpu_baseline": None,
         "e2e": {"value": T * world * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",

@@ -4,18 +4,30 @@
 // A decode step's projections multiply a handful of token rows (one per live lane, or 1 + drafts)
 // by a large weight matrix, so the weights are the operand that matters and the GEMM is
 // HBM-bound on them (2 m flops per weight byte, far below the FP8 ridge).  The weights take the
-// MMA's M side (128 weight rows = one 128x128 scale block row) and a tile of up to 64 token rows
-// the N side: D[128 weight rows][64 tokens] = W[rows][kb] . X[tokens][kb]^T per 128-wide K block
-// (tcgen05 kind::f8f6f4, M 128, N 64, four K-32 instructions), into one of four TMEM buffers.
-// Promotion warps add D * sw[row block][kb] * sx[token][kb] in fp32 registers, the DeepSeek-style
-// scale rule the one- and two-SM kernels apply, and write y[token][weight row] as bf16 at the end.
+// MMA's M side and a tile of up to 64 token rows the N side: per 128-wide K block,
+// D[128 weight rows][64 tokens] = W[rows][kb] . X[tokens][kb]^T (tcgen05 kind::f8f6f4, M 128,
+// N 64, four K-32 instructions) for two 128-row weight blocks side by side in one of four TMEM
+// buffers.  Promotion warps add D * sw[row block][kb] * sx[token][kb] in fp32 registers, the
+// DeepSeek-style scale rule of the one- and two-SM kernels, and write y[token][weight row] as
+// bf16 at the end of the unit.
 //
-// Work unit = (128-row weight block, 64-row token tile), so each weight byte is read once per
-// token tile (once in all for m <= 64).  Roles per CTA (10 warps): warp 0 TMA producer, warp 1
-// TMEM owner and MMA issuer, warps 2..9 promotion (two per TMEM lane quarter, 32 token columns
-// each; thread = weight row).  Persistent over the units; every wait is bounded (1 s) and
-// records the error word; copies and MMAs in flight are drained before exit.
+// Work unit = (64-row token tile, 256 weight rows = two scale-block rows), so each weight byte
+// is read once per token tile (once in all for m <= 64), and the token tile (8 KB) is re-read once
+// per 32 KB of weights.  Small-n, long-K shapes (the o projection: 7168 x 65536 has 28 units)
+// would leave most SMs idle, so their K range is split into up to 4 parts: each work item writes
+// its fp32 partial to a stream-ordered scratch (from a memory pool of this library's own, on the
+// call's stream), and a second kernel adds the parts in a fixed order and writes y
+// (deterministic).
+//
+// Roles per CTA (10 warps): warp 0 TMA producer, warp 1 TMEM owner and MMA issuer, warps 2..9
+// promotion (two per TMEM lane quarter, 32 token columns each; thread = one row of each weight
+// block).  The activation scales of the tile are staged in shared memory 64 K blocks at a time
+// by the promotion warps.  Persistent over the units; every wait is bounded (1 s) and records
+// the error word; copies and MMAs in flight are drained before exit.
 #include <cuda.h>
+
+#include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 #include "gemm_fp8.cuh"
@@ -26,45 +38,61 @@ namespace {
 using namespace hk::sm100;
 
 constexpr int kTok = 64;     // token rows per unit: the MMA's N
-constexpr int kWRows = 128;  // weight rows per unit: the MMA's M
+constexpr int kWRows = 128;  // rows of one weight block: the MMA's M
 constexpr int kBK = 128;
 constexpr int kThreads = 320;
+constexpr int kPromo = 256;  // promotion threads (warps 2..9)
 constexpr int kCols = 32;    // token columns per promotion warp
 constexpr int kWBytes = kWRows * kBK;  // 16 KB
 constexpr int kXBytes = kTok * kBK;    // 8 KB
-constexpr int kStageBytes = kWBytes + kXBytes;
-constexpr int kStages = 8;
+constexpr int kStageBytes = 2 * kWBytes + kXBytes;  // 40 KB
+constexpr int kStages = 5;
 constexpr int kTBufs = 4;
-constexpr uint32_t kTmemCols = kTBufs * kTok;  // 256
+constexpr uint32_t kTmemCols = kTBufs * 2 * kTok;  // 512
 constexpr uint32_t kIdesc = idesc_e4m3(kWRows, kTok);
 constexpr unsigned long long kDrainNs = 1000000000ull;
+constexpr int kChunk = 64;  // K blocks of activation scales staged at a time
 
-constexpr int kOffCtl = kStages * kStageBytes;
-constexpr int kBarFull = 0;     // [kStages]
-constexpr int kBarEmpty = 64;   // [kStages]
-constexpr int kBarTFull = 128;  // [kTBufs]
-constexpr int kBarTEmpty = 160; // [kTBufs]
-constexpr int kTmemSlot = 192;
-constexpr int kAbort = 196;
+constexpr int kOffScales = kStages * kStageBytes;  // [kTok][kChunk] floats
+constexpr int kOffCtl = kOffScales + kTok * kChunk * 4;
+constexpr int kBarFull = 0;      // [kStages]
+constexpr int kBarEmpty = 64;    // [kStages]
+constexpr int kBarTFull = 128;   // [kTBufs]
+constexpr int kBarTEmpty = 160;  // [kTBufs]
+constexpr int kTmemSlot = 208;
+constexpr int kAbort = 212;
 constexpr int kCtlBytes = 256;
 constexpr int kSmem = kOffCtl + kCtlBytes;
 static_assert(kSmem <= 232448, "shared memory budget");
-static_assert(kStageBytes % 1024 == 0 && kWBytes % 1024 == 0, "128-byte swizzle atoms stay aligned");
+static_assert(kStageBytes % 1024 == 0 && kWBytes % 1024 == 0 && kOffScales % 1024 == 0, "swizzle atoms aligned");
 
 struct Params {
   const float* sx;  // [m][kblocks]
   const float* sw;  // [ceil(n/128)][kblocks]
-  uint16_t* y;      // [m][n]
+  uint16_t* y;      // [m][n] (split == 1)
+  float* part;      // [split][m][n] fp32 partials (split > 1)
   int64_t m;
-  int32_t n, kblocks, wblocks, tiles;
+  int32_t n, kblocks, wblocks, pairs, tiles, split;
   unsigned long long* err;
 };
+
+// Named barrier over the promotion threads that also ANDs a predicate across them.
+__device__ __forceinline__ bool promo_and(bool v) {
+  int out;
+  asm volatile(
+      "{\n.reg .pred p, q;\nsetp.ne.b32 p, %1, 0;\nbar.red.and.pred q, 1, 256, p;\nselp.s32 %0, 1, 0, q;\n}"
+      : "=r"(out)
+      : "r"((int)v)
+      : "memory");
+  return out != 0;
+}
 
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_fp8_swapab_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
                            Params p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t* ctl = smem + kOffCtl;
+  float* scales = reinterpret_cast<float*>(smem + kOffScales);  // [kTok][kChunk]
   const uint32_t ctl_u = smem_u32(ctl);
   volatile int* abort = reinterpret_cast<volatile int*>(ctl + kAbort);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -89,15 +117,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(ctl + kTmemSlot);
-  const int units = p.wblocks * p.tiles;
+  // work item w = (unit w / split, K part w % split); unit = (pair of weight blocks, token tile)
+  const int items = p.pairs * p.tiles * p.split;
 
   if (warp == 0) {
     if (lane == 0) {
       int g = 0;
       bool ok = true;
-      for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
-        const int wb = u % p.wblocks, tile = u / p.wblocks;
-        for (int kb = 0; kb < p.kblocks; ++kb) {
+      for (int w = blockIdx.x; ok && w < items; w += gridDim.x) {
+        const int u = w / p.split, ks = w % p.split;
+        const int pr = u % p.pairs, tile = u / p.pairs;
+        const int kb0 = (int)((int64_t)p.kblocks * ks / p.split), kb1 = (int)((int64_t)p.kblocks * (ks + 1) / p.split);
+        for (int kb = kb0; kb < kb1; ++kb) {
           const int s = g % kStages, fill = g / kStages;
           if (fill > 0 && !mbar_wait(ctl_u + kBarEmpty + 8 * s, (fill - 1) & 1, abort, p.err, 951)) {
             ok = false;
@@ -106,13 +137,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t dst = smem_u32(smem + s * kStageBytes);
           const uint32_t full = ctl_u + kBarFull + 8 * s;
           mbar_expect_tx(full, kStageBytes);
-          tma_load_2d(dst, &wmap, full, kb * kBK, wb * kWRows);
-          tma_load_2d(dst + kWBytes, &xmap, full, kb * kBK, tile * kTok);
+          tma_load_2d(dst, &wmap, full, kb * kBK, pr * 2 * kWRows);
+          tma_load_2d(dst + kWBytes, &wmap, full, kb * kBK, pr * 2 * kWRows + kWRows);
+          tma_load_2d(dst + 2 * kWBytes, &xmap, full, kb * kBK, tile * kTok);
           ++g;
         }
       }
-      // drain: the copies still in flight complete before the CTA exits
-      for (int i = g > kStages ? g - kStages : 0; i < g; ++i) {
+      for (int i = g > kStages ? g - kStages : 0; i < g; ++i) {  // copies in flight complete first
         const int s = i % kStages, fill = i / kStages;
         const unsigned long long t0 = globaltimer();
         while (!mbar_try_wait(ctl_u + kBarFull + 8 * s, fill & 1) && globaltimer() - t0 < kDrainNs) {
@@ -123,8 +154,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int g = 0;
       bool ok = true;
-      for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
-        for (int kb = 0; kb < p.kblocks; ++kb) {
+      for (int w = blockIdx.x; ok && w < items; w += gridDim.x) {
+        const int ks = w % p.split;
+        const int kb0 = (int)((int64_t)p.kblocks * ks / p.split), kb1 = (int)((int64_t)p.kblocks * (ks + 1) / p.split);
+        for (int kb = kb0; kb < kb1; ++kb) {
           const int s = g % kStages, fill = g / kStages, buf = g % kTBufs, use = g / kTBufs;
           if (!mbar_wait(ctl_u + kBarFull + 8 * s, fill & 1, abort, p.err, 952) ||
               (use > 0 && !mbar_wait(ctl_u + kBarTEmpty + 8 * buf, (use - 1) & 1, abort, p.err, 953))) {
@@ -133,12 +166,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
           const uint32_t a = smem_u32(smem + s * kStageBytes);
-          const uint32_t x = a + kWBytes;
-          const uint32_t d = tmem + (uint32_t)(buf * kTok);
+          const uint32_t x = a + 2 * kWBytes;
+          const uint32_t d = tmem + (uint32_t)(buf * 2 * kTok);
 #pragma unroll
-          for (int kk = 0; kk < kBK / 32; ++kk)
-            umma_f8(d, sdesc_sw128(a + 32 * kk, 16, 1024), sdesc_sw128(x + 32 * kk, 16, 1024), kIdesc,
-                    kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < kBK / 32; ++kk) {
+            const uint64_t bdesc = sdesc_sw128(x + 32 * kk, 16, 1024);
+            umma_f8(d, sdesc_sw128(a + 32 * kk, 16, 1024), bdesc, kIdesc, kk > 0 ? 1u : 0u);
+            umma_f8(d + kTok, sdesc_sw128(a + kWBytes + 32 * kk, 16, 1024), bdesc, kIdesc, kk > 0 ? 1u : 0u);
+          }
           umma_commit(ctl_u + kBarEmpty + 8 * s);
           umma_commit(ctl_u + kBarTFull + 8 * buf);
           ++g;
@@ -155,17 +190,33 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     const int q = warp & 3;            // TMEM lane quarter
     const int half = (warp - 2) >> 2;  // token columns [half * 32, half * 32 + 32)
-    const int r = q * 32 + lane;       // weight row inside the unit's 128-row block
+    const int r = q * 32 + lane;       // row inside each of the unit's two 128-row weight blocks
+    const int et = threadIdx.x - 64;   // 0..255 among the promotion threads
     int g = 0;
     bool live = true;
-    for (int u = blockIdx.x; live && u < units; u += gridDim.x) {
-      const int wb = u % p.wblocks, tile = u / p.wblocks;
-      const int64_t t0 = (int64_t)tile * kTok + half * kCols;  // this warp's first token row
-      float acc[kCols];
+    for (int w = blockIdx.x; live && w < items; w += gridDim.x) {
+      const int u = w / p.split, ks = w % p.split;
+      const int pr = u % p.pairs, tile = u / p.pairs;
+      const int kb0 = (int)((int64_t)p.kblocks * ks / p.split), kb1 = (int)((int64_t)p.kblocks * (ks + 1) / p.split);
+      const int64_t tok0 = (int64_t)tile * kTok;
+      const bool second = 2 * pr + 1 < p.wblocks;
+      const float* swa = p.sw + (int64_t)(2 * pr) * p.kblocks;
+      const float* swb = second ? swa + p.kblocks : swa;
+      float acc_a[kCols], acc_b[kCols];
 #pragma unroll
-      for (int i = 0; i < kCols; ++i) acc[i] = 0.f;
-      const float* swr = p.sw + (int64_t)wb * p.kblocks;
-      for (int kb = 0; kb < p.kblocks; ++kb, ++g) {
+      for (int i = 0; i < kCols; ++i) acc_a[i] = acc_b[i] = 0.f;
+      for (int kb = kb0; kb < kb1; ++kb, ++g) {
+        const int kl = (kb - kb0) % kChunk;
+        if (kl == 0) {  // stage the next chunk of the tile's activation scales, [token][kb]
+          if (!promo_and(live)) live = false;  // every promotion thread is past the previous chunk
+          for (int i = et; i < kTok * kChunk; i += kPromo) {
+            const int t = i / kChunk, c = i % kChunk;
+            const int64_t tt = tok0 + t;
+            const int kk = kb + c;
+            scales[t * kChunk + c] = (tt < p.m && kk < kb1) ? __ldg(p.sx + tt * p.kblocks + kk) : 0.f;
+          }
+          asm volatile("bar.sync 1, 256;" ::: "memory");
+        }
         if (!live) continue;
         const int buf = g % kTBufs, use = g / kTBufs;
         bool ok = true;
@@ -176,25 +227,38 @@ __global__ void __launch_bounds__(kThreads, 1)
           continue;
         }
         tc_fence_after();
-        float v[kCols];
-        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * kTok + half * kCols), v);
+        const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * 2 * kTok + half * kCols);
+        float va[kCols], vb[kCols];
+        tmem_ld32x2(base, base + kTok, va, vb);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(ctl_u + kBarTEmpty + 8 * buf);
-        const float s_w = __ldg(swr + kb);
+        const float sa = __ldg(swa + kb), sb = __ldg(swb + kb);
+        const float* sc = scales + (half * kCols) * kChunk + kl;
 #pragma unroll
         for (int i = 0; i < kCols; ++i) {
-          const int64_t t = t0 + i;
-          const float s_x = t < p.m ? __ldg(p.sx + t * p.kblocks + kb) : 0.f;
-          acc[i] = fmaf(v[i], s_x * s_w, acc[i]);
+          const float sv = sc[i * kChunk];
+          acc_a[i] = fmaf(va[i], sv * sa, acc_a[i]);
+          acc_b[i] = fmaf(vb[i], sv * sb, acc_b[i]);
         }
       }
-      const int64_t col = (int64_t)wb * kWRows + r;
-      if (live && col < p.n) {
+      if (!promo_and(live)) {  // the promotion threads leave together
+        live = false;
+        break;
+      }
+      const int64_t col_a = (int64_t)(2 * pr) * kWRows + r;
+      const int64_t col_b = col_a + kWRows;
 #pragma unroll
-        for (int i = 0; i < kCols; ++i) {
-          const int64_t t = t0 + i;
-          if (t < p.m) p.y[t * p.n + col] = f32_to_bf16_bits(acc[i]);
+      for (int i = 0; i < kCols; ++i) {
+        const int64_t t = tok0 + half * kCols + i;
+        if (t >= p.m) continue;
+        if (p.split == 1) {
+          if (col_a < p.n) p.y[t * p.n + col_a] = f32_to_bf16_bits(acc_a[i]);
+          if (second && col_b < p.n) p.y[t * p.n + col_b] = f32_to_bf16_bits(acc_b[i]);
+        } else {
+          float* pt = p.part + ((int64_t)ks * p.m + t) * p.n;
+          if (col_a < p.n) pt[col_a] = acc_a[i];
+          if (second && col_b < p.n) pt[col_b] = acc_b[i];
         }
       }
     }
@@ -205,6 +269,43 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
+}
+
+// y = bf16(sum over the split parts, in part order) of the fp32 partials.
+__global__ void reduce_parts_kernel(const float* __restrict__ part, int32_t split, int64_t count,
+                                    uint16_t* __restrict__ y) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x) {
+    float v = 0.f;
+    for (int s = 0; s < split; ++s) v += part[s * count + i];
+    y[i] = f32_to_bf16_bits(v);
+  }
+}
+
+// A memory pool of this library's own per device for the split-K scratch: stream-ordered
+// allocations that stay mapped between calls (the default pool hands memory back at every
+// synchronisation, which made each call re-map its scratch).
+constexpr int kMaxDevices = 64;
+cudaMemPool_t g_pool[kMaxDevices] = {};
+std::mutex g_pool_mu;
+
+int scratch_pool(cudaMemPool_t* out) {
+  int dev = -1;
+  HK_TRY_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return hk::fail(HK_ENODEV, "device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_pool_mu);
+  if (g_pool[dev] == nullptr) {
+    cudaMemPoolProps props = {};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = dev;
+    cudaMemPool_t pool = nullptr;
+    HK_TRY_CUDA(cudaMemPoolCreate(&pool, &props));
+    uint64_t keep = UINT64_MAX;
+    HK_TRY_CUDA(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep));
+    g_pool[dev] = pool;
+  }
+  *out = g_pool[dev];
+  return HK_OK;
 }
 
 }  // namespace
@@ -234,10 +335,35 @@ int gemm_fp8_swapab(const uint8_t* xq, const float* sx, const uint8_t* wq, const
   p.n = n;
   p.kblocks = k / kBK;
   p.wblocks = (n + kWRows - 1) / kWRows;
+  p.pairs = (p.wblocks + 1) / 2;
   p.tiles = (int32_t)((m + kTok - 1) / kTok);
   p.err = err_word();
-  const int units = p.wblocks * p.tiles;
-  const int grid = units < sm_count() ? units : sm_count();
+  const int units = p.pairs * p.tiles, sms = sm_count();
+  // split K when the units fill less than half the SMs and every part keeps >= 8 K blocks
+  p.split = 1;
+  while (p.split < 4 && units * p.split * 2 <= sms && p.kblocks >= 16 * p.split) p.split *= 2;
+  const int items = units * p.split;
+  const int grid = items < sms ? items : sms;
+  if (p.split > 1) {
+    const size_t bytes = sizeof(float) * (size_t)p.split * (size_t)m * (size_t)n;
+    cudaMemPool_t pool = nullptr;
+    HK_TRY(scratch_pool(&pool));
+    HK_TRY_CUDA(cudaMallocFromPoolAsync(reinterpret_cast<void**>(&p.part), bytes, pool, stream));
+    gemm_fp8_swapab_kernel<<<grid, kThreads, kSmem, stream>>>(wmap, xmap, p);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) {
+      note_launch();
+      const int64_t count = m * (int64_t)n;
+      reduce_parts_kernel<<<(unsigned)std::min<int64_t>((count + 255) / 256, 4 * sms), 256, 0, stream>>>(
+          p.part, p.split, count, y);
+      e = cudaGetLastError();
+      if (e == cudaSuccess) note_launch();
+    }
+    const cudaError_t f = cudaFreeAsync(p.part, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "gemm_fp8_swapab (split K)");
+    if (f != cudaSuccess) return cuda_fail(f, "cudaFreeAsync");
+    return HK_OK;
+  }
   gemm_fp8_swapab_kernel<<<grid, kThreads, kSmem, stream>>>(wmap, xmap, p);
   HK_TRY_LAUNCH("gemm_fp8_swapab_kernel");
   return HK_OK;

@@ -203,7 +203,9 @@ int hk_quant_fp8(const uint16_t* x, int64_t rows, int32_t k, uint8_t* xq, float*
 
 /* y[m][n] bf16 = sum over 128-blocks kb of (xq[m][kb] . wq[n][kb]) * sx[m][kb] * sw[n/128][kb]
  * with wq[n][k] e4m3 and sw[ceil(n/128)][k/128] fp32; fp32 accumulation.
- * k % 128 == 0, n % 16 == 0. */
+ * k % 128 == 0, n % 16 == 0.  Tensor-core kernels: m >= 256 SM pairs, 128 <= m < 256 one SM,
+ * m < 128 swap-AB (the weights on the MMA's M side); a long-K, small-n shape with m < 128 splits
+ * K and takes its fp32 partials from a stream-ordered memory pool the library keeps per device. */
 int hk_gemm_fp8(const uint8_t* xq, const float* sx, const uint8_t* wq, const float* sw,
                 int64_t m, int32_t n, int32_t k, uint16_t* y, void* stream);
 
