@@ -269,7 +269,8 @@ def main(argv=None):
     ap.add_argument("--no-legs", action="store_true",
                     help="skip the expert-parallel (config 4) and context-parallel (config 5) legs")
     ap.add_argument("--workload", default="decode",
-                    choices=["decode", "moe", "linear", "longctx", "sample", "mixed", "engine", "step"])
+                    choices=["decode", "moe", "linear", "linear-decode", "longctx", "sample", "mixed", "engine",
+                             "step"])
     ap.add_argument("--experts", type=int, default=None, help="profiling override of config 4's 256 experts")
     ap.add_argument("--full-dequant", action="store_true",
                     help="longctx: convert the whole FP8 pool to bf16 every step (no mirror)")
@@ -774,6 +775,9 @@ def run_layer(args):
     elif args.workload == "mixed":
         line = _run_mixed(args, torch, dist, hk, ClockSampler, world, rank, local, device, stream, gen,
                           hbm_peak, peak_src, barrier)
+    elif args.workload == "linear-decode":
+        line = _run_linear_decode(args, torch, dist, hk, ClockSampler, world, rank, local, device, stream, gen,
+                                  hbm_peak, peak_src, barrier)
     elif args.workload == "step":
         line = _run_step(args, torch, dist, hk, ClockSampler, world, rank, local, device, stream, gen,
                          hbm_peak, peak_src, barrier)
@@ -1138,6 +1142,81 @@ def _run_linear(args, torch, dist, hk, ClockSampler, world, rank, local, device,
                 "h2d_bytes_per_step": x.numel() * 2 + attn.numel() * 2,
                 "d2h_bytes_per_step": T * sum(n for nm, n, _ in LINEAR_PROJ if nm != "q_a") * 2},
         "gpu_launches": int(launches), "clocks": clocks,
+    }
+
+
+# The decode step's dense projections at a decode batch (64 rows: one per lane of config 2), in
+# their absorbed-MLA shapes, plus the vocabulary projection: (name, out features, in features).
+DECODE_PROJ = [("q_a", 1536, 7168), ("kv_a", 576, 7168), ("q_b", 128 * 576, 1536), ("o", 7168, 128 * 512),
+               ("vocab", 129280, 7168)]
+
+
+def _run_linear_decode(args, torch, dist, hk, ClockSampler, world, rank, local, device, stream, gen, hbm_peak,
+                       peak_src, barrier):
+    """--workload linear-decode: the FP8 projections of a decode step for 64 token rows (the
+    swap-AB kernel: weights on the MMA's M side, split K for the long-K o projection).  At 64 rows
+    a projection does 128 flops per weight byte, far below the FP8 ridge, so the bound is HBM:
+    `value` is weight bytes streamed per second.  N > 1: independent replicas."""
+    T = 64
+    ws = {name: (_rand_e4m3(torch, (n, k), gen, device),
+                 torch.rand(((n + 127) // 128, k // 128), generator=gen, device=device) * 1e-2)
+          for name, n, k in DECODE_PROJ}
+    xs = {name: hk.quant_fp8(torch.randn((T, k), generator=gen, device=device).to(torch.bfloat16))
+          for name, _n, k in DECODE_PROJ}
+    outs = {name: torch.empty((T, n), dtype=torch.bfloat16, device=device) for name, n, _k in DECODE_PROJ}
+    wbytes = {name: n * k for name, n, k in DECODE_PROJ}
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(len(DECODE_PROJ) + 1)] for _ in range(args.steps)]
+
+    def step(ev=None):
+        for j, (name, _n, _k) in enumerate(DECODE_PROJ):
+            if ev is not None:
+                ev[j].record(stream)
+            w, sw = ws[name]
+            hk.gemm_fp8(xs[name][0], xs[name][1], w, sw, out=outs[name])
+        if ev is not None:
+            ev[len(DECODE_PROJ)].record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    hk.check_errors()
+    sampler = ClockSampler(local).start()
+    launches0 = hk.kernel_launches()
+    barrier()
+    t0 = time.perf_counter()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for i in range(args.steps):
+        step(evs[i])
+    end.record(stream)
+    torch.cuda.synchronize()
+    t1 = time.perf_counter()
+    barrier()
+    launches = hk.kernel_launches() - launches0
+    sampler.stop()
+    hk.check_errors()
+    ms = start.elapsed_time(end)
+    per = [float(np.mean([e[j].elapsed_time(e[j + 1]) for e in evs])) for j in range(len(DECODE_PROJ))]
+    vals = _reduce_max(torch, dist, world, device, ms, *per)
+    ms, per = vals[0], list(vals[1:])
+    total_bytes = sum(wbytes.values())
+    gbs = total_bytes / (ms / args.steps) / 1e6
+    parts = {name: {"us": per[j] * 1e3, "weight_mb": wbytes[name] / 1e6, "gbs": wbytes[name] / per[j] / 1e6,
+                    "frac_of_hbm": wbytes[name] / per[j] / 1e6 / hbm_peak}
+             for j, (name, _n, _k) in enumerate(DECODE_PROJ)}
+    return {
+        "metric": "decode-batch FP8 projection weight GB/s (64 token rows)", "value": gbs * world,
+        "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "e4m3 x e4m3 -> f32", "data": "synthetic (seeded)",
+        "config": {"workload": "64 token rows through q_a 7168->1536, kv_a 7168->576, q_b 1536->128x576, "
+                               "o 128x512->7168, vocabulary 7168->129280 (1.53 GB of e4m3 weights per step)",
+                   "parallelism": f"replicas{world}" if world > 1 else "single",
+                   "l2": "1.5 GB of weights per step, larger than L2; no flush", "parts": parts},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
+                     "traffic": None, "kernel": "gemm_fp8_swapab_kernel (hk_gemm_fp8, m = 64)",
+                     "kernel_ms": ms / args.steps, "algorithmic_bytes": total_bytes, "peak_source": peak_src},
+        "cpu_baseline": None, "e2e": None, "gpu_launches": int(launches), "clocks": sampler.summary(t0, t1),
     }
 
 
