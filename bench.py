@@ -596,7 +596,9 @@ def leg_cp(args, torch, dist, hk, par, world, rank, device, stream, barrier, hbm
     max_kv = int(kv.max())
     scale = 1.0 / math.sqrt(DK)
     long_rows = int(lay.new_rows[0]) * H
-    kv_bf16 = torch.empty((lay.num_slots, DK), dtype=torch.bfloat16, device=device)
+    # zeroed: the tcgen05 kernel reads whole pages, the scratch page included, at zero weight, so the
+    # pages this rank does not convert must hold finite values
+    kv_bf16 = torch.zeros((lay.num_slots, DK), dtype=torch.bfloat16, device=device)
     my_pages = torch.from_numpy(np.concatenate(
         [lay.block_table[i, int(begin[i]) // PAGE:(int(end[i]) + PAGE - 1) // PAGE] for i in range(L)]
     ).astype(np.int32)).to(device)
@@ -952,7 +954,7 @@ def _run_longctx(args, torch, dist, hk, par, ClockSampler, world, rank, local, d
     long_rows = int(lay.new_rows[0]) * H
 
     portable = world > 1 and args.attn_impl == 1
-    kv_bf16 = None if portable else torch.empty((lay.num_slots, DK), dtype=torch.bfloat16, device=device)
+    kv_bf16 = None if portable else torch.zeros((lay.num_slots, DK), dtype=torch.bfloat16, device=device)
     # pages of this rank's ranges (the long lane's shard and its short lanes)
     my_pages = torch.from_numpy(np.concatenate(
         [lay.block_table[i, int(begin[i]) // PAGE:(int(end[i]) + PAGE - 1) // PAGE] for i in range(L)]
