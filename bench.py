@@ -1338,7 +1338,7 @@ def _run_step(args, torch, dist, hk, ClockSampler, world, rank, local, device, s
     # in [1K, 128K]) through the same layer: the decode-sized step
     lay = W.config2_layout(seed=0) if args.step_batch == "decode" else W.config3_attn_layout(seed=0)
     T, Hh = lay.num_tokens, HEADS
-    HID, QL, E, K, I = 7168, 1536, MOE_E, MOE_K, MOE_I
+    HID, QL, E, K, I = 7168, 1536, args.experts or MOE_E, MOE_K, MOE_I
     projs = {"q_a": (QL, HID), "kv_a": (DK, HID), "q_b": (Hh * DK, QL), "o": (HID, Hh * DV), "router": (E, HID)}
     ws = {n: (_rand_e4m3(torch, (a, b), gen, device),
               torch.rand(((a + 127) // 128, b // 128), generator=gen, device=device) * 2e-4 + 1e-4)
