@@ -808,31 +808,39 @@ def _run_moe(args, torch, dist, hk, par, ClockSampler, world, rank, local, devic
     T, E, H, I, K = MOE_T, args.experts or MOE_E, MOE_H, MOE_I, MOE_K
     e0, e1 = par.expert_range(E, world, rank)
     El = e1 - e0
-    w13 = _rand_e4m3(torch, (El, 2 * I, H), gen, device)
-    w2 = _rand_e4m3(torch, (El, H, I), gen, device)
-    s13 = torch.rand((El, 2 * I // 128, H // 128), generator=gen, device=device) * 1e-3
-    s2 = torch.rand((El, H // 128, I // 128), generator=gen, device=device) * 1e-3
-    sh13 = _rand_e4m3(torch, (1, 2 * I, H), gen, device)
-    sh2 = _rand_e4m3(torch, (1, H, I), gen, device)
-    shs13 = torch.rand((1, 2 * I // 128, H // 128), generator=gen, device=device) * 1e-3
-    shs2 = torch.rand((1, H // 128, I // 128), generator=gen, device=device) * 1e-3
+    # the local routed experts and then the shared one in one weight array each: on one GPU the
+    # shared expert runs as expert E of the routed grouped call (rows [T*K, T*K + T) = every
+    # token), as the model step behind hk_open_mla runs it
+    w13_all = _rand_e4m3(torch, (El + 1, 2 * I, H), gen, device)
+    w2_all = _rand_e4m3(torch, (El + 1, H, I), gen, device)
+    s13_all = torch.rand((El + 1, 2 * I // 128, H // 128), generator=gen, device=device) * 1e-3
+    s2_all = torch.rand((El + 1, H // 128, I // 128), generator=gen, device=device) * 1e-3
+    w13, w2, s13, s2 = w13_all[:El], w2_all[:El], s13_all[:El], s2_all[:El]
+    sh13, sh2, shs13, shs2 = w13_all[El:], w2_all[El:], s13_all[El:], s2_all[El:]
     x = torch.randn((T, H), generator=gen, device=device).to(torch.bfloat16)
     logits = torch.randn((T, E), generator=gen, device=device)
     rows = T * K
     rows_max = rows * world  # the most rows one rank's experts can receive
-    ws = torch.empty(hk.moe_workspace_size(rows_max, H, I), dtype=torch.uint8, device=device)
+    ws = torch.empty(hk.moe_workspace_size(rows_max + T, H, I), dtype=torch.uint8, device=device)
     ws_sh = torch.empty(hk.moe_workspace_size(T, H, I), dtype=torch.uint8, device=device)
-    y_buf = torch.empty((rows_max, H), dtype=torch.bfloat16, device=device)
+    y_buf = torch.empty((rows_max + T, H), dtype=torch.bfloat16, device=device)
     y_sh = torch.empty((T, H), dtype=torch.bfloat16, device=device)
     sh_off = torch.tensor([0, T], dtype=torch.int32, device=device)
     sh_tok = torch.arange(T, dtype=torch.int32, device=device)
+    off_ext = torch.empty(E + 2, dtype=torch.int32, device=device)
+    off_ext[E + 1] = rows + T
+    tok_ext = torch.empty(rows + T, dtype=torch.int32, device=device)
+    tok_ext[rows:] = sh_tok
     peer = par.EpPeer(E, T, K, H) if world > 1 and args.ep == "peer" else None
     info = {}
 
     def step(x_in, logits_in, ev=None):
         xq, sx = hk.quant_fp8(x_in)
         ids, w = hk.route(logits_in, None, K, 1.0)
-        off, tok, pw, inv = hk.permute(ids, w, E)
+        if world == 1:
+            off, tok, pw, inv = hk.permute(ids, w, E, offsets=off_ext[:E + 1], perm_token=tok_ext[:rows])
+        else:
+            off, tok, pw, inv = hk.permute(ids, w, E)
         if peer is not None:
             xr, sr, loff, lperm = peer.dispatch(xq, sx, off, tok)
             n_in = peer.rows_cap
@@ -843,9 +851,12 @@ def _run_moe(args, torch, dist, hk, par, ClockSampler, world, rank, local, devic
             ev[0].record(stream)
         if world > 1:
             y_local = hk.moe_grouped(xr, sr, loff, lperm, n_in, H, I, w13, s13, w2, s2, out=y_buf, workspace=ws)
+            shared = hk.moe_grouped(xq, sx, sh_off, sh_tok, T, H, I, sh13, shs13, sh2, shs2, out=y_sh,
+                                    workspace=ws_sh)
         else:
-            y_local = hk.moe_grouped(xq, sx, off, tok, rows, H, I, w13, s13, w2, s2, out=y_buf, workspace=ws)
-        hk.moe_grouped(xq, sx, sh_off, sh_tok, T, H, I, sh13, shs13, sh2, shs2, out=y_sh, workspace=ws_sh)
+            y_all = hk.moe_grouped(xq, sx, off_ext, tok_ext, rows + T, H, I, w13_all, s13_all, w2_all, s2_all,
+                                   out=y_buf, workspace=ws)
+            y_local, shared = y_all[:rows], y_all[rows:rows + T]
         if ev is not None:
             ev[1].record(stream)
         if peer is not None:
@@ -854,7 +865,7 @@ def _run_moe(args, torch, dist, hk, par, ClockSampler, world, rank, local, devic
             y = par.ep_return(y_local, plan, lperm)
         else:
             y = y_local
-        return hk.combine(y, pw, inv, y_sh, T, K), (loff if world > 1 else off)
+        return hk.combine(y, pw, inv, shared, T, K), (loff if world > 1 else off)
 
     for _ in range(args.warmup):
         _, off = step(x, logits)
@@ -1357,11 +1368,14 @@ def _run_step(args, torch, dist, hk, ClockSampler, world, rank, local, device, s
     attn_ws = torch.empty(max(hk.mla_workspace_size(lay.lanes, T, Hh, max_kv), 16), dtype=torch.uint8, device=device)
     o = torch.empty((T, Hh, DV), dtype=torch.bfloat16, device=device)
     lse = torch.empty((T, Hh), dtype=torch.float32, device=device)
-    moe_ws = torch.empty(hk.moe_workspace_size(T * K, HID, I), dtype=torch.uint8, device=device)
-    ym = torch.empty((T * K, HID), dtype=torch.bfloat16, device=device)
-    ys = torch.empty((T, HID), dtype=torch.bfloat16, device=device)
-    every = torch.arange(T, dtype=torch.int32, device=device)
-    sh_off = torch.tensor([0, T], dtype=torch.int32, device=device)
+    # the shared expert runs as expert E of the routed grouped call (its weights follow the routed
+    # ones), as the model step behind hk_open_mla runs it: rows [T*K, T*K + T) are every token
+    moe_ws = torch.empty(hk.moe_workspace_size(T * (K + 1), HID, I), dtype=torch.uint8, device=device)
+    ym = torch.empty((T * (K + 1), HID), dtype=torch.bfloat16, device=device)
+    off_ext = torch.empty(E + 2, dtype=torch.int32, device=device)
+    off_ext[E + 1] = T * (K + 1)
+    tok_ext = torch.empty(T * (K + 1), dtype=torch.int32, device=device)
+    tok_ext[T * K:] = torch.arange(T, dtype=torch.int32, device=device)
     parts = ["projections in (q_a, kv_a, q_b)", "KV append", "attention", "o projection", "MoE layer"]
 
     def lin(aq, name):
@@ -1388,10 +1402,9 @@ def _run_step(args, torch, dist, hk, ClockSampler, world, rank, local, device, s
         hq, hs = hk.quant_fp8(y)
         logits = lin((hq, hs), "router").float()
         ids, wt = hk.route(logits, None, K, 2.5)
-        off, tok, pw, inv = hk.permute(ids, wt, E)
-        hk.moe_grouped(hq, hs, off, tok, T * K, HID, I, w13[:E], s13[:E], w2[:E], s2[:E], out=ym, workspace=moe_ws)
-        hk.moe_grouped(hq, hs, sh_off, every, T, HID, I, w13[E:], s13[E:], w2[E:], s2[E:], out=ys, workspace=moe_ws)
-        out = hk.combine(ym, pw, inv, ys, T, K)
+        off, tok, pw, inv = hk.permute(ids, wt, E, offsets=off_ext[:E + 1], perm_token=tok_ext[:T * K])
+        hk.moe_grouped(hq, hs, off_ext, tok_ext, T * (K + 1), HID, I, w13, s13, w2, s2, out=ym, workspace=moe_ws)
+        out = hk.combine(ym[:T * K], pw, inv, ym[T * K:], T, K)
         mark(5)
         return out, off
 

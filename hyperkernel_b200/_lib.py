@@ -383,11 +383,17 @@ def route(logits, bias, top_k, route_scale, stream=None):
     return ids, w
 
 
-def permute(ids, weights, num_experts, stream=None):
+def permute(ids, weights, num_experts, stream=None, offsets=None, perm_token=None):
+    """`offsets` / `perm_token` may be given as contiguous views of larger buffers (the first
+    num_experts + 1 and T * K entries are written)."""
     T, K = ids.shape
     dev = ids.device
-    offsets = torch.empty(num_experts + 1, dtype=torch.int32, device=dev)
-    perm_token = torch.empty(max(T * K, 1), dtype=torch.int32, device=dev)
+    if offsets is None:
+        offsets = torch.empty(num_experts + 1, dtype=torch.int32, device=dev)
+    if perm_token is None:
+        perm_token = torch.empty(max(T * K, 1), dtype=torch.int32, device=dev)
+    if offsets.numel() < num_experts + 1 or perm_token.numel() < T * K:
+        raise ValueError("permute: output buffers too small")
     perm_weight = torch.empty(max(T * K, 1), dtype=torch.float32, device=dev)
     inv = torch.empty(max(T * K, 1), dtype=torch.int32, device=dev)
     call("hk_permute", ptr(ids), ptr(weights), T, K, num_experts, ptr(offsets), ptr(perm_token),

@@ -60,8 +60,16 @@ __global__ void fill_f32_kernel(float* p, int64_t n, float v) {
     p[i] = v;
 }
 
-__global__ void iota_kernel(int32_t* p, int32_t n) {
-  for (int32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) p[i] = i;
+// The shared expert as expert E of the routed grouped call: its rows are every token in order,
+// appended after the T*K permuted rows (perm_token[T*K + i] = i, offsets[E+1] = T*K + T), so
+// its weights stream in the same launch as the routed experts' instead of a launch of its own
+// that a decode batch's one row tile would spread over a tenth of the SMs.
+__global__ void shared_rows_kernel(int32_t* __restrict__ offsets, int32_t* __restrict__ perm_token, int32_t E,
+                                   int32_t T, int32_t K) {
+  const int64_t base = (int64_t)T * K;
+  for (int32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < T; i += gridDim.x * blockDim.x)
+    perm_token[base + i] = i;
+  if (blockIdx.x == 0 && threadIdx.x == 0) offsets[E + 1] = (int32_t)(base + T);
 }
 
 __device__ __forceinline__ void unpack8(const uint4 u, float* v) {
@@ -441,13 +449,13 @@ int forward(MlaModel* m, int32_t T, int32_t R, bool gather, const int32_t* rows_
     HK_TRY_LAUNCH("f32_of_bf16_kernel");
     HK_TRY(hk_route(m->rlf, nullptr, T, E, K, route_scale, m->ids_e, m->w_e, s));
     HK_TRY(hk_permute(m->ids_e, m->w_e, T, K, E, m->offsets, m->perm_token, m->perm_w, m->inv, s));
-    HK_TRY(hk_moe_grouped(m->xq, m->xs, T, m->offsets, m->perm_token, (int64_t)T * K, E, H, I, L.w13, L.s13, L.w2,
-                          L.s2, m->ym, m->moe_ws, m->moe_ws_bytes, s));
-    const size_t e13 = (size_t)2 * I * H, es13 = (size_t)(2 * I / 128) * (H / 128);
-    const size_t e2 = (size_t)H * I, es2 = (size_t)(H / 128) * (I / 128);
-    HK_TRY(hk_moe_grouped(m->xq, m->xs, T, m->shared_off, m->every, T, 1, H, I, L.w13 + E * e13, L.s13 + E * es13,
-                          L.w2 + E * e2, L.s2 + E * es2, m->ys, m->moe_ws, m->moe_ws_bytes, s));
-    HK_TRY(hk_combine(m->ym, (int64_t)T * K, m->perm_w, m->inv, m->ys, T, K, H, m->mo, s));
+    shared_rows_kernel<<<grid_for(T, 256), 256, 0, s>>>(m->offsets, m->perm_token, E, T, K);
+    HK_TRY_LAUNCH("shared_rows_kernel");
+    // E + 1 experts (the shared one last, as the weights store it): rows [T*K, T*K + T) of ym
+    // are the shared expert's output of every token
+    HK_TRY(hk_moe_grouped(m->xq, m->xs, T, m->offsets, m->perm_token, (int64_t)T * (K + 1), E + 1, H, I, L.w13,
+                          L.s13, L.w2, L.s2, m->ym, m->moe_ws, m->moe_ws_bytes, s));
+    HK_TRY(hk_combine(m->ym, (int64_t)T * K, m->perm_w, m->inv, m->ym + (size_t)T * K * H, T, K, H, m->mo, s));
     pending = m->mo;
   }
   HK_TRY(rms_quant(m->x, pending, nullptr, gather ? m->gather : nullptr, R, H, m->xq, m->xs, s));
@@ -458,9 +466,9 @@ int forward(MlaModel* m, int32_t T, int32_t R, bool gather, const int32_t* rows_
 }
 
 // Stage layout (int32 words): lane_tokens [width], lane_pos [width], cu_rows [width + 1],
-// gather [r_cap], shared_off [2], tokens_in [t_cap].
+// gather [r_cap], tokens_in [t_cap].
 struct Stage {
-  size_t lane_tokens, lane_pos, cu_rows, gather, shared_off, tokens_in, words;
+  size_t lane_tokens, lane_pos, cu_rows, gather, tokens_in, words;
 };
 
 Stage stage_layout(int32_t width, int32_t r_cap, int32_t t_cap) {
@@ -469,8 +477,7 @@ Stage stage_layout(int32_t width, int32_t r_cap, int32_t t_cap) {
   st.lane_pos = st.lane_tokens + width;
   st.cu_rows = st.lane_pos + width;
   st.gather = st.cu_rows + width + 1;
-  st.shared_off = st.gather + r_cap;
-  st.tokens_in = st.shared_off + 2;
+  st.tokens_in = st.gather + r_cap;
   st.words = st.tokens_in + t_cap;
   return st;
 }
@@ -565,7 +572,6 @@ int mla_create(const hk_config& c, const hk_mla_model& d, MlaModel** out, cudaSt
   HK_A(m->token_lane, T);
   HK_A(m->active, W + 1);
   HK_A(m->drafts, (int64_t)W * std::max(1, m->block - 1));
-  HK_A(m->every, T);
   HK_A(m->x, T * H);
   HK_A(m->xq, T * H);
   HK_A(m->xs, T * (H / 128));
@@ -583,12 +589,11 @@ int mla_create(const hk_config& c, const hk_mla_model& d, MlaModel** out, cudaSt
   HK_A(m->rlf, T * E);
   HK_A(m->ids_e, T * K);
   HK_A(m->w_e, T * K);
-  HK_A(m->offsets, E + 1);
-  HK_A(m->perm_token, T * K);
+  HK_A(m->offsets, E + 2);
+  HK_A(m->perm_token, T * (K + 1));
   HK_A(m->perm_w, T * K);
   HK_A(m->inv, T * K);
-  HK_A(m->ym, T * K * H);
-  HK_A(m->ys, T * H);
+  HK_A(m->ym, T * (K + 1) * H);
   HK_A(m->mo, T * H);
   HK_A(m->logits_bf16, R * V);
   HK_A(m->logits, R * V);
@@ -598,7 +603,7 @@ int mla_create(const hk_config& c, const hk_mla_model& d, MlaModel** out, cudaSt
   HK_A(m->state, W);
   HK_A(m->tok, W);
   m->attn_ws_bytes = hk_mla_workspace_size(W, (int32_t)T, kHeads, m->context);
-  m->moe_ws_bytes = hk_moe_workspace_size(T * K, (int32_t)H, (int32_t)I);
+  m->moe_ws_bytes = hk_moe_workspace_size(T * (K + 1), (int32_t)H, (int32_t)I);
   m->sample_ws_bytes = hk_sample_workspace_size((int32_t)R, (int32_t)V);
   if ((rc = dev_alloc(m, &m->attn_ws, m->attn_ws_bytes)) != HK_OK) return fail(rc);
   if ((rc = dev_alloc(m, &m->moe_ws, m->moe_ws_bytes)) != HK_OK) return fail(rc);
@@ -614,10 +619,7 @@ int mla_create(const hk_config& c, const hk_mla_model& d, MlaModel** out, cudaSt
   m->lane_pos = m->stage_d + st.lane_pos;
   m->cu_rows = m->stage_d + st.cu_rows;
   m->gather = m->stage_d + st.gather;
-  m->shared_off = m->stage_d + st.shared_off;
   m->tokens_in = m->stage_d + st.tokens_in;
-  iota_kernel<<<grid_for(T, 256), 256, 0, s>>>(m->every, (int32_t)T);
-  if ((rc = [&] { HK_TRY_LAUNCH("iota_kernel"); return HK_OK; }()) != HK_OK) return fail(rc);
   cudaError_t e = cudaMemsetAsync(m->sampling, 0, sizeof(hk_sampling) * W, s);
   if (e == cudaSuccess) e = cudaMemsetAsync(m->state, 0, sizeof(uint64_t) * W, s);
   if (e == cudaSuccess) e = cudaMemsetAsync(m->tok, 0, sizeof(int32_t) * W, s);
@@ -687,7 +689,6 @@ int mla_decode_step(MlaModel* m, const std::vector<MlaLaneRows>& lanes, const in
     max_kv = std::max(max_kv, r.pos + r.rows);
   }
   HK_REQUIRE(T <= m->r_cap, "MLA decode step: %d rows past %d", T, m->r_cap);
-  h[st.shared_off + 1] = T;
   HK_TRY_CUDA(cudaMemcpyAsync(m->stage_d, h, st.tokens_in * 4, cudaMemcpyHostToDevice, s));
   HK_TRY(hk_pack(m->lane_tokens, m->lane_pos, rows_dev, m->bt_stride, m->width, kPage, (int32_t)m->pages, m->t_cap,
                  m->cu_seqlens, m->seq_lens, m->positions, m->slots, m->token_lane, m->active, s));
@@ -728,7 +729,6 @@ int mla_prompt_step(MlaModel* m, const std::vector<MlaLaneRows>& lanes, const st
     for (const MlaLaneRows& r : lanes) acc += r.lane == l ? 1 : 0;
   }
   h[st.cu_rows + m->width] = acc;
-  h[st.shared_off + 1] = T;
   memcpy(h + st.tokens_in, tokens.data(), 4 * tokens.size());
   HK_TRY_CUDA(cudaMemcpyAsync(m->stage_d, h, (st.tokens_in + T) * 4, cudaMemcpyHostToDevice, s));
   HK_TRY(hk_pack(m->lane_tokens, m->lane_pos, rows_dev, m->bt_stride, m->width, kPage, (int32_t)m->pages, m->t_cap,

@@ -34,8 +34,8 @@ struct MlaModel {
   std::vector<MlaLayer> layers;
   // step buffers
   int32_t *lane_tokens, *lane_pos, *cu_seqlens, *seq_lens, *positions, *slots, *token_lane, *active;
-  int32_t *tokens_in, *drafts, *gather, *cu_rows, *shared_off, *every;
-  uint16_t *x, *qa, *q, *kvn, *o, *y, *rl, *ym, *ys, *mo, *logits_bf16;
+  int32_t *tokens_in, *drafts, *gather, *cu_rows;
+  uint16_t *x, *qa, *q, *kvn, *o, *y, *rl, *ym, *mo, *logits_bf16;
   uint8_t *xq, *qaq, *oq;
   float *xs, *qas, *os, *rlf, *logits, *lse;
   int32_t *ids_e, *perm_token, *inv, *offsets, *out_ids;
