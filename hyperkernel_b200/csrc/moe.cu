@@ -19,6 +19,8 @@
 
 namespace {
 
+using hk::kMoeWideRows;
+
 constexpr int kMaxExperts = 512;
 constexpr int kPermThreads = 1024;
 constexpr int kTileRows = 64;
@@ -199,6 +201,70 @@ __global__ void tile_list_kernel(const int32_t* __restrict__ offsets, int32_t E,
     base += __shfl_sync(0xffffffffu, incl, 31);
   }
   if (lane == 0) *num_tiles = base < max_tiles ? base : max_tiles;
+}
+
+// The tcgen05 kernels' two tile lists: wide tiles of kMoeWideRows (96) rows and narrow tiles
+// of at most 64.  An expert with n rows gets n / 96 wide tiles, then its remainder as one wide
+// tile when it is over 64 rows, else as one narrow tile; so an expert with at most 64 rows
+// (every expert of a decode batch) has one narrow tile, and one with 65-96 rows streams its
+// weights once instead of twice (145 rows: twice instead of three times).  With `wide` false
+// every tile is narrow (64-row tiles, as the portable kernels cut them) and the wide list is
+// empty.  One warp, experts in rounds of 32, a warp scan per list.
+__global__ void tile_lists_kernel(const int32_t* __restrict__ offsets, int32_t E, int64_t rows, bool wide,
+                                  int32_t max_narrow, int32_t* __restrict__ narrow_expert,
+                                  int32_t* __restrict__ narrow_row, int32_t* __restrict__ num_narrow,
+                                  int32_t max_wide, int32_t* __restrict__ wide_expert,
+                                  int32_t* __restrict__ wide_row, int32_t* __restrict__ num_wide,
+                                  unsigned long long* err) {
+  const int lane = threadIdx.x;
+  if (lane >= 32) return;
+  bool bad = false;
+  for (int e = lane; e < E; e += 32) bad |= offsets[e] > offsets[e + 1];
+  bad = __any_sync(0xffffffffu, bad) || offsets[0] != 0 || offsets[E] > rows;
+  if (bad) {
+    if (lane == 0) {
+      hk_flag(err, hk::kErrMoeRow, (unsigned)offsets[E]);
+      *num_narrow = 0;
+      *num_wide = 0;
+    }
+    return;
+  }
+  int nbase = 0, wbase = 0;
+  for (int e0 = 0; e0 < E; e0 += 32) {
+    const int e = e0 + lane;
+    const int lo = e < E ? offsets[e] : 0, hi = e < E ? offsets[e + 1] : 0;
+    const int n = hi - lo, step = wide ? kMoeWideRows : 64, full = n / step, rem = n % step;
+    const int nw = wide ? full + (rem > 64 ? 1 : 0) : 0;
+    const int nn = wide ? ((rem > 0 && rem <= 64) ? 1 : 0) : full + (rem > 0 ? 1 : 0);
+    int iw = nw, in = nn;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int vw = __shfl_up_sync(0xffffffffu, iw, o), vn = __shfl_up_sync(0xffffffffu, in, o);
+      if (lane >= o) {
+        iw += vw;
+        in += vn;
+      }
+    }
+    const int wfirst = wbase + iw - nw, nfirst = nbase + in - nn;
+    for (int i = 0; i < nw; ++i) {
+      if (wfirst + i < max_wide) {
+        wide_expert[wfirst + i] = e;
+        wide_row[wfirst + i] = lo + kMoeWideRows * i;
+      }
+    }
+    for (int i = 0; i < nn; ++i) {
+      if (nfirst + i < max_narrow) {
+        narrow_expert[nfirst + i] = e;
+        narrow_row[nfirst + i] = wide ? lo + kMoeWideRows * full : lo + 64 * i;
+      }
+    }
+    wbase += __shfl_sync(0xffffffffu, iw, 31);
+    nbase += __shfl_sync(0xffffffffu, in, 31);
+  }
+  if (lane == 0) {
+    *num_wide = wbase < max_wide ? wbase : max_wide;
+    *num_narrow = nbase < max_narrow ? nbase : max_narrow;
+  }
 }
 
 // Gate/up GEMM for one (row tile, 128-column block of h): g and u accumulate in fp32,
@@ -438,9 +504,14 @@ size_t moe_portable_workspace(int64_t rows, int32_t inter) {
          align256((size_t)max_tiles * 2 * sizeof(int32_t) + sizeof(int32_t));
 }
 
+// The tcgen05 path's wide tile list: expert / row pairs and a count.
+size_t wide_list_bytes(int64_t rows) {
+  return align256((size_t)(rows / kMoeWideRows + kMaxExperts + 1) * 2 * sizeof(int32_t) + sizeof(int32_t));
+}
+
 size_t moe_full_workspace(int64_t rows, int32_t hidden, int32_t inter) {
   return moe_portable_workspace(rows, inter) + align256((size_t)rows * hidden) +
-         align256((size_t)rows * (hidden / 128) * sizeof(float));
+         align256((size_t)rows * (hidden / 128) * sizeof(float)) + wide_list_bytes(rows);
 }
 
 // The grouped FFN launcher behind hk_moe_grouped: `err` is the device error word the kernels
@@ -477,12 +548,26 @@ int moe_grouped_run(const uint8_t* xq, const float* sx, int32_t tokens, const in
   ws.num_tiles = tiles + 2 * ws.max_tiles;
   ws.xp = base + moe_portable_workspace(rows, inter);
   ws.sxp = reinterpret_cast<float*>(ws.xp + align256((size_t)rows * hidden));
+  if (tc) {
+    int32_t* wide_list = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(ws.sxp) +
+                                                    align256((size_t)rows * (hidden / 128) * sizeof(float)));
+    ws.max_wide = (int32_t)(rows / kMoeWideRows + kMaxExperts + 1);
+    ws.wide_expert = wide_list;
+    ws.wide_row = wide_list + ws.max_wide;
+    ws.num_wide = wide_list + 2 * ws.max_wide;
+    // Wide tiles only where an expert can hold more than 64 rows: a batch of at most 64 tokens
+    // (a decode step; hk_permute gives an expert each token once) or one with fewer than 32
+    // rows an expert on average keeps to narrow tiles and skips the wide launches.
+    const bool wide = tokens > 64 && rows >= 32 * (int64_t)num_experts;
+    tile_lists_kernel<<<1, 32, 0, s>>>(offsets, num_experts, rows, wide, ws.max_tiles, ws.tile_expert, ws.tile_row,
+                                       ws.num_tiles, ws.max_wide, ws.wide_expert, ws.wide_row, ws.num_wide, err);
+    HK_TRY_LAUNCH("tile_lists_kernel");
+    return moe_sm100_run(xq, sx, tokens, offsets, perm_token, rows, num_experts, hidden, inter, w13, s13, w2,
+                         s2, y, ws, wide, err, s);
+  }
   tile_list_kernel<<<1, 32, 0, s>>>(offsets, num_experts, rows, ws.max_tiles, ws.tile_expert, ws.tile_row,
                                     ws.num_tiles, err);
   HK_TRY_LAUNCH("tile_list_kernel");
-  if (tc)
-    return moe_sm100_run(xq, sx, tokens, offsets, perm_token, rows, num_experts, hidden, inter, w13, s13, w2,
-                         s2, y, ws, err, s);
   moe_up_kernel<<<dim3(ws.max_tiles, inter / 128), 256, 0, s>>>(
       xq, sx, offsets, perm_token, ws.tile_expert, ws.tile_row, ws.num_tiles, hidden, inter, tokens, w13, s13,
       ws.hq, ws.hs, err);

@@ -7,9 +7,16 @@
 
 namespace hk {
 
+// Rows of the tensor-core path's wide row tiles (the MMA's N).  Each promotion thread keeps
+// gate and up sums for half of a tile's rows, and 96 rows is what 168 registers a thread (the
+// most a 320-thread CTA gets: three warps of a sub-partition share its 16,384) hold without
+// spilling; the narrow tiles have 64.
+constexpr int kMoeWideRows = 96;
+
 // Scratch of one grouped-FFN call, carved from the caller's workspace:
-//   hq [rows][inter] e4m3, hs [rows][inter/128], the tile list (portable and tcgen05),
-//   then xp [rows][hidden] e4m3 and sxp [rows][hidden/128] (tcgen05 only).
+//   hq [rows][inter] e4m3, hs [rows][inter/128], the tile list (the portable kernels' 64-row
+//   tiles, or the tcgen05 kernels' narrow tiles), then xp [rows][hidden] e4m3,
+//   sxp [rows][hidden/128] and the wide (kMoeWideRows-row) tile list (tcgen05 only).
 struct MoeScratch {
   uint8_t* hq;
   float* hs;
@@ -19,6 +26,10 @@ struct MoeScratch {
   int32_t max_tiles;
   uint8_t* xp;
   float* sxp;
+  int32_t* wide_expert;
+  int32_t* wide_row;
+  int32_t* num_wide;
+  int32_t max_wide;
 };
 
 // Bytes of the portable kernels' scratch (hq, hs, tile list): a prefix of the full layout.
@@ -40,6 +51,6 @@ bool moe_sm100_supported(int32_t num_experts, int32_t hidden, int32_t inter);
 int moe_sm100_run(const uint8_t* xq, const float* sx, int32_t tokens, const int32_t* offsets,
                   const int32_t* perm_token, int64_t rows, int32_t num_experts, int32_t hidden, int32_t inter,
                   const uint8_t* w13, const float* s13, const uint8_t* w2, const float* s2, uint16_t* y,
-                  const MoeScratch& ws, unsigned long long* err, cudaStream_t s);
+                  const MoeScratch& ws, bool wide, unsigned long long* err, cudaStream_t s);
 
 }  // namespace hk

@@ -3,24 +3,34 @@
 // Decode-sized MoE gives each expert a handful of rows (config 4: ~16 of 4096 permuted rows
 // per expert), so the expert weights are the large operand and the kernel is HBM-bound on
 // them.  Weights therefore take the MMA's M side (128 weight rows, one 128x128 scale block)
-// and the expert's rows the N side (a tile of up to 64 rows), and each work unit streams one
-// 128-row block of one expert's weights exactly once per row tile.
+// and the expert's rows the N side (a row tile), and each work unit streams one 128-row block
+// of one expert's weights exactly once per row tile.
+//
+// Two row-tile widths, two launches per projection over two device-built tile lists: narrow
+// tiles of at most 64 rows (N 64; every expert of a decode batch) and wide tiles of 96 rows
+// (N 96) for experts with more rows (expert parallelism on 4-8 GPUs, prompt chunks), so an
+// expert with 65-96 rows streams its weights once instead of twice.  The wide form keeps four
+// 44 KB stages instead of five 40 KB ones and two TMEM accumulator buffers instead of four;
+// its promotion threads hold 48 token columns each (gate and up: 96 fp32 sums, what the 168
+// registers of a 320-thread CTA's threads hold beside the rest).
 //
 //  gather   xp[p] = xq[perm_token[p]], sxp[p] = sx[perm_token[p]]: the routed rows laid out
 //           contiguously in permuted order, so TMA can load a row tile (out-of-range
 //           indices are recorded and give a zero row).
 //  up       unit = (row tile, 128-column block nb of h): D_g = Wg[nb] . X^T and
-//           D_u = Wu[nb] . X^T per 128-wide K block (tcgen05 kind::f8f6f4, M 128, N 64) into
-//           double-buffered TMEM; promotion warps add partial * sw * sx[row] in registers;
+//           D_u = Wu[nb] . X^T per 128-wide K block (tcgen05 kind::f8f6f4, M 128, N 64 or 128)
+//           into multi-buffered TMEM; promotion warps add partial * sw * sx[row] in registers;
 //           at the end h = silu(g) * u is requantised to e4m3 with one scale per (row, nb)
 //           (amax over the block's 128 columns across the four warps).
 //  down     unit = (row tile, 256-column block of y as two 128-row blocks of W2):
 //           D = W2[block] . hq^T over inter, promoted with sw * hs[row], stored as bf16.
 // Roles per CTA (10 warps): warp 0 TMA, warp 1 MMA and TMEM owner, warps 2..9 promotion (two
-// per TMEM lane quarter, each with 32 of the 64 token columns; thread = weight row), so a K
-// block costs each promotion warp one TMEM round trip.  Persistent over the units of the device-built
-// tile list; every wait bounded (1 s) with the error word, in-flight copies and MMAs drained
-// before exit.
+// per TMEM lane quarter, each with half of the tile's token columns; thread = weight row), so
+// a K block costs each promotion warp one TMEM round trip.  Every output element is one
+// weight row's dot product with one token row in the same K-block order whichever tile holds
+// the row, so a row's result does not depend on the tile width.  Persistent over the units of
+// the tile list; every wait bounded (1 s) with the error word, in-flight copies and MMAs
+// drained before exit.
 #include <cuda.h>
 #include <math.h>
 
@@ -31,23 +41,20 @@
 namespace {
 
 using namespace hk::sm100;
+using hk::kMoeWideRows;
 
-constexpr int kRowsTile = 64;   // rows (tokens) per unit: the MMA's N
 constexpr int kWRows = 128;     // weight rows per unit: the MMA's M
 constexpr int kBK = 128;
 constexpr int kThreads = 320;       // TMA, MMA, 8 promotion warps
-constexpr int kCols = 32;           // token columns per promotion warp
 constexpr int kWBytes = kWRows * kBK;      // 16 KB
-constexpr int kXBytes = kRowsTile * kBK;   // 8 KB
-constexpr uint32_t kIdesc = idesc_e4m3(kWRows, kRowsTile);
 constexpr unsigned long long kDrainNs = 1000000000ull;
-// TMEM accumulator buffers: the MMA runs this many K blocks ahead of the promotion warps, which
-// covers their per-unit work (scale table at the start, requantisation or stores at the end).
+// TMEM accumulator buffers of the narrow form: the MMA runs this many K blocks ahead of the
+// promotion warps, which covers their per-unit work (scale table at the start, requantisation
+// or stores at the end).
 #ifndef HK_MOE_TBUFS
 #define HK_MOE_TBUFS 4
 #endif
-constexpr int kTBufs = HK_MOE_TBUFS;
-static_assert(kTBufs == 2 || kTBufs == 4, "TMEM buffers");
+static_assert(HK_MOE_TBUFS == 2 || HK_MOE_TBUFS == 4, "TMEM buffers");
 
 
 // Control block offsets (after the ring and the scale table).
@@ -57,18 +64,27 @@ constexpr int kBarTFull = 128;   // [kTBufs]
 constexpr int kBarTEmpty = 160;  // [kTBufs]
 constexpr int kTmemSlot = 192;
 constexpr int kAbort = 196;
-constexpr int kRed = 256;        // [4][64] floats: per-warp column amax (up epilogue)
-constexpr int kCtlBytes = kRed + 4 * kRowsTile * 4;
+constexpr int kRed = 256;        // [4][kRows] floats: per-warp column amax (up epilogue)
 
-template <bool kUp>
+// kRows: token rows per unit, the MMA's N (64: narrow tiles, kMoeWideRows: wide tiles).
+template <bool kUp, int kRows>
 struct Cfg {
+  static_assert(kRows == 64 || kRows == kMoeWideRows, "row tile");
+  static constexpr int kXBytes = kRows * kBK;                // 8 or 12 KB
   static constexpr int kStageBytes = 2 * kWBytes + kXBytes;  // two weight blocks, one row tile
   static constexpr int kMaxKb = kUp ? 64 : 32;  // scale-table capacity in K blocks
-  static constexpr int kStages = 5;
+  static constexpr int kStages = kRows == 64 ? 5 : 4;
+  static constexpr int kTBufs = kRows == 64 ? HK_MOE_TBUFS : 2;  // 2 * kRows columns each
+  static constexpr int kCols = kRows / 2;       // token columns per promotion warp
+  static constexpr int kChunk = kRows == 64 ? 32 : 16;  // columns per TMEM load
   static constexpr int kOffScales = kStages * kStageBytes;
-  static constexpr int kOffCtl = kOffScales + kMaxKb * kRowsTile * 4;
+  static constexpr int kOffCtl = kOffScales + kMaxKb * kRows * 4;
+  static constexpr int kCtlBytes = kRed + 4 * kRows * 4;
   static constexpr int kSmem = kOffCtl + kCtlBytes;
-  static constexpr uint32_t kTmemCols = kTBufs * 128;
+  static constexpr uint32_t kTmemCols = 512;  // allocated (a power of two); kTBufs * 2 * kRows used
+  static constexpr uint32_t kIdesc = idesc_e4m3(kWRows, kRows);
+  static_assert(kTBufs * 2 * kRows <= 512 && kCols % kChunk == 0 && kRows % 16 == 0, "TMEM columns");
+  static_assert(kStageBytes % 1024 == 0, "stage alignment (128-byte swizzle atoms)");
   static_assert(kSmem <= 232448, "shared memory budget");
 };
 
@@ -115,10 +131,12 @@ __device__ __forceinline__ bool bar_and(int id, int count, bool v) {
   return out != 0;
 }
 
-template <bool kUp>
+template <bool kUp, int kRows>
 __global__ void __launch_bounds__(kThreads, 1)
     moe_sm100_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap, Params p) {
-  using C = Cfg<kUp>;
+  using C = Cfg<kUp, kRows>;
+  constexpr int kTBufs = C::kTBufs, kCols = C::kCols, kChunk = C::kChunk;
+  if (*p.num_tiles == 0) return;  // an empty list: leave before any set-up
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t* ctl = smem + C::kOffCtl;
   float* scales = reinterpret_cast<float*>(smem + C::kOffScales);  // [kb][64]
@@ -200,12 +218,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           const uint32_t a = smem_u32(smem + s * C::kStageBytes);
           const uint32_t x = a + 2 * kWBytes;
-          const uint32_t d = tmem + (uint32_t)(buf * 128);
+          const uint32_t d = tmem + (uint32_t)(buf * 2 * kRows);
 #pragma unroll
           for (int kk = 0; kk < kBK / 32; ++kk) {
             const uint64_t bdesc = sdesc_sw128(x + 32 * kk, 16, 1024);
-            umma_f8(d, sdesc_sw128(a + 32 * kk, 16, 1024), bdesc, kIdesc, kk > 0 ? 1u : 0u);
-            umma_f8(d + 64, sdesc_sw128(a + kWBytes + 32 * kk, 16, 1024), bdesc, kIdesc, kk > 0 ? 1u : 0u);
+            umma_f8(d, sdesc_sw128(a + 32 * kk, 16, 1024), bdesc, C::kIdesc, kk > 0 ? 1u : 0u);
+            umma_f8(d + kRows, sdesc_sw128(a + kWBytes + 32 * kk, 16, 1024), bdesc, C::kIdesc, kk > 0 ? 1u : 0u);
           }
           umma_commit(ctl_u + kBarEmpty + 8 * s);
           umma_commit(ctl_u + kBarTFull + 8 * buf);
@@ -231,12 +249,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int u = blockIdx.x; live && u < units; u += gridDim.x) {
       const int tile = u / nblocks, nb = u % nblocks;
       const int e = p.tile_expert[tile], r0 = p.tile_row[tile];
-      const int count = min(kRowsTile, p.offsets[e + 1] - r0);
+      const int count = min(kRows, p.offsets[e + 1] - r0);
       // Per-row activation scales of the tile for every K block: scales[kb][n].
       asm volatile("bar.sync 1, 256;" ::: "memory");  // the previous unit is done reading them
-      for (int i = et; i < kblocks * kRowsTile; i += 256) {
-        const int n = i % kRowsTile, kb = i / kRowsTile;
-        scales[kb * kRowsTile + n] = n < count ? p.act_scale[(int64_t)(r0 + n) * kblocks + kb] : 0.f;
+      for (int i = et; i < kblocks * kRows; i += 256) {
+        const int n = i % kRows, kb = i / kRows;
+        scales[kb * kRows + n] = n < count ? p.act_scale[(int64_t)(r0 + n) * kblocks + kb] : 0.f;
       }
       asm volatile("bar.sync 1, 256;" ::: "memory");
       // Weight scales of the unit's two row blocks (g: gate or first block, u: up or second).
@@ -265,18 +283,28 @@ __global__ void __launch_bounds__(kThreads, 1)
           continue;
         }
         tc_fence_after();
-        const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * 128 + half * kCols);
-        float vg[kCols], vu[kCols];
-        tmem_ld32x2(base, base + 64, vg, vu);  // both blocks' columns of this half, one wait
-        const float4* sc4 = reinterpret_cast<const float4*>(scales + kb * kRowsTile + half * kCols);
+        const uint32_t base =
+            tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * 2 * kRows + half * kCols);
 #pragma unroll
-        for (int j = 0; j < kCols / 4; ++j) {
-          const float4 s4 = sc4[j];
-          const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
+        for (int c = 0; c < kCols / kChunk; ++c) {
+          float vg[kChunk], vu[kChunk];
+          // both blocks' columns of this chunk, one wait
+          if constexpr (kChunk == 32) {
+            tmem_ld32x2(base + c * kChunk, base + kRows + c * kChunk, vg, vu);
+          } else {
+            tmem_ld16x2(base + c * kChunk, base + kRows + c * kChunk, vg, vu);
+          }
+          const float4* sc4 = reinterpret_cast<const float4*>(scales + kb * kRows + half * kCols + c * kChunk);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            acc_g[4 * j + i] = fmaf(vg[4 * j + i], sv[i] * sg, acc_g[4 * j + i]);
-            acc_u[4 * j + i] = fmaf(vu[4 * j + i], sv[i] * su, acc_u[4 * j + i]);
+          for (int j = 0; j < kChunk / 4; ++j) {
+            const float4 s4 = sc4[j];
+            const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int col = c * kChunk + 4 * j + i;
+              acc_g[col] = fmaf(vg[4 * j + i], sv[i] * sg, acc_g[col]);
+              acc_u[col] = fmaf(vu[4 * j + i], sv[i] * su, acc_u[col]);
+            }
           }
         }
         tc_fence_before();
@@ -294,7 +322,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           float a = fabsf(acc_g[i]);
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
-          if (lane == 0) red[q * kRowsTile + half * kCols + i] = a;
+          if (lane == 0) red[q * kRows + half * kCols + i] = a;
         }
         asm volatile("bar.sync 1, 256;" ::: "memory");
         const int inter_blocks = p.inter / 128;
@@ -302,8 +330,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < kCols; ++i) {
           const int n = half * kCols + i;
           if (n < count) {
-            const float amax =
-                fmaxf(fmaxf(red[n], red[kRowsTile + n]), fmaxf(red[2 * kRowsTile + n], red[3 * kRowsTile + n]));
+            const float amax = fmaxf(fmaxf(red[n], red[kRows + n]), fmaxf(red[2 * kRows + n], red[3 * kRows + n]));
             const float s = __fdiv_rn(fmaxf(amax, 1e-12f), 448.0f);
             const int64_t row = r0 + n;
             p.hq[row * p.inter + nb * 128 + m] = f32_to_e4m3(__fdiv_rn(acc_g[i], s));
@@ -331,15 +358,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <bool kUp>
+template <bool kUp, int kRows>
 int launch(const CUtensorMap& wmap, const CUtensorMap& xmap, const Params& p, int grid, cudaStream_t s) {
+  using C = Cfg<kUp, kRows>;
   static bool attr = false;
   if (!attr) {
-    HK_TRY_CUDA(cudaFuncSetAttribute(moe_sm100_kernel<kUp>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     Cfg<kUp>::kSmem));
+    HK_TRY_CUDA(cudaFuncSetAttribute(moe_sm100_kernel<kUp, kRows>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     C::kSmem));
     attr = true;
   }
-  moe_sm100_kernel<kUp><<<grid, kThreads, Cfg<kUp>::kSmem, s>>>(wmap, xmap, p);
+  moe_sm100_kernel<kUp, kRows><<<grid, kThreads, C::kSmem, s>>>(wmap, xmap, p);
   HK_TRY_LAUNCH(kUp ? "moe_sm100_kernel<up>" : "moe_sm100_kernel<down>");
   return HK_OK;
 }
@@ -349,24 +377,26 @@ int launch(const CUtensorMap& wmap, const CUtensorMap& xmap, const Params& p, in
 namespace hk {
 
 bool moe_sm100_supported(int32_t num_experts, int32_t hidden, int32_t inter) {
-  return hidden % 128 == 0 && inter % 128 == 0 && hidden / 128 <= Cfg<true>::kMaxKb &&
-         inter / 128 <= Cfg<false>::kMaxKb && (int64_t)num_experts * 2 * inter < (1ll << 31) &&
+  return hidden % 128 == 0 && inter % 128 == 0 && hidden / 128 <= Cfg<true, 64>::kMaxKb &&
+         inter / 128 <= Cfg<false, 64>::kMaxKb && (int64_t)num_experts * 2 * inter < (1ll << 31) &&
          (int64_t)num_experts * hidden < (1ll << 31);
 }
 
 int moe_sm100_run(const uint8_t* xq, const float* sx, int32_t tokens, const int32_t* offsets,
                   const int32_t* perm_token, int64_t rows, int32_t num_experts, int32_t hidden, int32_t inter,
                   const uint8_t* w13, const float* s13, const uint8_t* w2, const float* s2, uint16_t* y,
-                  const MoeScratch& ws, unsigned long long* err, cudaStream_t s) {
+                  const MoeScratch& ws, bool wide, unsigned long long* err, cudaStream_t s) {
   HK_REQUIRE(moe_sm100_supported(num_experts, hidden, inter), "moe_sm100: hidden %d inter %d", hidden, inter);
   HK_REQUIRE(rows < (1ll << 31), "moe_sm100: %lld rows", (long long)rows);
   gather_rows_kernel<<<(unsigned)rows, 128, 0, s>>>(xq, sx, perm_token, rows, tokens, hidden, ws.xp, ws.sxp, err);
   HK_TRY_LAUNCH("gather_rows_kernel");
-  CUtensorMap w13map, xmap, w2map, hmap;
+  CUtensorMap w13map, xmap, xmap_w, w2map, hmap, hmap_w;
   HK_TRY(sm100::make_map_u8(&w13map, w13, (uint64_t)num_experts * 2 * inter, (uint64_t)hidden, kWRows));
-  HK_TRY(sm100::make_map_u8(&xmap, ws.xp, (uint64_t)rows, (uint64_t)hidden, kRowsTile));
+  HK_TRY(sm100::make_map_u8(&xmap, ws.xp, (uint64_t)rows, (uint64_t)hidden, 64));
+  HK_TRY(sm100::make_map_u8(&xmap_w, ws.xp, (uint64_t)rows, (uint64_t)hidden, kMoeWideRows));
   HK_TRY(sm100::make_map_u8(&w2map, w2, (uint64_t)num_experts * hidden, (uint64_t)inter, kWRows));
-  HK_TRY(sm100::make_map_u8(&hmap, ws.hq, (uint64_t)rows, (uint64_t)inter, kRowsTile));
+  HK_TRY(sm100::make_map_u8(&hmap, ws.hq, (uint64_t)rows, (uint64_t)inter, 64));
+  HK_TRY(sm100::make_map_u8(&hmap_w, ws.hq, (uint64_t)rows, (uint64_t)inter, kMoeWideRows));
   Params p{};
   p.offsets = offsets;
   p.tile_expert = ws.tile_expert;
@@ -382,11 +412,17 @@ int moe_sm100_run(const uint8_t* xq, const float* sx, int32_t tokens, const int3
   p.w_scale = s13;
   p.hq = ws.hq;
   p.hs = ws.hs;
-  HK_TRY(launch<true>(w13map, xmap, p, grid, s));
-  p.act_scale = ws.hs;
-  p.w_scale = s2;
-  p.y = y;
-  HK_TRY(launch<false>(w2map, hmap, p, grid, s));
+  Params pw = p;  // the wide tiles' list
+  pw.tile_expert = ws.wide_expert;
+  pw.tile_row = ws.wide_row;
+  pw.num_tiles = ws.num_wide;
+  HK_TRY((launch<true, 64>(w13map, xmap, p, grid, s)));
+  if (wide) HK_TRY((launch<true, kMoeWideRows>(w13map, xmap_w, pw, grid, s)));
+  p.act_scale = pw.act_scale = ws.hs;
+  p.w_scale = pw.w_scale = s2;
+  p.y = pw.y = y;
+  HK_TRY((launch<false, 64>(w2map, hmap, p, grid, s)));
+  if (wide) HK_TRY((launch<false, kMoeWideRows>(w2map, hmap_w, pw, grid, s)));
   return HK_OK;
 }
 

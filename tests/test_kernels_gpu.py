@@ -484,6 +484,45 @@ def test_moe_layer_matches_oracle(hk, orc, cuda, T, E, H, I, K):
     assert rel_err(to_np_bf16(out), want) <= TOL
 
 
+def test_moe_grouped_narrow_and_wide_row_tiles_match_oracle(hk, orc, cuda):
+    """Experts whose row counts sit on every edge of the two tile lists of the tensor-core
+    path (narrow tiles of at most 64 rows, wide tiles of 96): none, one narrow tile (1, 64
+    rows), one wide tile (65, 96), a wide tile and a narrow remainder (97, 160), two wide
+    tiles (161 = 96 + 65, 192) and three wide tiles with a narrow remainder (300 = 3 x 96 +
+    12).  Rows come from a random token map, so tiles mix tokens as a real permutation does."""
+    counts = [0, 1, 64, 65, 96, 97, 160, 161, 192, 300]
+    E, H, I, T = len(counts), 256, 256, 400
+    inp = _moe_case(T, E, H, I, 2, seed=58)
+    rng = W.Rng(59)
+    off = np.concatenate([[0], np.cumsum(counts)]).astype(np.int32)
+    tok = rng.integers(0, T - 1, int(off[-1])).astype(np.int32)  # inclusive bounds
+    xq, sx = orc.quant_fp8(inp["x"])
+    y = orc.moe_grouped(xq, sx, off, tok, H, I, inp["w13"], inp["s13"], inp["w2"], inp["s2"])
+    gxq, gsx = hk.quant_fp8(bf16_dev(inp["x"], cuda))
+    gy = hk.moe_grouped(gxq, gsx, dev(off, cuda), dev(tok, cuda), int(off[-1]), H, I, dev(inp["w13"], cuda),
+                        dev(inp["s13"], cuda), dev(inp["w2"], cuda), dev(inp["s2"], cuda))
+    hk.check_errors()
+    assert rel_err(to_np_bf16(gy), y) <= TOL
+
+
+def test_moe_grouped_row_result_does_not_depend_on_the_tile_width(hk, cuda):
+    """The same 96 rows through one expert (one wide tile) and through two copies of that
+    expert with 48 rows each (two narrow tiles) give the same bits: each output is one weight
+    row's dot product with one token row in the same K-block order either way (expert
+    parallelism relies on this: a rank's experts receive more rows than the same experts on
+    one GPU and may take the other tile width)."""
+    E, H, I, T = 1, 512, 256, 96
+    inp = _moe_case(T, E, H, I, 2, seed=60)
+    gxq, gsx = hk.quant_fp8(bf16_dev(inp["x"], cuda))
+    tok = dev(np.random.default_rng(61).permutation(T).astype(np.int32), cuda)
+    w = [dev(inp[k], cuda) for k in ("w13", "s13", "w2", "s2")]
+    one = hk.moe_grouped(gxq, gsx, dev(np.array([0, T], np.int32), cuda), tok, T, H, I, *w)
+    two_w = [torch.cat([t, t]) for t in w]
+    two = hk.moe_grouped(gxq, gsx, dev(np.array([0, 48, T], np.int32), cuda), tok, T, H, I, *two_w)
+    hk.check_errors()
+    assert torch.equal(one.view(torch.int16), two.view(torch.int16))
+
+
 def test_moe_layer_full_size_matches_oracle_on_sampled_tokens(hk, orc, cuda):
     """Config 4 at full size (512 tokens, 256 routed experts + 1 shared, top 8, hidden 7168,
     inter 2048: 11.3 GB of e4m3 weights, so every expert is hit): the whole layer on the GPU,
