@@ -203,14 +203,17 @@ __global__ void tile_list_kernel(const int32_t* __restrict__ offsets, int32_t E,
   if (lane == 0) *num_tiles = base < max_tiles ? base : max_tiles;
 }
 
-// The tcgen05 kernels' two tile lists: wide tiles of kMoeWideRows (96) rows and narrow tiles
-// of at most 64.  An expert with n rows gets n / 96 wide tiles, then its remainder as one wide
-// tile when it is over 64 rows, else as one narrow tile; so an expert with at most 64 rows
-// (every expert of a decode batch) has one narrow tile, and one with 65-96 rows streams its
-// weights once instead of twice (145 rows: twice instead of three times).  With `wide` false
-// every tile is narrow (64-row tiles, as the portable kernels cut them) and the wide list is
-// empty.  One warp, experts in rounds of 32, a warp scan per list.
-__global__ void tile_lists_kernel(const int32_t* __restrict__ offsets, int32_t E, int64_t rows, bool wide,
+// The tcgen05 kernels' tile lists: one of them gets every tile, the other stays empty (its
+// launch returns at once).  When the experts hold at least kWideMinRows rows on average (and
+// `allow_wide`), the wide list gets tiles of kMoeWideRows (96) rows — an expert with 65-96
+// rows then streams its weights once instead of twice, one with 145 twice instead of three
+// times; otherwise (a decode batch, config 4's 16 rows an expert) the narrow list gets 64-row
+// tiles, as the portable kernels cut them.  The choice reads the actual row total on the
+// device, so a caller that passes a row capacity (expert parallelism) gets the right one.
+// One warp, experts in rounds of 32, a warp scan.
+constexpr int kWideMinRows = 56;
+
+__global__ void tile_lists_kernel(const int32_t* __restrict__ offsets, int32_t E, int64_t rows, bool allow_wide,
                                   int32_t max_narrow, int32_t* __restrict__ narrow_expert,
                                   int32_t* __restrict__ narrow_row, int32_t* __restrict__ num_narrow,
                                   int32_t max_wide, int32_t* __restrict__ wide_expert,
@@ -229,13 +232,13 @@ __global__ void tile_lists_kernel(const int32_t* __restrict__ offsets, int32_t E
     }
     return;
   }
+  const bool wide = allow_wide && (int64_t)offsets[E] >= (int64_t)kWideMinRows * E;
   int nbase = 0, wbase = 0;
   for (int e0 = 0; e0 < E; e0 += 32) {
     const int e = e0 + lane;
     const int lo = e < E ? offsets[e] : 0, hi = e < E ? offsets[e + 1] : 0;
-    const int n = hi - lo, step = wide ? kMoeWideRows : 64, full = n / step, rem = n % step;
-    const int nw = wide ? full + (rem > 64 ? 1 : 0) : 0;
-    const int nn = wide ? ((rem > 0 && rem <= 64) ? 1 : 0) : full + (rem > 0 ? 1 : 0);
+    const int n = hi - lo, step = wide ? kMoeWideRows : 64, tiles = (n + step - 1) / step;
+    const int nw = wide ? tiles : 0, nn = wide ? 0 : tiles;
     int iw = nw, in = nn;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -255,7 +258,7 @@ __global__ void tile_lists_kernel(const int32_t* __restrict__ offsets, int32_t E
     for (int i = 0; i < nn; ++i) {
       if (nfirst + i < max_narrow) {
         narrow_expert[nfirst + i] = e;
-        narrow_row[nfirst + i] = wide ? lo + kMoeWideRows * full : lo + 64 * i;
+        narrow_row[nfirst + i] = lo + 64 * i;
       }
     }
     wbase += __shfl_sync(0xffffffffu, iw, 31);
@@ -555,10 +558,10 @@ int moe_grouped_run(const uint8_t* xq, const float* sx, int32_t tokens, const in
     ws.wide_expert = wide_list;
     ws.wide_row = wide_list + ws.max_wide;
     ws.num_wide = wide_list + 2 * ws.max_wide;
-    // Wide tiles only where an expert can hold more than 64 rows: a batch of at most 64 tokens
-    // (a decode step; hk_permute gives an expert each token once) or one with fewer than 32
-    // rows an expert on average keeps to narrow tiles and skips the wide launches.
-    const bool wide = tokens > 64 && rows >= 32 * (int64_t)num_experts;
+    // No wide tiles (and no wide launches) where no expert can hold more than 64 rows: a batch
+    // of at most 64 tokens (a decode step; hk_permute gives an expert each token once) or of
+    // fewer rows than the wide threshold over all experts.
+    const bool wide = tokens > 64 && rows >= (int64_t)kWideMinRows * num_experts;
     tile_lists_kernel<<<1, 32, 0, s>>>(offsets, num_experts, rows, wide, ws.max_tiles, ws.tile_expert, ws.tile_row,
                                        ws.num_tiles, ws.max_wide, ws.wide_expert, ws.wide_row, ws.num_wide, err);
     HK_TRY_LAUNCH("tile_lists_kernel");

@@ -6,19 +6,21 @@
 // and the expert's rows the N side (a row tile), and each work unit streams one 128-row block
 // of one expert's weights exactly once per row tile.
 //
-// Two row-tile widths, two launches per projection over two device-built tile lists: narrow
-// tiles of at most 64 rows (N 64; every expert of a decode batch) and wide tiles of 96 rows
-// (N 96) for experts with more rows (expert parallelism on 4-8 GPUs, prompt chunks), so an
-// expert with 65-96 rows streams its weights once instead of twice.  The wide form keeps four
-// 44 KB stages instead of five 40 KB ones and two TMEM accumulator buffers instead of four;
-// its promotion threads hold 48 token columns each (gate and up: 96 fp32 sums, what the 168
+// Two row-tile widths: narrow tiles of at most 64 rows (N 64) and wide tiles of 96 rows (N 96).
+// The device-built tile lists give every tile of a call to one width: wide when the experts
+// hold at least 56 rows on average (expert parallelism on 4-8 GPUs, prompt chunks), so an
+// expert with 65-96 rows streams its weights once instead of twice; narrow otherwise (decode
+// batches, config 4).  Both widths are launched (a decode batch of at most 64 tokens only the
+// narrow one) and the one whose list is empty returns at once.  The wide form keeps four 44 KB
+// stages instead of five 40 KB ones and two TMEM accumulator buffers instead of four; its
+// promotion threads hold 48 token columns each (gate and up: 96 fp32 sums, what the 168
 // registers of a 320-thread CTA's threads hold beside the rest).
 //
 //  gather   xp[p] = xq[perm_token[p]], sxp[p] = sx[perm_token[p]]: the routed rows laid out
 //           contiguously in permuted order, so TMA can load a row tile (out-of-range
 //           indices are recorded and give a zero row).
 //  up       unit = (row tile, 128-column block nb of h): D_g = Wg[nb] . X^T and
-//           D_u = Wu[nb] . X^T per 128-wide K block (tcgen05 kind::f8f6f4, M 128, N 64 or 128)
+//           D_u = Wu[nb] . X^T per 128-wide K block (tcgen05 kind::f8f6f4, M 128, N 64 or 96)
 //           into multi-buffered TMEM; promotion warps add partial * sw * sx[row] in registers;
 //           at the end h = silu(g) * u is requantised to e4m3 with one scale per (row, nb)
 //           (amax over the block's 128 columns across the four warps).

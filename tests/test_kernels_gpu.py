@@ -484,13 +484,14 @@ def test_moe_layer_matches_oracle(hk, orc, cuda, T, E, H, I, K):
     assert rel_err(to_np_bf16(out), want) <= TOL
 
 
-def test_moe_grouped_narrow_and_wide_row_tiles_match_oracle(hk, orc, cuda):
-    """Experts whose row counts sit on every edge of the two tile lists of the tensor-core
-    path (narrow tiles of at most 64 rows, wide tiles of 96): none, one narrow tile (1, 64
-    rows), one wide tile (65, 96), a wide tile and a narrow remainder (97, 160), two wide
-    tiles (161 = 96 + 65, 192) and three wide tiles with a narrow remainder (300 = 3 x 96 +
-    12).  Rows come from a random token map, so tiles mix tokens as a real permutation does."""
-    counts = [0, 1, 64, 65, 96, 97, 160, 161, 192, 300]
+@pytest.mark.parametrize("empty", [0, 20])
+def test_moe_grouped_narrow_and_wide_row_tiles_match_oracle(hk, orc, cuda, empty):
+    """Experts whose row counts sit on the tile edges of the tensor-core path: none, 1, 64,
+    65, 96, 97, 160, 161, 192 and 300 rows.  Averaging 134 rows an expert, every tile is a
+    96-row wide tile (65-96 rows: one tile; 97-192: two; 300: four); with 20 more experts
+    without rows (45 on average) every tile is a 64-row narrow tile.  Rows come from a random
+    token map, so tiles mix tokens as a real permutation does."""
+    counts = [0, 1, 64, 65, 96, 97, 160, 161, 192, 300] + [0] * empty
     E, H, I, T = len(counts), 256, 256, 400
     inp = _moe_case(T, E, H, I, 2, seed=58)
     rng = W.Rng(59)
@@ -506,11 +507,11 @@ def test_moe_grouped_narrow_and_wide_row_tiles_match_oracle(hk, orc, cuda):
 
 
 def test_moe_grouped_row_result_does_not_depend_on_the_tile_width(hk, cuda):
-    """The same 96 rows through one expert (one wide tile) and through two copies of that
-    expert with 48 rows each (two narrow tiles) give the same bits: each output is one weight
-    row's dot product with one token row in the same K-block order either way (expert
-    parallelism relies on this: a rank's experts receive more rows than the same experts on
-    one GPU and may take the other tile width)."""
+    """The same 96 rows through one expert (96 rows on average: one wide tile) and through two
+    copies of that expert with 48 rows each (48 on average: two narrow tiles) give the same
+    bits: each output is one weight row's dot product with one token row in the same K-block
+    order either way (expert parallelism relies on this: a rank's experts receive more rows
+    than the same experts on one GPU and may take the other tile width)."""
     E, H, I, T = 1, 512, 256, 96
     inp = _moe_case(T, E, H, I, 2, seed=60)
     gxq, gsx = hk.quant_fp8(bf16_dev(inp["x"], cuda))
