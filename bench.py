@@ -491,31 +491,35 @@ def leg_ep(args, torch, dist, hk, par, world, rank, device, stream, barrier, hbm
     logits = torch.randn((T, E), generator=gx, device=device)
     rows = T * K
     rows_max = rows * world
-    ws = torch.empty(hk.moe_workspace_size(rows_max, H, I), dtype=torch.uint8, device=device)
+    ws = torch.empty(hk.moe_workspace_size(rows_max + T, H, I), dtype=torch.uint8, device=device)
     ws_sh = torch.empty(hk.moe_workspace_size(T, H, I), dtype=torch.uint8, device=device)
-    y_buf = torch.empty((rows_max, H), dtype=torch.bfloat16, device=device)
+    y_buf = torch.empty((rows_max + T, H), dtype=torch.bfloat16, device=device)
     y_sh = torch.empty((T, H), dtype=torch.bfloat16, device=device)
     every = torch.arange(T, dtype=torch.int32, device=device)
     sh_off = torch.tensor([0, T], dtype=torch.int32, device=device)
-    peer = par.EpPeer(E, T, K, H) if world > 1 else None
+    # the shared expert runs in the same grouped-FFN call as this rank's routed experts, as
+    # expert 0 of a weight copy ordered [shared, local experts]
+    peer = par.EpPeer(E, T, K, H, shared_tokens=T) if world > 1 else None
+    fold = tuple(torch.cat([a[E:], a[e0:e1]]) for a in (w13, s13, w2, s2)) if peer is not None else None
 
     def step(ev=None):
         xq, sx = hk.quant_fp8(x)
         ids, w = hk.route(logits, None, K, 1.0)
         off, tok, pw, inv = hk.permute(ids, w, E)
         if peer is not None:
-            xr, sr, loff, lperm = peer.dispatch(xq, sx, off, tok)
+            xr, sr, foff, fperm, frows = peer.dispatch_with_shared(xq, sx, off, tok)
         if ev is not None:
             ev[0].record(stream)
         if peer is not None:
-            y_loc = hk.moe_grouped(xr, sr, loff, lperm, peer.rows_cap, H, I, *loc, out=y_buf, workspace=ws)
+            y_all = hk.moe_grouped(xr, sr, foff, fperm, frows, H, I, *fold, out=y_buf, workspace=ws)
+            y_shared, y_loc = y_all[:T], y_all[T:]
         else:
             y_loc = hk.moe_grouped(xq, sx, off, tok, rows, H, I, *loc, out=y_buf, workspace=ws)
-        hk.moe_grouped(xq, sx, sh_off, every, T, H, I, *shr, out=y_sh, workspace=ws_sh)
+            y_shared = hk.moe_grouped(xq, sx, sh_off, every, T, H, I, *shr, out=y_sh, workspace=ws_sh)
         if ev is not None:
             ev[1].record(stream)
         y = peer.give_back(y_loc) if peer is not None else y_loc
-        return hk.combine(y, pw, inv, y_sh, T, K), (loff if peer is not None else off)
+        return hk.combine(y, pw, inv, y_shared, T, K), (peer.local_off if peer is not None else off)
 
     for _ in range(args.warmup):
         out, off = step()
@@ -554,7 +558,8 @@ def leg_ep(args, torch, dist, hk, par, world, rank, device, stream, barrier, hbm
         "workload": "config4 MoE layer: 512 tokens per GPU, 256 routed experts top-8 + 1 shared, hidden 7168, "
                     "inter 2048, FP8 128x128 block scales; quant+route+permute+dispatch+grouped FFN+return+combine",
         "parallelism": f"ep{world}" if world > 1 else "single GPU (no exchange)",
-        "exchange": "NVLink peer stores from hk_ep_counts/hk_ep_dispatch/hk_ep_return, bounded epoch waits"
+        "exchange": "NVLink peer stores from hk_ep_counts/hk_ep_dispatch/hk_ep_return, bounded epoch waits; "
+                    "the shared expert in the same grouped-FFN launch as the rank's routed experts"
                     if world > 1 else None,
         "scaling": "weak", "ms_per_step": ms / args.steps, "tokens_per_s": T * world * args.steps / (ms / 1e3),
         "routed_rows_per_s": rows * world * args.steps / (ms / 1e3), "experts_per_gpu": e1 - e0,
@@ -831,7 +836,10 @@ def _run_moe(args, torch, dist, hk, par, ClockSampler, world, rank, local, devic
     off_ext[E + 1] = rows + T
     tok_ext = torch.empty(rows + T, dtype=torch.int32, device=device)
     tok_ext[rows:] = sh_tok
-    peer = par.EpPeer(E, T, K, H) if world > 1 and args.ep == "peer" else None
+    peer = par.EpPeer(E, T, K, H, shared_tokens=T) if world > 1 and args.ep == "peer" else None
+    # with the peer exchange the shared expert runs in the rank's grouped-FFN call, as expert 0
+    # of a weight copy ordered [shared, local experts]
+    fold = tuple(torch.cat([b[El:], b[:El]]) for b in (w13_all, s13_all, w2_all, s2_all)) if peer is not None else None
     info = {}
 
     def step(x_in, logits_in, ev=None):
@@ -842,14 +850,16 @@ def _run_moe(args, torch, dist, hk, par, ClockSampler, world, rank, local, devic
         else:
             off, tok, pw, inv = hk.permute(ids, w, E)
         if peer is not None:
-            xr, sr, loff, lperm = peer.dispatch(xq, sx, off, tok)
-            n_in = peer.rows_cap
+            xr, sr, loff, lperm, n_in = peer.dispatch_with_shared(xq, sx, off, tok)
         elif world > 1:
             xr, sr, loff, lperm, plan = par.ep_dispatch(xq, sx, off, tok, E)
             n_in = xr.shape[0]
         if ev is not None:
             ev[0].record(stream)
-        if world > 1:
+        if peer is not None:
+            y_all = hk.moe_grouped(xr, sr, loff, lperm, n_in, H, I, *fold, out=y_buf, workspace=ws)
+            shared, y_local = y_all[:T], y_all[T:]
+        elif world > 1:
             y_local = hk.moe_grouped(xr, sr, loff, lperm, n_in, H, I, w13, s13, w2, s2, out=y_buf, workspace=ws)
             shared = hk.moe_grouped(xq, sx, sh_off, sh_tok, T, H, I, sh13, shs13, sh2, shs2, out=y_sh,
                                     workspace=ws_sh)
@@ -865,7 +875,8 @@ def _run_moe(args, torch, dist, hk, par, ClockSampler, world, rank, local, devic
             y = par.ep_return(y_local, plan, lperm)
         else:
             y = y_local
-        return hk.combine(y, pw, inv, shared, T, K), (loff if world > 1 else off)
+        return hk.combine(y, pw, inv, shared, T, K), (peer.local_off if peer is not None else
+                                                      loff if world > 1 else off)
 
     for _ in range(args.warmup):
         _, off = step(x, logits)

@@ -239,11 +239,14 @@ class EpPeer:
 
     The receive buffer comes out expert-major, so the grouped FFN runs over it with the
     identity permutation.  Buffers are sized for `tokens` tokens per rank routed top_k ways.
-    The process group only carries the IPC handles at set-up (`exchange`)."""
+    With `shared_tokens` the receive buffer keeps that many more rows after the peers' part,
+    for this rank's own rows of the shared expert (`dispatch_with_shared`).  The process group
+    only carries the IPC handles at set-up (`exchange`)."""
 
     FLAGS_COUNTS, FLAGS_DISPATCH, FLAGS_RETURN = 0, 1, 2
 
-    def __init__(self, num_experts, tokens, top_k, hidden, group=None, timeout_us=2_000_000, exchange=None):
+    def __init__(self, num_experts, tokens, top_k, hidden, group=None, timeout_us=2_000_000, exchange=None,
+                 shared_tokens=0):
         self.group = group or dist.group.WORLD
         self.world = dist.get_world_size(self.group)
         self.rank = dist.get_rank(self.group)
@@ -251,6 +254,7 @@ class EpPeer:
         self.El = num_experts // self.world
         self.back_cap = tokens * top_k
         self.rows_cap = tokens * top_k * self.world
+        self.shared = shared_tokens
         self.timeout_us = timeout_us
         dev = torch.device("cuda", torch.cuda.current_device())
         ex = exchange or (lambda b: all_gather_bytes(b, self.group))
@@ -259,7 +263,8 @@ class EpPeer:
             return SymBuffer(shape, dtype, self.world, self.rank, ex)
 
         self._bufs = [sym((self.world * num_experts,), torch.int32), sym((3 * 8,), torch.int32),
-                      sym((self.rows_cap, hidden), torch.uint8), sym((self.rows_cap, hidden // 128), torch.float32),
+                      sym((self.rows_cap + shared_tokens, hidden), torch.uint8),
+                      sym((self.rows_cap + shared_tokens, hidden // 128), torch.float32),
                       sym((self.back_cap, hidden), torch.bfloat16)]
         c, f, x, sc, b = self._bufs
         self.counts, self.counts_ptrs = c.tensor, c.ptrs
@@ -274,6 +279,11 @@ class EpPeer:
         self.ret_base = torch.zeros(self.world * self.El, dtype=torch.int32, device=dev)
         self.done = torch.zeros(2, dtype=torch.int32, device=dev)
         self.identity = torch.arange(self.rows_cap, dtype=torch.int32, device=dev)
+        # with the shared expert first: rows [0, T) read the own rows kept after the peers'
+        # part, rows [T, T + received) read the received rows in order
+        p = torch.arange(self.rows_cap + shared_tokens, dtype=torch.int32, device=dev)
+        self.perm_shared = torch.where(p < shared_tokens, p + self.rows_cap, p - shared_tokens)
+        self.zero = torch.zeros(1, dtype=torch.int32, device=dev)
         self.epoch = 0
 
     def close(self):
@@ -301,6 +311,20 @@ class EpPeer:
                   _lib.ptr(self.done[0:1]), self.epoch, s)
         self._wait(self.FLAGS_DISPATCH, stream)
         return self.recv_x, self.recv_s, self.local_off, self.identity
+
+    def dispatch_with_shared(self, xq, sx, offsets, perm_token, stream=None):
+        """dispatch() plus this rank's own `shared_tokens` rows for the shared expert, so one
+        grouped-FFN call runs the shared expert (expert 0 of its weights) and this rank's
+        routed experts (1 .. E/N): returns (x, scales, offsets [E/N + 2], row map, rows).  Rows
+        [0, T) of that call's output are the shared expert's, rows [T, ...) go to give_back."""
+        T = self.shared
+        if T <= 0 or xq.shape[0] != T:
+            raise ValueError("dispatch_with_shared: the peer was built for %d shared rows" % T)
+        xr, sr, loff, _ = self.dispatch(xq, sx, offsets, perm_token, stream)
+        xr[self.rows_cap:].copy_(xq)
+        sr[self.rows_cap:].copy_(sx)
+        off = torch.cat([self.zero, loff + T])
+        return xr, sr, off, self.perm_shared, self.rows_cap + T
 
     def give_back(self, y_local, stream=None):
         """Returns the expert outputs (rows in the receive buffer's order) to their sources;

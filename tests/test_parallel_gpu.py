@@ -61,6 +61,8 @@ def _rank_main(rank, port, what):
             _ep(rank, dev)
         elif what == "ep_peer":
             _ep_peer(rank, dev)
+        elif what == "ep_peer_shared":
+            _ep_peer_shared(rank, dev)
         elif what == "cp_peer":
             _cp_peer(rank, dev)
         else:
@@ -120,6 +122,41 @@ def _ep_peer(rank, dev):
         back = ep.give_back(y_local)
         torch.cuda.synchronize()
         hk.check_errors()
+        assert torch.equal(back[:T * K].view(torch.int16), want.view(torch.int16)), f"rank {rank} step {step}"
+    ep.close()
+
+
+def _ep_peer_shared(rank, dev):
+    """EpPeer with the shared expert in the rank's own grouped-FFN call (dispatch_with_shared:
+    the shared expert is expert 0 of [shared, local experts], its rows read the rank's own rows
+    kept after the peers' part of the receive buffer): the shared rows and every routed row
+    that comes back must equal the one-GPU calls bit for bit, over several steps."""
+    from hyperkernel_b200 import _lib as hk
+    from hyperkernel_b200 import parallel as P
+
+    T, E, H, I, K = 64, 8, 512, 256, 4
+    inp = W.moe_inputs(T * 2, E + 1, H, I, top_k=K, seed=94)  # expert E is the shared one
+    d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    w13, s13, w2, s2 = d(inp["w13"]), d(inp["s13"]), d(inp["w2"]), d(inp["s2"])
+    e0, e1 = P.expert_range(E, 2, rank)
+    fold = [torch.cat([t[E:], t[e0:e1]]) for t in (w13, s13, w2, s2)]
+    every = torch.arange(T, dtype=torch.int32, device=dev)
+    sh_off = torch.tensor([0, T], dtype=torch.int32, device=dev)
+    ep = P.EpPeer(E, T, K, H, shared_tokens=T)
+    for step in range(3):
+        x = torch.from_numpy(inp["x"][rank * T:(rank + 1) * T].view(np.int16)).to(dev).view(torch.bfloat16)
+        logits = d(inp["logits"][rank * T:(rank + 1) * T, :E]) * (1.0 + 0.1 * step)
+        ids, w = hk.route(logits, None, K, 1.0)
+        off, tok, pw, inv = hk.permute(ids, w, E)
+        xq, sx = hk.quant_fp8(x)
+        want = hk.moe_grouped(xq, sx, off, tok, T * K, H, I, w13[:E], s13[:E], w2[:E], s2[:E])[:T * K]
+        want_sh = hk.moe_grouped(xq, sx, sh_off, every, T, H, I, w13[E:], s13[E:], w2[E:], s2[E:])
+        rx, rs, foff, fperm, frows = ep.dispatch_with_shared(xq, sx, off, tok)
+        y_all = hk.moe_grouped(rx, rs, foff, fperm, frows, H, I, *fold)
+        back = ep.give_back(y_all[T:])
+        torch.cuda.synchronize()
+        hk.check_errors()
+        assert torch.equal(y_all[:T].view(torch.int16), want_sh.view(torch.int16)), f"shared, rank {rank} step {step}"
         assert torch.equal(back[:T * K].view(torch.int16), want.view(torch.int16)), f"rank {rank} step {step}"
     ep.close()
 
@@ -223,3 +260,8 @@ def test_context_parallel_on_two_gpus():
 @pytest.mark.skipif(not _two_gpus(), reason="needs two GPUs")
 def test_expert_parallel_over_peer_memory_on_two_gpus():
     mp.spawn(_rank_main, args=(_port(), "ep_peer"), nprocs=2, join=True)
+
+
+@pytest.mark.skipif(not _two_gpus(), reason="needs two GPUs")
+def test_ep_peer_with_the_shared_expert_in_the_same_call_on_two_gpus():
+    mp.spawn(_rank_main, args=(_port(), "ep_peer_shared"), nprocs=2, join=True)
