@@ -1604,6 +1604,7 @@ def _run_sample(args, torch, dist, hk, ClockSampler, world, rank, local, device,
 # The decode step behind the Kernel boundary (HK_MODEL_MLA): one DeepSeek-V3-shaped layer.
 ENGINE_LANES, ENGINE_PAGE_ROWS, ENGINE_CHUNK, ENGINE_BLOCK = 64, 64, 512, 1
 ENGINE_REQUESTS, ENGINE_LIMIT, ENGINE_PROMPT = 128, 64, (64, 1024)
+ENGINE_BUDGET = 8192  # prefill tokens a step: the reference's tuned pacing presets (src/model/cli.rs)
 ENGINE_ENTRIES = (ENGINE_PROMPT[1] + ENGINE_LIMIT + ENGINE_PAGE_ROWS - 1) // ENGINE_PAGE_ROWS + 1
 ENGINE_DIMS = dict(hidden=7168, q_lora=1536, vocab=129280, experts=256, top_k=8, inter=2048, layers=1,
                    logprobs=20, seed=1234, rope_theta=10000.0, route_scale=2.5)
@@ -1631,7 +1632,7 @@ def _engine_session(H, dev, requests, logprobs):
     context = ENGINE_PAGE_ROWS * ENGINE_ENTRIES
     eng = H.Engine(H.engine_config(page_rows=ENGINE_PAGE_ROWS, entries=ENGINE_ENTRIES, window=ENGINE_ENTRIES,
                                    window_keep=0, context=context, width=ENGINE_LANES, chunk=ENGINE_CHUNK,
-                                   block=ENGINE_BLOCK, pad=0, budget=None, every=1, headroom=2048),
+                                   block=ENGINE_BLOCK, pad=0, budget=ENGINE_BUDGET, every=1, headroom=2048),
                    dev.ops(), keep=dev)
     samp = H.Sampling(0.0, 1.0, 0, logprobs, 0)
     reqs = [eng.submit(pr, lim, sampling=samp) for pr, lim in requests]
@@ -1687,7 +1688,8 @@ def leg_engine(args, torch, dist, hk, world, rank, local, device, barrier, hbm_p
     return {
         "workload": f"HK_MODEL_MLA behind hk_push/hk_drain driven by hk_engine_run: {len(requests)} requests, "
                     f"prompts U[{ENGINE_PROMPT[0]},{ENGINE_PROMPT[1]}), {ENGINE_LIMIT} tokens each, {ENGINE_LANES} "
-                    "lanes, 1 DeepSeek-V3-shaped layer (hidden 7168, MLA 128 heads 512+64, FP8 projections, 256+1 "
+                    f"lanes, prefill budget {ENGINE_BUDGET} tokens a step in chunks of {ENGINE_CHUNK}, "
+                    "1 DeepSeek-V3-shaped layer (hidden 7168, MLA 128 heads 512+64, FP8 projections, 256+1 "
                     "experts top-8, inter 2048), vocabulary 129280, greedy with 20 logprob pairs per token",
         "parallelism": f"replicas{world}" if world > 1 else "single GPU",
         "timing": "host clock around hk_engine_run, max over ranks (host-driven loop; commands and ids cross "

@@ -530,7 +530,12 @@ int mla_create(const hk_config& c, const hk_mla_model& d, MlaModel** out, cudaSt
   m->entries = (int32_t)c.entries;
   m->bt_stride = (int32_t)(c.entries + c.window);
   m->pages = (int64_t)c.pages;
-  m->t_cap = std::max<int32_t>(m->width * m->block, m->chunk);
+  // Rows of one forward pass: a decode step's rows, or a group of prompt chunks of distinct
+  // lanes.  Every pass streams all the weights a few hundred rows already hit (the expert FFN
+  // alone is ~11 GB at DeepSeek-V3's shape), so the prompt chunks of one share (an engine with
+  // a prefill token budget sends several: the reference's tuned presets allow 8192 tokens a
+  // step) go through in groups of up to 8192 rows (16 chunks of 512), not a pass a chunk.
+  m->t_cap = std::max<int32_t>({m->width * m->block, m->chunk, std::min<int32_t>(16 * m->chunk, 8192)});
   m->r_cap = m->width * m->block;
   m->n_lp = (int32_t)d.logprobs;
   const int64_t H = d.hidden, QL = d.q_lora, E = d.experts, K = d.top_k, I = d.inter, V = d.vocab;
