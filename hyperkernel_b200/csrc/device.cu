@@ -1021,29 +1021,49 @@ int mla_prompt_group(hk_handle* h, const std::vector<const Cmd*>& group) {
   return HK_OK;
 }
 
+// A batch's commands in order, with prompt chunks gathered into as few forward passes as
+// possible: a pass takes prompt chunks of distinct lanes up to t_cap rows, and the non-prompt
+// commands (pages, seats, starts, ends) met between them go to the apply kernel first when
+// they concern none of the pass's lanes — they only touch their own lanes' block-table rows
+// and state, which the pass does not read — and otherwise after the pass has run.  A lane's
+// second chunk waits for the pass holding its first.  Prompted replies keep push order.
 int apply_batch_mla(hk_handle* h, const std::vector<Cmd>& batch) {
-  size_t i = 0;
-  while (i < batch.size()) {
-    if (batch[i].c.kind != HK_CMD_PROMPT) {  // pages, seats, starts and ends: the apply kernel
-      std::vector<Cmd> run;
-      while (i < batch.size() && batch[i].c.kind != HK_CMD_PROMPT) run.push_back(batch[i++]);
-      HK_TRY(apply_batch(h, run));
+  std::vector<const Cmd*> group;
+  std::vector<uint32_t> lanes;
+  std::vector<Cmd> run;  // non-prompt commands not yet applied
+  size_t rows = 0;
+  auto in_group = [&](uint32_t lane) { return std::find(lanes.begin(), lanes.end(), lane) != lanes.end(); };
+  auto flush = [&]() -> int {
+    if (!group.empty()) HK_TRY(mla_prompt_group(h, group));
+    group.clear();
+    lanes.clear();
+    rows = 0;
+    return HK_OK;
+  };
+  auto apply_run = [&]() -> int {
+    if (run.empty()) return HK_OK;
+    for (const Cmd& c : run)
+      if (in_group(c.c.lane)) {
+        HK_TRY(flush());
+        break;
+      }
+    HK_TRY(apply_batch(h, run));
+    run.clear();
+    return HK_OK;
+  };
+  for (const Cmd& c : batch) {
+    if (c.c.kind != HK_CMD_PROMPT) {
+      run.push_back(c);
       continue;
     }
-    std::vector<const Cmd*> group;
-    std::vector<uint32_t> seen;
-    size_t rows = 0;
-    while (i < batch.size() && batch[i].c.kind == HK_CMD_PROMPT &&
-           std::find(seen.begin(), seen.end(), batch[i].c.lane) == seen.end() &&
-           (group.empty() || rows + batch[i].data.size() <= (size_t)h->mla->t_cap)) {
-      group.push_back(&batch[i]);
-      seen.push_back(batch[i].c.lane);
-      rows += batch[i].data.size();
-      ++i;
-    }
-    HK_TRY(mla_prompt_group(h, group));
+    HK_TRY(apply_run());
+    if (in_group(c.c.lane) || (!group.empty() && rows + c.data.size() > (size_t)h->mla->t_cap)) HK_TRY(flush());
+    group.push_back(&c);
+    lanes.push_back(c.c.lane);
+    rows += c.data.size();
   }
-  return HK_OK;
+  HK_TRY(apply_run());
+  return flush();
 }
 
 int run_step_mla(hk_handle* h) {
