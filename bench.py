@@ -501,21 +501,29 @@ def leg_ep(args, torch, dist, hk, par, world, rank, device, stream, barrier, hbm
     # expert 0 of a weight copy ordered [shared, local experts]
     peer = par.EpPeer(E, T, K, H, shared_tokens=T) if world > 1 else None
     fold = tuple(torch.cat([a[E:], a[e0:e1]]) for a in (w13, s13, w2, s2)) if peer is not None else None
+    # one GPU: the shared expert as expert E of the routed call (rows [T*K, T*K + T))
+    off_ext = torch.empty(E + 2, dtype=torch.int32, device=device)
+    off_ext[E + 1] = rows + T
+    tok_ext = torch.empty(rows + T, dtype=torch.int32, device=device)
+    tok_ext[rows:] = every
 
     def step(ev=None):
         xq, sx = hk.quant_fp8(x)
         ids, w = hk.route(logits, None, K, 1.0)
-        off, tok, pw, inv = hk.permute(ids, w, E)
         if peer is not None:
+            off, tok, pw, inv = hk.permute(ids, w, E)
             xr, sr, foff, fperm, frows = peer.dispatch_with_shared(xq, sx, off, tok)
+        else:
+            off, tok, pw, inv = hk.permute(ids, w, E, offsets=off_ext[:E + 1], perm_token=tok_ext[:rows])
         if ev is not None:
             ev[0].record(stream)
         if peer is not None:
             y_all = hk.moe_grouped(xr, sr, foff, fperm, frows, H, I, *fold, out=y_buf, workspace=ws)
             y_shared, y_loc = y_all[:T], y_all[T:]
         else:
-            y_loc = hk.moe_grouped(xq, sx, off, tok, rows, H, I, *loc, out=y_buf, workspace=ws)
-            y_shared = hk.moe_grouped(xq, sx, sh_off, every, T, H, I, *shr, out=y_sh, workspace=ws_sh)
+            y_all = hk.moe_grouped(xq, sx, off_ext, tok_ext, rows + T, H, I, w13, s13, w2, s2, out=y_buf,
+                                   workspace=ws)
+            y_loc, y_shared = y_all[:rows], y_all[rows:rows + T]
         if ev is not None:
             ev[1].record(stream)
         y = peer.give_back(y_loc) if peer is not None else y_loc

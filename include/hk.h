@@ -235,9 +235,12 @@ int hk_permute(const int32_t* ids, const float* weights, int32_t tokens, int32_t
  * y[p] = h Wd^T (w2[e][hidden][inter]), all weights e4m3 with 128x128 fp32 block scales
  * (s13[e][2*inter/128][hidden/128], s2[e][hidden/128][inter/128]); h is re-quantised to
  * e4m3 1x128 blocks before the down projection.  y[P][hidden] bf16.
- * On sm_100 the expert GEMMs run on the tensor cores (weights on the MMA's M side, up to 64
- * routed rows of an expert on N).  `workspace` (256-byte aligned, hk_moe_workspace_size
- * bytes) holds h, its scales, the tile list and the routed rows gathered in permuted order. */
+ * On sm_100 the expert GEMMs run on the tensor cores (weights on the MMA's M side, a tile of
+ * an expert's routed rows on N: 64-row tiles, or 96-row tiles when the experts hold at least
+ * 56 rows on average and `tokens` > 64; a row's result does not depend on the tile width).  A
+ * shared expert can run in the same call as one more expert whose rows map to every token.
+ * `workspace` (256-byte aligned, hk_moe_workspace_size bytes) holds h, its scales, the tile
+ * lists and the routed rows gathered in permuted order. */
 size_t hk_moe_workspace_size(int64_t rows, int32_t hidden, int32_t inter);
 int hk_moe_grouped(const uint8_t* xq, const float* sx, int32_t tokens, const int32_t* offsets,
                    const int32_t* perm_token, int64_t rows, int32_t num_experts, int32_t hidden,
