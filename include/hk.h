@@ -509,9 +509,12 @@ int hk_open(const hk_config* config, hk_handle** handle);
  * so a loader can overwrite them.
  * Decode steps verify `block` rows per lane: the lane's last token and block - 1 drafts found
  * by prompt lookup (the tokens that followed the latest earlier occurrence of the last token in
- * the lane's last 4096 positions; -1 where there is none).  Prompt chunks are prefilled in one
- * forward pass per batch of distinct lanes and answered with a token sampled from the chunk's
- * last row.  Each sampled token carries `logprobs` (id, logprob) pairs then its own logprob. */
+ * the lane's last 4096 positions; -1 where there is none).  A share's prompt chunks of
+ * distinct lanes are prefilled together, up to max(chunk, min(16 * chunk, 8192)) rows a forward
+ * pass (the share's commands for other lanes are applied before the pass, a command for one of
+ * its lanes after it), and each is answered, in push order, with a token sampled from the
+ * chunk's last row.  Each sampled token carries `logprobs` (id, logprob) pairs then its own
+ * logprob. */
 typedef struct {
     uint32_t hidden;      /* model width, a multiple of 128 */
     uint32_t q_lora;      /* query low-rank width, a multiple of 128 */
@@ -528,7 +531,8 @@ typedef struct {
 
 /* Opens a device kernel running HK_MODEL_MLA (config->model == HK_MODEL_MLA, page_rows == 64,
  * transport HK_TRANSPORT_LAUNCH): allocates the pools as hk_open does, plus the weights, a
- * page-blocked bf16 latent cache of config->pages pages per layer and the step's buffers. */
+ * page-blocked bf16 latent cache of config->pages pages per layer and the step's buffers (sized
+ * for the larger of a decode step's width * block rows and a prefill pass's rows). */
 int hk_open_mla(const hk_config* config, const hk_mla_model* model, hk_handle** handle);
 
 /* Device address and size of one of an HK_MODEL_MLA handle's tensors: `name` is one of "embed"
