@@ -21,7 +21,8 @@ def test_every_header_function_is_exported(hk):
 
 
 def test_every_header_function_has_a_reference_side_binding(hk):
-    """INTEGRATION.md shows the Rust declaration a maintainer adds for each entry point."""
+    """The integration guide at the repository root shows the Rust declaration a maintainer
+    adds for each entry point."""
     text = (Path(__file__).resolve().parents[1] / "INTEGRATION.md").read_text()
     missing = [n for n in hk.header_functions() if f"fn {n}(" not in text]
     assert not missing, f"no Rust binding shown for: {missing}"
