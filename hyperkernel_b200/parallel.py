@@ -321,9 +321,10 @@ class EpPeer:
         if T <= 0 or xq.shape[0] != T:
             raise ValueError("dispatch_with_shared: the peer was built for %d shared rows" % T)
         xr, sr, loff, _ = self.dispatch(xq, sx, offsets, perm_token, stream)
-        xr[self.rows_cap:].copy_(xq)
-        sr[self.rows_cap:].copy_(sx)
-        off = torch.cat([self.zero, loff + T])
+        with torch.cuda.stream(stream if stream is not None else torch.cuda.current_stream()):
+            xr[self.rows_cap:].copy_(xq)
+            sr[self.rows_cap:].copy_(sx)
+            off = torch.cat([self.zero, loff + T])
         return xr, sr, off, self.perm_shared, self.rows_cap + T
 
     def give_back(self, y_local, stream=None):
