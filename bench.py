@@ -578,8 +578,9 @@ def leg_ep(args, torch, dist, hk, par, world, rank, device, stream, barrier, hbm
 
 def leg_cp(args, torch, dist, hk, par, world, rank, device, stream, barrier, hbm_peak):
     """Config 5 (one lane at 1,048,576 cached rows + 7 at U[4K, 64K], 1 + 4 spec-verify rows
-    each, FP8 latent cache), context parallel over the N GPUs: the long lane's KV is cut into
-    page-aligned position ranges, one per rank, the short lanes go round-robin; each rank keeps
+    each, FP8 latent cache), context parallel over the N GPUs: the short lanes go largest first
+    to the least-loaded rank and the long lane's KV is cut into page-aligned position ranges
+    that bring every rank to the same number of KV rows (parallel.cp_plan); each rank keeps
     a bf16 mirror of its pages current and runs one tcgen05 partial launch over its ranges,
     then the long lane's (o, lse) partials are all-gathered over NCCL and merged by LSE (strong
     scaling).  Every rank builds the same pool (one seed); rank 0 then runs the whole batch on
@@ -592,9 +593,10 @@ def leg_cp(args, torch, dist, hk, par, world, rank, device, stream, barrier, hbm
     kv = lay.kv_len.astype(np.int64)
     begin = np.zeros(L, np.int32)
     end = np.zeros(L, np.int32)
-    begin[0], end[0] = par.cp_ranges(int(kv[0]), world)[rank]
+    ranges, owner = par.cp_plan(int(kv[0]), kv[1:], world)  # equal KV rows per rank
+    begin[0], end[0] = ranges[rank]
     for ln in range(1, L):
-        if (ln - 1) % world == rank:
+        if owner[ln - 1] == rank:
             end[ln] = kv[ln]
     g = torch.Generator(device=device)
     g.manual_seed(CP_SEED)
@@ -952,8 +954,9 @@ def _run_moe(args, torch, dist, hk, par, ClockSampler, world, rank, local, devic
 def _run_longctx(args, torch, dist, hk, par, ClockSampler, world, rank, local, device, stream, gen, hbm_peak,
                  peak_src, barrier):
     """Config 5: one lane at 1M cached tokens and 7 at U[4K, 64K], each verifying 1 + 4 rows,
-    FP8 latent cache.  N > 1: the long lane's KV is split into page-aligned position ranges, one
-    per rank (context parallel), the short lanes go round-robin; every rank converts the pages
+    FP8 latent cache.  N > 1: the short lanes go largest first to the least-loaded rank and the
+    long lane's KV is split into page-aligned position ranges that bring every rank to the same
+    number of KV rows (context parallel, parallel.cp_plan); every rank converts the pages
     of its ranges to the blocked bf16 layout and runs one tcgen05 partial attention launch over
     them (--attn-impl 1: the CUDA-core FP8 partial kernel instead), then the long lane's
     partials are all-gathered and merged by LSE (strong scaling: the total work is fixed)."""
@@ -964,10 +967,10 @@ def _run_longctx(args, torch, dist, hk, par, ClockSampler, world, rank, local, d
     kv = lay.kv_len.astype(np.int64)
     begin = np.zeros(L, np.int32)
     end = np.zeros(L, np.int32)
-    b0, e0 = par.cp_ranges(int(kv[0]), world)[rank]
-    begin[0], end[0] = b0, e0
+    ranges, owner = par.cp_plan(int(kv[0]), kv[1:], world)  # equal KV rows per rank
+    begin[0], end[0] = ranges[rank]
     for ln in range(1, L):
-        if (ln - 1) % world == rank:
+        if owner[ln - 1] == rank:
             end[ln] = kv[ln]
     my_rows = int(sum(int(end[i]) - int(begin[i]) for i in range(L)))
     cache = _rand_e4m3(torch, (lay.num_slots, DK), gen, device)

@@ -142,6 +142,42 @@ def cp_ranges(kv_len: int, world: int, page: int = 64) -> list[tuple[int, int]]:
     return out
 
 
+def cp_plan(long_kv: int, short_kv, world: int, page: int = 64):
+    """Context-parallel plan of one long lane and whole short lanes over `world` ranks with
+    equal KV rows per rank: the short lanes go, largest first, to the rank holding the fewest
+    rows so far; the long lane is then cut into page-aligned contiguous ranges, in rank order,
+    that fill every rank up to a common level (a rank whose short lanes already pass it gets
+    none of the long lane).  Returns (ranges [(begin, end)] per rank, owner rank per short
+    lane).  The same inputs give the same plan on every rank."""
+    short_kv = [int(k) for k in short_kv]
+    load = [0] * world
+    owner = [0] * len(short_kv)
+    for i in sorted(range(len(short_kv)), key=lambda i: (-short_kv[i], i)):
+        r = min(range(world), key=lambda r: (load[r], r))
+        owner[i] = r
+        load[r] += short_kv[i]
+    # water level L with sum(max(0, L - load[r])) = long_kv
+    order = sorted(load)
+    level, filled = float(order[0]), 0
+    for n in range(1, world + 1):
+        nxt = order[n] if n < world else float("inf")
+        if filled + n * (nxt - level) >= long_kv:
+            level += (long_kv - filled) / n
+            break
+        filled += n * (nxt - level)
+        level = nxt
+    ranges, at, cum = [], 0, 0.0
+    pages = (long_kv + page - 1) // page
+    for r in range(world):
+        cum += max(0.0, level - load[r])
+        stop = long_kv if r == world - 1 else min(long_kv, int(round(cum / page)) * page)
+        stop = max(stop, at)
+        ranges.append((at, stop))
+        at = stop
+    assert at == long_kv and pages * page >= long_kv
+    return ranges, owner
+
+
 def _default_merge(o_parts, lse_parts):
     return _lib.lse_merge(o_parts, lse_parts)
 

@@ -108,6 +108,30 @@ def _cp_rank(rank, port, ctx, rows, heads):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+def test_cp_plan_balances_kv_rows_across_ranks(world):
+    """The long lane's ranges are contiguous, page-aligned and cover it; every short lane has
+    one owner; no rank holds more than the average plus a page, unless a single short lane is
+    itself above the average (then that rank holds only its short lanes)."""
+    rng = np.random.default_rng(world)
+    for case in range(20):
+        long_kv = int(rng.integers(1, 1 << 21))
+        short = [int(v) for v in rng.integers(1, 1 << 16, int(rng.integers(0, 12)))]
+        ranges, owner = P.cp_plan(long_kv, short, world)
+        assert len(ranges) == world and len(owner) == len(short)
+        assert ranges[0][0] == 0 and ranges[-1][1] == long_kv
+        for (b0, e0), (b1, e1) in zip(ranges, ranges[1:]):
+            assert e0 == b1 and b0 <= e0 and (e0 % 64 == 0 or e0 == long_kv)
+        rows = [e - b for b, e in ranges]
+        for i, r in enumerate(owner):
+            assert 0 <= r < world
+            rows[r] += short[i]
+        avg = (long_kv + sum(short)) / world
+        for r in range(world):
+            if ranges[r][1] > ranges[r][0]:  # a rank with part of the long lane
+                assert rows[r] <= avg + 64 + 1, (case, rows, avg)
+
+
 def test_cp_ranges_are_page_aligned_and_cover_the_lane():
     for kv, world in [(1 << 20, 8), (7005, 2), (100, 4), (64, 8)]:
         r = P.cp_ranges(kv, world)
