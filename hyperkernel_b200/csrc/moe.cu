@@ -19,8 +19,6 @@
 
 namespace {
 
-using hk::kMoeWideRows;
-
 constexpr int kMaxExperts = 512;
 constexpr int kPermThreads = 1024;
 constexpr int kTileRows = 64;
@@ -203,22 +201,18 @@ __global__ void tile_list_kernel(const int32_t* __restrict__ offsets, int32_t E,
   if (lane == 0) *num_tiles = base < max_tiles ? base : max_tiles;
 }
 
-// The tcgen05 kernels' tile lists: one of them gets every tile, the other stays empty (its
-// launch returns at once).  When the experts hold at least kWideMinRows rows on average (and
-// `allow_wide`), the wide list gets tiles of kMoeWideRows (96) rows — an expert with 65-96
-// rows then streams its weights once instead of twice, one with 145 twice instead of three
-// times; otherwise (a decode batch, config 4's 16 rows an expert) the narrow list gets 64-row
-// tiles, as the portable kernels cut them.  The choice reads the actual row total on the
-// device, so a caller that passes a row capacity (expert parallelism) gets the right one.
-// One warp, experts in rounds of 32, a warp scan.
-constexpr int kWideMinRows = 56;
-
-__global__ void tile_lists_kernel(const int32_t* __restrict__ offsets, int32_t E, int64_t rows, bool allow_wide,
-                                  int32_t max_narrow, int32_t* __restrict__ narrow_expert,
-                                  int32_t* __restrict__ narrow_row, int32_t* __restrict__ num_narrow,
-                                  int32_t max_wide, int32_t* __restrict__ wide_expert,
-                                  int32_t* __restrict__ wide_row, int32_t* __restrict__ num_wide,
-                                  unsigned long long* err) {
+// The tcgen05 kernels' tile list: every expert's rows cut into tiles of one width, the widest
+// of those allowed (bit i of `widths` for moe_tile_width(i)) whose threshold the experts' rows
+// per expert on average reach — a decode batch's ~2 rows an expert take 16-row tiles, config
+// 4's ~18 take 32, a prompt pass's ~145 take 96 — so most experts stream their weights once,
+// in the narrowest tile that holds them.  The choice reads the actual row total on the
+// device, so a caller that passes a row capacity (expert parallelism) gets the right width;
+// num[1] tells the launched kernels which of them has the tiles.  One warp, experts in rounds
+// of 32, a warp scan.
+__global__ void tc_list_kernel(const int32_t* __restrict__ offsets, int32_t E, int64_t rows, int32_t widths,
+                               int32_t max_tiles, int32_t* __restrict__ tile_expert,
+                               int32_t* __restrict__ tile_row, int32_t* __restrict__ num,
+                               unsigned long long* err) {
   const int lane = threadIdx.x;
   if (lane >= 32) return;
   bool bad = false;
@@ -227,46 +221,41 @@ __global__ void tile_lists_kernel(const int32_t* __restrict__ offsets, int32_t E
   if (bad) {
     if (lane == 0) {
       hk_flag(err, hk::kErrMoeRow, (unsigned)offsets[E]);
-      *num_narrow = 0;
-      *num_wide = 0;
+      num[0] = 0;
+      num[1] = 0;
     }
     return;
   }
-  const bool wide = allow_wide && (int64_t)offsets[E] >= (int64_t)kWideMinRows * E;
-  int nbase = 0, wbase = 0;
+  int step = hk::moe_tile_width(0);
+#pragma unroll
+  for (int i = 3; i > 0; --i)
+    if ((widths >> i) & 1 && (int64_t)offsets[E] >= (int64_t)hk::moe_tile_min_avg(i) * E) {
+      step = hk::moe_tile_width(i);
+      break;
+    }
+  int base = 0;
   for (int e0 = 0; e0 < E; e0 += 32) {
     const int e = e0 + lane;
     const int lo = e < E ? offsets[e] : 0, hi = e < E ? offsets[e + 1] : 0;
-    const int n = hi - lo, step = wide ? kMoeWideRows : 64, tiles = (n + step - 1) / step;
-    const int nw = wide ? tiles : 0, nn = wide ? 0 : tiles;
-    int iw = nw, in = nn;
+    const int n = (hi - lo + step - 1) / step;
+    int incl = n;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const int vw = __shfl_up_sync(0xffffffffu, iw, o), vn = __shfl_up_sync(0xffffffffu, in, o);
-      if (lane >= o) {
-        iw += vw;
-        in += vn;
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    const int first = base + incl - n;
+    for (int i = 0; i < n; ++i) {
+      if (first + i < max_tiles) {
+        tile_expert[first + i] = e;
+        tile_row[first + i] = lo + step * i;
       }
     }
-    const int wfirst = wbase + iw - nw, nfirst = nbase + in - nn;
-    for (int i = 0; i < nw; ++i) {
-      if (wfirst + i < max_wide) {
-        wide_expert[wfirst + i] = e;
-        wide_row[wfirst + i] = lo + kMoeWideRows * i;
-      }
-    }
-    for (int i = 0; i < nn; ++i) {
-      if (nfirst + i < max_narrow) {
-        narrow_expert[nfirst + i] = e;
-        narrow_row[nfirst + i] = lo + 64 * i;
-      }
-    }
-    wbase += __shfl_sync(0xffffffffu, iw, 31);
-    nbase += __shfl_sync(0xffffffffu, in, 31);
+    base += __shfl_sync(0xffffffffu, incl, 31);
   }
   if (lane == 0) {
-    *num_wide = wbase < max_wide ? wbase : max_wide;
-    *num_narrow = nbase < max_narrow ? nbase : max_narrow;
+    num[0] = base < max_tiles ? base : max_tiles;
+    num[1] = step;
   }
 }
 
@@ -507,14 +496,15 @@ size_t moe_portable_workspace(int64_t rows, int32_t inter) {
          align256((size_t)max_tiles * 2 * sizeof(int32_t) + sizeof(int32_t));
 }
 
-// The tcgen05 path's wide tile list: expert / row pairs and a count.
-size_t wide_list_bytes(int64_t rows) {
-  return align256((size_t)(rows / kMoeWideRows + kMaxExperts + 1) * 2 * sizeof(int32_t) + sizeof(int32_t));
+// The tcgen05 path's tile list: expert / row pairs (room for 16-row tiles), count and width.
+size_t tc_list_bytes(int64_t rows) {
+  return align256((size_t)(rows / hk::moe_tile_width(0) + kMaxExperts + 1) * 2 * sizeof(int32_t) +
+                  2 * sizeof(int32_t));
 }
 
 size_t moe_full_workspace(int64_t rows, int32_t hidden, int32_t inter) {
   return moe_portable_workspace(rows, inter) + align256((size_t)rows * hidden) +
-         align256((size_t)rows * (hidden / 128) * sizeof(float)) + wide_list_bytes(rows);
+         align256((size_t)rows * (hidden / 128) * sizeof(float)) + tc_list_bytes(rows);
 }
 
 // The grouped FFN launcher behind hk_moe_grouped: `err` is the device error word the kernels
@@ -552,21 +542,24 @@ int moe_grouped_run(const uint8_t* xq, const float* sx, int32_t tokens, const in
   ws.xp = base + moe_portable_workspace(rows, inter);
   ws.sxp = reinterpret_cast<float*>(ws.xp + align256((size_t)rows * hidden));
   if (tc) {
-    int32_t* wide_list = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(ws.sxp) +
-                                                    align256((size_t)rows * (hidden / 128) * sizeof(float)));
-    ws.max_wide = (int32_t)(rows / kMoeWideRows + kMaxExperts + 1);
-    ws.wide_expert = wide_list;
-    ws.wide_row = wide_list + ws.max_wide;
-    ws.num_wide = wide_list + 2 * ws.max_wide;
-    // No wide tiles (and no wide launches) where no expert can hold more than 64 rows: a batch
-    // of at most 64 tokens (a decode step; hk_permute gives an expert each token once) or of
-    // fewer rows than the wide threshold over all experts.
-    const bool wide = tokens > 64 && rows >= (int64_t)kWideMinRows * num_experts;
-    tile_lists_kernel<<<1, 32, 0, s>>>(offsets, num_experts, rows, wide, ws.max_tiles, ws.tile_expert, ws.tile_row,
-                                       ws.num_tiles, ws.max_wide, ws.wide_expert, ws.wide_row, ws.num_wide, err);
-    HK_TRY_LAUNCH("tile_lists_kernel");
+    int32_t* list = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(ws.sxp) +
+                                               align256((size_t)rows * (hidden / 128) * sizeof(float)));
+    ws.max_tc = (int32_t)(rows / hk::moe_tile_width(0) + kMaxExperts + 1);
+    ws.tc_expert = list;
+    ws.tc_row = list + ws.max_tc;
+    ws.tc_num = list + 2 * ws.max_tc;
+    // The widths the device may choose: a width whose threshold the call's rows per expert
+    // cannot reach (rows / num_experts bounds the average) is not launched; 96-row tiles also
+    // need more than 64 tokens (hk_permute gives an expert each token once).  A decode batch
+    // launches the 16-row kernel alone.
+    int widths = 1;
+    for (int i = 1; i < 4; ++i)
+      if (rows >= (int64_t)hk::moe_tile_min_avg(i) * num_experts && (i < 3 || tokens > 64)) widths |= 1 << i;
+    tc_list_kernel<<<1, 32, 0, s>>>(offsets, num_experts, rows, widths, ws.max_tc, ws.tc_expert, ws.tc_row,
+                                    ws.tc_num, err);
+    HK_TRY_LAUNCH("tc_list_kernel");
     return moe_sm100_run(xq, sx, tokens, offsets, perm_token, rows, num_experts, hidden, inter, w13, s13, w2,
-                         s2, y, ws, wide, err, s);
+                         s2, y, ws, widths, err, s);
   }
   tile_list_kernel<<<1, 32, 0, s>>>(offsets, num_experts, rows, ws.max_tiles, ws.tile_expert, ws.tile_row,
                                     ws.num_tiles, err);

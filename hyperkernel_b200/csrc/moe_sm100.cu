@@ -6,21 +6,21 @@
 // and the expert's rows the N side (a row tile), and each work unit streams one 128-row block
 // of one expert's weights exactly once per row tile.
 //
-// Two row-tile widths: narrow tiles of at most 64 rows (N 64) and wide tiles of 96 rows (N 96).
-// The device-built tile lists give every tile of a call to one width: wide when the experts
-// hold at least 56 rows on average (expert parallelism on 4-8 GPUs, prompt chunks), so an
-// expert with 65-96 rows streams its weights once instead of twice; narrow otherwise (decode
-// batches, config 4).  Both widths are launched (a decode batch of at most 64 tokens only the
-// narrow one) and the one whose list is empty returns at once.  The wide form keeps four 44 KB
-// stages instead of five 40 KB ones and two TMEM accumulator buffers instead of four; its
-// promotion threads hold 48 token columns each (gate and up: 96 fp32 sums, what the 168
-// registers of a 320-thread CTA's threads hold beside the rest).
+// Four row-tile widths (N 16, 32, 64, 96), one per call: the device-built tile list cuts every
+// expert's rows in the widest width whose threshold the experts' average rows reach (below 8
+// rows: 16; 8-23: 32; 24-55: 64; 56 and up: 96), so most experts stream their weights once and
+// the tile is no wider than they need.  A narrower tile leaves room for more weights in flight:
+// six 34 or 36 KB stages (16 and 32 rows), five 40 KB stages (64), four 44 KB stages (96).
+// The host launches every width the call's rows per expert can reach; a launched width that the
+// list did not choose returns at once (a decode batch launches only the 16-row kernel).  The
+// 96-row form's promotion threads hold 48 token columns each (gate and up: 96 fp32 sums, what
+// the 168 registers of a 320-thread CTA's threads hold beside the rest).
 //
 //  gather   xp[p] = xq[perm_token[p]], sxp[p] = sx[perm_token[p]]: the routed rows laid out
 //           contiguously in permuted order, so TMA can load a row tile (out-of-range
 //           indices are recorded and give a zero row).
 //  up       unit = (row tile, 128-column block nb of h): D_g = Wg[nb] . X^T and
-//           D_u = Wu[nb] . X^T per 128-wide K block (tcgen05 kind::f8f6f4, M 128, N 64 or 96)
+//           D_u = Wu[nb] . X^T per 128-wide K block (tcgen05 kind::f8f6f4, M 128, N = tile width)
 //           into multi-buffered TMEM; promotion warps add partial * sw * sx[row] in registers;
 //           at the end h = silu(g) * u is requantised to e4m3 with one scale per (row, nb)
 //           (amax over the block's 128 columns across the four warps).
@@ -43,16 +43,15 @@
 namespace {
 
 using namespace hk::sm100;
-using hk::kMoeWideRows;
 
 constexpr int kWRows = 128;     // weight rows per unit: the MMA's M
 constexpr int kBK = 128;
 constexpr int kThreads = 320;       // TMA, MMA, 8 promotion warps
 constexpr int kWBytes = kWRows * kBK;      // 16 KB
 constexpr unsigned long long kDrainNs = 1000000000ull;
-// TMEM accumulator buffers of the narrow form: the MMA runs this many K blocks ahead of the
-// promotion warps, which covers their per-unit work (scale table at the start, requantisation
-// or stores at the end).
+// TMEM accumulator buffers of the forms up to 64 rows: the MMA runs this many K blocks ahead of
+// the promotion warps, which covers their per-unit work (scale table at the start,
+// requantisation or stores at the end).
 #ifndef HK_MOE_TBUFS
 #define HK_MOE_TBUFS 4
 #endif
@@ -68,17 +67,17 @@ constexpr int kTmemSlot = 192;
 constexpr int kAbort = 196;
 constexpr int kRed = 256;        // [4][kRows] floats: per-warp column amax (up epilogue)
 
-// kRows: token rows per unit, the MMA's N (64: narrow tiles, kMoeWideRows: wide tiles).
+// kRows: token rows per unit, the MMA's N (16, 32, 64 or 96).
 template <bool kUp, int kRows>
 struct Cfg {
-  static_assert(kRows == 64 || kRows == kMoeWideRows, "row tile");
-  static constexpr int kXBytes = kRows * kBK;                // 8 or 12 KB
+  static_assert(kRows == 16 || kRows == 32 || kRows == 64 || kRows == 96, "row tile");
+  static constexpr int kXBytes = kRows * kBK;                // 2 to 12 KB
   static constexpr int kStageBytes = 2 * kWBytes + kXBytes;  // two weight blocks, one row tile
   static constexpr int kMaxKb = kUp ? 64 : 32;  // scale-table capacity in K blocks
-  static constexpr int kStages = kRows == 64 ? 5 : 4;
-  static constexpr int kTBufs = kRows == 64 ? HK_MOE_TBUFS : 2;  // 2 * kRows columns each
+  static constexpr int kStages = kRows <= 32 ? 6 : kRows == 64 ? 5 : 4;
+  static constexpr int kTBufs = kRows <= 64 ? HK_MOE_TBUFS : 2;  // 2 * kRows columns each
   static constexpr int kCols = kRows / 2;       // token columns per promotion warp
-  static constexpr int kChunk = kRows == 64 ? 32 : 16;  // columns per TMEM load
+  static constexpr int kChunk = kRows == 64 ? 32 : kRows == 16 ? 8 : 16;  // columns per TMEM load
   static constexpr int kOffScales = kStages * kStageBytes;
   static constexpr int kOffCtl = kOffScales + kMaxKb * kRows * 4;
   static constexpr int kCtlBytes = kRed + 4 * kRows * 4;
@@ -138,7 +137,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     moe_sm100_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap, Params p) {
   using C = Cfg<kUp, kRows>;
   constexpr int kTBufs = C::kTBufs, kCols = C::kCols, kChunk = C::kChunk;
-  if (*p.num_tiles == 0) return;  // an empty list: leave before any set-up
+  // not the width the tile list chose (or no tiles): leave before any set-up
+  if (p.num_tiles[0] == 0 || p.num_tiles[1] != kRows) return;
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t* ctl = smem + C::kOffCtl;
   float* scales = reinterpret_cast<float*>(smem + C::kOffScales);  // [kb][64]
@@ -172,7 +172,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // up: one unit per 128-column block of h (its gate and up row blocks); down: one unit per
   // pair of 128-row blocks of W2 (256 output columns; the second is empty past hidden).
   const int nblocks = kUp ? p.inter / 128 : (p.hidden / 128 + 1) / 2;
-  const int units = *p.num_tiles * nblocks;
+  const int units = p.num_tiles[0] * nblocks;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -293,6 +293,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           // both blocks' columns of this chunk, one wait
           if constexpr (kChunk == 32) {
             tmem_ld32x2(base + c * kChunk, base + kRows + c * kChunk, vg, vu);
+          } else if constexpr (kChunk == 8) {
+            tmem_ld8x2(base + c * kChunk, base + kRows + c * kChunk, vg, vu);
           } else {
             tmem_ld16x2(base + c * kChunk, base + kRows + c * kChunk, vg, vu);
           }
@@ -387,23 +389,24 @@ bool moe_sm100_supported(int32_t num_experts, int32_t hidden, int32_t inter) {
 int moe_sm100_run(const uint8_t* xq, const float* sx, int32_t tokens, const int32_t* offsets,
                   const int32_t* perm_token, int64_t rows, int32_t num_experts, int32_t hidden, int32_t inter,
                   const uint8_t* w13, const float* s13, const uint8_t* w2, const float* s2, uint16_t* y,
-                  const MoeScratch& ws, bool wide, unsigned long long* err, cudaStream_t s) {
+                  const MoeScratch& ws, int widths, unsigned long long* err, cudaStream_t s) {
   HK_REQUIRE(moe_sm100_supported(num_experts, hidden, inter), "moe_sm100: hidden %d inter %d", hidden, inter);
   HK_REQUIRE(rows < (1ll << 31), "moe_sm100: %lld rows", (long long)rows);
   gather_rows_kernel<<<(unsigned)rows, 128, 0, s>>>(xq, sx, perm_token, rows, tokens, hidden, ws.xp, ws.sxp, err);
   HK_TRY_LAUNCH("gather_rows_kernel");
-  CUtensorMap w13map, xmap, xmap_w, w2map, hmap, hmap_w;
+  CUtensorMap w13map, w2map, xmap[4], hmap[4];
   HK_TRY(sm100::make_map_u8(&w13map, w13, (uint64_t)num_experts * 2 * inter, (uint64_t)hidden, kWRows));
-  HK_TRY(sm100::make_map_u8(&xmap, ws.xp, (uint64_t)rows, (uint64_t)hidden, 64));
-  HK_TRY(sm100::make_map_u8(&xmap_w, ws.xp, (uint64_t)rows, (uint64_t)hidden, kMoeWideRows));
   HK_TRY(sm100::make_map_u8(&w2map, w2, (uint64_t)num_experts * hidden, (uint64_t)inter, kWRows));
-  HK_TRY(sm100::make_map_u8(&hmap, ws.hq, (uint64_t)rows, (uint64_t)inter, 64));
-  HK_TRY(sm100::make_map_u8(&hmap_w, ws.hq, (uint64_t)rows, (uint64_t)inter, kMoeWideRows));
+  for (int i = 0; i < 4; ++i) {
+    if (!((widths >> i) & 1)) continue;
+    HK_TRY(sm100::make_map_u8(&xmap[i], ws.xp, (uint64_t)rows, (uint64_t)hidden, moe_tile_width(i)));
+    HK_TRY(sm100::make_map_u8(&hmap[i], ws.hq, (uint64_t)rows, (uint64_t)inter, moe_tile_width(i)));
+  }
   Params p{};
   p.offsets = offsets;
-  p.tile_expert = ws.tile_expert;
-  p.tile_row = ws.tile_row;
-  p.num_tiles = ws.num_tiles;
+  p.tile_expert = ws.tc_expert;
+  p.tile_row = ws.tc_row;
+  p.num_tiles = ws.tc_num;
   p.hidden = hidden;
   p.inter = inter;
   p.num_experts = num_experts;
@@ -414,17 +417,17 @@ int moe_sm100_run(const uint8_t* xq, const float* sx, int32_t tokens, const int3
   p.w_scale = s13;
   p.hq = ws.hq;
   p.hs = ws.hs;
-  Params pw = p;  // the wide tiles' list
-  pw.tile_expert = ws.wide_expert;
-  pw.tile_row = ws.wide_row;
-  pw.num_tiles = ws.num_wide;
-  HK_TRY((launch<true, 64>(w13map, xmap, p, grid, s)));
-  if (wide) HK_TRY((launch<true, kMoeWideRows>(w13map, xmap_w, pw, grid, s)));
-  p.act_scale = pw.act_scale = ws.hs;
-  p.w_scale = pw.w_scale = s2;
-  p.y = pw.y = y;
-  HK_TRY((launch<false, 64>(w2map, hmap, p, grid, s)));
-  if (wide) HK_TRY((launch<false, kMoeWideRows>(w2map, hmap_w, pw, grid, s)));
+  if (widths & 1) HK_TRY((launch<true, 16>(w13map, xmap[0], p, grid, s)));
+  if (widths & 2) HK_TRY((launch<true, 32>(w13map, xmap[1], p, grid, s)));
+  if (widths & 4) HK_TRY((launch<true, 64>(w13map, xmap[2], p, grid, s)));
+  if (widths & 8) HK_TRY((launch<true, 96>(w13map, xmap[3], p, grid, s)));
+  p.act_scale = ws.hs;
+  p.w_scale = s2;
+  p.y = y;
+  if (widths & 1) HK_TRY((launch<false, 16>(w2map, hmap[0], p, grid, s)));
+  if (widths & 2) HK_TRY((launch<false, 32>(w2map, hmap[1], p, grid, s)));
+  if (widths & 4) HK_TRY((launch<false, 64>(w2map, hmap[2], p, grid, s)));
+  if (widths & 8) HK_TRY((launch<false, 96>(w2map, hmap[3], p, grid, s)));
   return HK_OK;
 }
 

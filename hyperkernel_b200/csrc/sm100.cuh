@@ -219,6 +219,24 @@ __device__ __forceinline__ void tmem_ld16x2(uint32_t addr0, uint32_t addr1, floa
   }
 }
 
+// Two 8-column loads (addr0, addr1) and one wait: v0 and v1 get 8 columns each.
+__device__ __forceinline__ void tmem_ld8x2(uint32_t addr0, uint32_t addr1, float* v0, float* v1) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%16];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%8,%9,%10,%11,%12,%13,%14,%15}, [%17];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(addr0), "r"(addr1)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    v0[i] = __uint_as_float(r[i]);
+    v1[i] = __uint_as_float(r[8 + i]);
+  }
+}
+
 // UMMA shared-memory descriptor: start >> 4, leading / stride byte offsets >> 4, version 1,
 // 128-byte swizzle.  For K-major tiles of 128-byte rows: LBO 16, SBO 1024 (one 8-row atom).
 __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t addr, uint32_t lbo, uint32_t sbo) {

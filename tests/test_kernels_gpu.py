@@ -484,13 +484,15 @@ def test_moe_layer_matches_oracle(hk, orc, cuda, T, E, H, I, K):
     assert rel_err(to_np_bf16(out), want) <= TOL
 
 
-@pytest.mark.parametrize("empty", [0, 20])
-def test_moe_grouped_narrow_and_wide_row_tiles_match_oracle(hk, orc, cuda, empty):
+@pytest.mark.parametrize("empty", [0, 20, 50, 160])
+def test_moe_grouped_row_tiles_of_every_width_match_oracle(hk, orc, cuda, empty):
     """Experts whose row counts sit on the tile edges of the tensor-core path: none, 1, 64,
-    65, 96, 97, 160, 161, 192 and 300 rows.  Averaging 134 rows an expert, every tile is a
-    96-row wide tile (65-96 rows: one tile; 97-192: two; 300: four); with 20 more experts
-    without rows (45 on average) every tile is a 64-row narrow tile.  Rows come from a random
-    token map, so tiles mix tokens as a real permutation does."""
+    65, 96, 97, 160, 161, 192 and 300 rows.  The tile width follows the rows per expert on
+    average: 134 (no empty experts) gives 96-row tiles (65-96 rows: one tile; 97-192: two;
+    300: four), 45 (20 more experts without rows) 64-row tiles, 22 (50 more) 32-row tiles and
+    7.9 (160 more) 16-row tiles, so every width meets experts of one row, of exactly a tile,
+    of a tile and one row, and of many tiles.  Rows come from a random token map, so tiles mix
+    tokens as a real permutation does."""
     counts = [0, 1, 64, 65, 96, 97, 160, 161, 192, 300] + [0] * empty
     E, H, I, T = len(counts), 256, 256, 400
     inp = _moe_case(T, E, H, I, 2, seed=58)
@@ -507,21 +509,23 @@ def test_moe_grouped_narrow_and_wide_row_tiles_match_oracle(hk, orc, cuda, empty
 
 
 def test_moe_grouped_row_result_does_not_depend_on_the_tile_width(hk, cuda):
-    """The same 96 rows through one expert (96 rows on average: one wide tile) and through two
-    copies of that expert with 48 rows each (48 on average: two narrow tiles) give the same
-    bits: each output is one weight row's dot product with one token row in the same K-block
-    order either way (expert parallelism relies on this: a rank's experts receive more rows
-    than the same experts on one GPU and may take the other tile width)."""
+    """The same 96 rows through one expert (96 rows on average: a 96-row tile) and through 2,
+    6 and 16 copies of that expert holding 48, 16 and 6 rows each (64-, 32- and 16-row tiles)
+    give the same bits: each output is one weight row's dot product with one token row in the
+    same K-block order whatever the tile (expert parallelism relies on this: a rank's experts
+    receive more rows than the same experts on one GPU and may take another width)."""
     E, H, I, T = 1, 512, 256, 96
     inp = _moe_case(T, E, H, I, 2, seed=60)
     gxq, gsx = hk.quant_fp8(bf16_dev(inp["x"], cuda))
     tok = dev(np.random.default_rng(61).permutation(T).astype(np.int32), cuda)
     w = [dev(inp[k], cuda) for k in ("w13", "s13", "w2", "s2")]
     one = hk.moe_grouped(gxq, gsx, dev(np.array([0, T], np.int32), cuda), tok, T, H, I, *w)
-    two_w = [torch.cat([t, t]) for t in w]
-    two = hk.moe_grouped(gxq, gsx, dev(np.array([0, 48, T], np.int32), cuda), tok, T, H, I, *two_w)
-    hk.check_errors()
-    assert torch.equal(one.view(torch.int16), two.view(torch.int16))
+    for copies in (2, 6, 16):
+        cw = [torch.cat([t] * copies) for t in w]
+        off = dev(np.arange(0, T + 1, T // copies, dtype=np.int32), cuda)
+        got = hk.moe_grouped(gxq, gsx, off, tok, T, H, I, *cw)
+        hk.check_errors()
+        assert torch.equal(one.view(torch.int16), got.view(torch.int16)), f"{copies} experts"
 
 
 def test_moe_layer_full_size_matches_oracle_on_sampled_tokens(hk, orc, cuda):
