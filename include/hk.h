@@ -236,9 +236,10 @@ int hk_permute(const int32_t* ids, const float* weights, int32_t tokens, int32_t
  * (s13[e][2*inter/128][hidden/128], s2[e][hidden/128][inter/128]); h is re-quantised to
  * e4m3 1x128 blocks before the down projection.  y[P][hidden] bf16.
  * On sm_100 the expert GEMMs run on the tensor cores (weights on the MMA's M side, a tile of
- * an expert's routed rows on N: 64-row tiles, or 96-row tiles when the experts hold at least
- * 56 rows on average and `tokens` > 64; a row's result does not depend on the tile width).  A
- * shared expert can run in the same call as one more expert whose rows map to every token.
+ * an expert's routed rows on N: 16, 32, 64 or 96 rows, picked from the rows per expert on
+ * average — below 8, 8-23, 24-55, 56 and up, the last only with `tokens` > 64; a row's result
+ * does not depend on the tile width).  A shared expert can run in the same call as one more
+ * expert whose rows map to every token.
  * `workspace` (256-byte aligned, hk_moe_workspace_size bytes) holds h, its scales, the tile
  * lists and the routed rows gathered in permuted order. */
 size_t hk_moe_workspace_size(int64_t rows, int32_t hidden, int32_t inter);
